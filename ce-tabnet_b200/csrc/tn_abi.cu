@@ -1,0 +1,190 @@
+// tn_abi.cu -- single-op C entry points: quantised matrices, attention, the
+// activation hop codec and the sampler, for parity tests and microbenchmarks.
+#include <vector>
+
+#include "tn_kernels.cuh"
+
+namespace tn {
+
+struct DevSwitch {
+  int prev = -1;
+  cudaError_t err = cudaSuccess;
+  explicit DevSwitch(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev) err = cudaSetDevice(dev);
+  }
+  ~DevSwitch() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+__global__ void k_rows_from_slots(const int32_t* __restrict__ slot, const int32_t* __restrict__ len, int n,
+                                  int n_slots, int max_ctx, RowInfo* __restrict__ rows) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= n) return;
+  int s = slot[r], l = len[r];
+  if (s < 0 || s >= n_slots || l < 1) {
+    s = 0;
+    l = 0;
+  }
+  rows[r] = RowInfo{s, 0, 0, l > max_ctx ? max_ctx : l};
+}
+
+}  // namespace tn
+
+using namespace tn;
+
+struct tn_matrix {
+  Matrix m;
+  int device = 0;
+};
+
+extern "C" int tn_matrix_create(int32_t device, int32_t quant, int32_t rows, int32_t cols, const void* packed,
+                                uint64_t len, int32_t on_device, tn_matrix** out) {
+  clear_error();
+  TN_REQUIRE(out && packed && rows > 0 && cols > 0, TN_EINVAL, "tn_matrix_create: bad argument");
+  *out = nullptr;
+  const uint64_t need = quant_bytes((uint64_t)rows * cols, quant);
+  TN_REQUIRE(need != 0, TN_EUNSUPPORTED, "unsupported quant %d", quant);
+  TN_REQUIRE(len >= need, TN_EINVAL, "tn_matrix_create: %llu bytes given, %llu needed",
+             (unsigned long long)len, (unsigned long long)need);
+  TN_REQUIRE(cols <= 32768, TN_EUNSUPPORTED, "tn_matrix_create: more than 32768 columns");
+  DevSwitch g(device);
+  TN_REQUIRE(g.err == cudaSuccess, TN_ECUDA, "cudaSetDevice(%d): %s", device, cudaGetErrorString(g.err));
+  tn_matrix* M = new (std::nothrow) tn_matrix();
+  TN_REQUIRE(M, TN_ENOMEM, "out of host memory");
+  M->device = device;
+  int rc = matrix_alloc(&M->m, quant, rows, cols);
+  uint8_t* staging = nullptr;
+  const uint8_t* src = (const uint8_t*)packed;
+  if (!rc && !on_device) {
+    if (cudaMalloc(&staging, need) != cudaSuccess ||
+        cudaMemcpy(staging, packed, need, cudaMemcpyHostToDevice) != cudaSuccess) {
+      set_error("tn_matrix_create: staging upload failed");
+      rc = TN_ECUDA;
+    }
+    src = staging;
+  }
+  if (!rc) rc = matrix_repack(&M->m, src, quant, rows, 0, 1, 0);
+  if (!rc && cudaStreamSynchronize(0) != cudaSuccess) {
+    set_error("tn_matrix_create: repack failed");
+    rc = TN_ECUDA;
+  }
+  if (staging) cudaFree(staging);
+  if (rc) {
+    matrix_free(&M->m);
+    delete M;
+    return rc;
+  }
+  *out = M;
+  return TN_OK;
+}
+
+extern "C" int tn_matrix_matvec(const tn_matrix* m, int32_t n_tokens, const float* d_x, float* d_y,
+                                void* stream) {
+  clear_error();
+  TN_REQUIRE(m && d_x && d_y && n_tokens >= 0, TN_EINVAL, "tn_matrix_matvec: bad argument");
+  DevSwitch g(m->device);
+  return matvec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, (cudaStream_t)stream);
+}
+
+extern "C" int tn_matrix_dequant(const tn_matrix* m, float* d_out, void* stream) {
+  clear_error();
+  TN_REQUIRE(m && d_out, TN_EINVAL, "tn_matrix_dequant: bad argument");
+  DevSwitch g(m->device);
+  return matrix_dequant(m->m, d_out, (cudaStream_t)stream);
+}
+
+extern "C" uint64_t tn_matrix_device_bytes(const tn_matrix* m) { return m ? m->m.bytes : 0; }
+
+extern "C" void tn_matrix_free(tn_matrix* m) {
+  if (!m) return;
+  DevSwitch g(m->device);
+  matrix_free(&m->m);
+  delete m;
+}
+
+static size_t attn_total_scratch(int n_rows, int n_heads, int n_kv_heads, int head_dim, int max_ctx) {
+  return ((size_t)n_rows * sizeof(RowInfo) + 255 & ~(size_t)255) +
+         attn_scratch_bytes(n_rows, n_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx));
+}
+
+extern "C" uint64_t tn_attention_scratch_bytes(int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,
+                                               int32_t head_dim, int32_t max_ctx) {
+  if (n_rows <= 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || max_ctx <= 0) return 0;
+  return attn_total_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx);
+}
+
+extern "C" int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
+                            int32_t head_dim, int32_t max_ctx, const float* d_q, const float* d_k,
+                            const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
+                            void* d_scratch, uint64_t scratch_bytes, void* stream) {
+  clear_error();
+  TN_REQUIRE(n_rows >= 0 && n_slots > 0 && n_heads > 0 && n_kv_heads > 0 && max_ctx > 0, TN_EINVAL,
+             "tn_attention: bad sizes");
+  TN_REQUIRE(d_q && d_k && d_v && d_slot && d_len && d_out && d_scratch, TN_EINVAL,
+             "tn_attention: null pointer");
+  TN_REQUIRE((reinterpret_cast<uintptr_t>(d_scratch) & 255) == 0, TN_EINVAL,
+             "tn_attention: scratch must be 256-byte aligned");
+  TN_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128, TN_EUNSUPPORTED,
+             "tn_attention: head_dim %d unsupported", head_dim);
+  if (n_rows == 0) return TN_OK;
+  const size_t need = attn_total_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx);
+  TN_REQUIRE(scratch_bytes >= need, TN_EINVAL, "tn_attention: scratch of %llu bytes, %zu needed",
+             (unsigned long long)scratch_bytes, need);
+  cudaStream_t s = (cudaStream_t)stream;
+  RowInfo* rows = (RowInfo*)d_scratch;
+  void* part = (char*)d_scratch + (((size_t)n_rows * sizeof(RowInfo) + 255) & ~(size_t)255);
+  k_rows_from_slots<<<(n_rows + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows);
+  TN_CHECK_LAUNCH();
+  const size_t kvh_stride = (size_t)max_ctx * head_dim;
+  return attention(d_q, n_heads * head_dim, d_k, d_v, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows,
+                   n_heads, n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out,
+                   n_heads * head_dim, part, s);
+}
+
+extern "C" int tn_hop_encode(const float* d_in, uint16_t* d_out, uint64_t n, void* stream) {
+  clear_error();
+  TN_REQUIRE(n == 0 || (d_in && d_out), TN_EINVAL, "tn_hop_encode: null pointer");
+  return hop_encode_flat(d_in, n, d_out, (cudaStream_t)stream);
+}
+
+extern "C" int tn_hop_decode(const uint16_t* d_in, float* d_out, uint64_t n, void* stream) {
+  clear_error();
+  TN_REQUIRE(n == 0 || (d_in && d_out), TN_EINVAL, "tn_hop_decode: null pointer");
+  return hop_decode(d_in, n, d_out, (cudaStream_t)stream);
+}
+
+extern "C" uint16_t tn_hop_encode_host(float v) { return hop_encode(v); }
+
+extern "C" double tn_sample_uniform(uint64_t rng_seed, uint64_t row) { return sample_uniform(rng_seed, row); }
+
+extern "C" int tn_sample(float* d_logits, int32_t n_rows, int32_t vocab, double temperature, double top_p,
+                         uint64_t rng_seed, int32_t* d_out, void* stream) {
+  clear_error();
+  TN_REQUIRE(d_logits && d_out && n_rows >= 0 && vocab > 0, TN_EINVAL, "tn_sample: bad argument");
+  if (n_rows == 0) return TN_OK;
+  std::vector<double> p(3 * (size_t)n_rows);
+  for (int r = 0; r < n_rows; r++) {
+    p[3 * r] = temperature;
+    p[3 * r + 1] = top_p;
+    p[3 * r + 2] = sample_uniform(rng_seed, (uint64_t)r);
+  }
+  double* dp = nullptr;
+  TN_CHECK_CUDA(cudaMalloc(&dp, p.size() * sizeof(double)));
+  cudaStream_t s = (cudaStream_t)stream;
+  int rc = TN_OK;
+  if (cudaMemcpyAsync(dp, p.data(), p.size() * sizeof(double), cudaMemcpyHostToDevice, s) != cudaSuccess) {
+    set_error("tn_sample: parameter upload failed");
+    rc = TN_ECUDA;
+  }
+  // the sampler overwrites logits with probabilities when temperature > 0
+  if (!rc) rc = sample_rows(d_logits, n_rows, vocab, dp, d_out, s);
+  if (cudaStreamSynchronize(s) != cudaSuccess && !rc) {
+    set_error("tn_sample: %s", cudaGetErrorString(cudaGetLastError()));
+    rc = TN_ECUDA;
+  }
+  cudaFree(dp);
+  return rc;
+}

@@ -1,0 +1,230 @@
+/*
+ * tabnet_stage.h -- C ABI of the B200 stage engine (libtabnet_stage.so).
+ *
+ * The engine replaces the stage engine of ce-tabnet, web/inference-worker.js,
+ * behind the same three-call contract (web/inference-worker.js:13-19,
+ * web/inference.js:9-15):
+ *
+ *   initStage(spec) -> ctx        tn_stage_init
+ *   forward(ctx, req) -> out      tn_stage_forward / tn_stage_forward_batch
+ *   freeStage(ctx)                tn_stage_free
+ *
+ * Plain C types only (no torch, no C++), so a Node-API addon, ctypes, cgo or
+ * JNI binding can call it directly.  All calls return 0 or a negative TN_E*
+ * status and never abort; tn_last_error() gives the calling thread's message.
+ * Calls on one tn_stage are serialised by an internal mutex; stages on
+ * different devices may run concurrently from different threads.
+ */
+#ifndef TABNET_STAGE_H
+#define TABNET_STAGE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define TN_ABI_VERSION 1
+
+/* ---- status codes ---- */
+#define TN_OK 0
+#define TN_EINVAL (-1)       /* bad argument (sizes, ids, null pointers) */
+#define TN_ENOMEM (-2)       /* host or device allocation failed */
+#define TN_ECUDA (-3)        /* a CUDA runtime call failed */
+#define TN_EUNSUPPORTED (-4) /* "unsupported quant" (web/inference-worker.js:126,136) */
+#define TN_ECAPACITY (-5)    /* max_ctx / max_seqs / max_tokens_per_step exceeded */
+#define TN_ESTATE (-6)       /* wrong stage role for the call (e.g. ids to a non-first stage) */
+#define TN_ETIMEOUT (-7)     /* a bounded device wait ran out */
+
+/* ---- weight formats (web/inference-worker.js:92-137) ---- */
+typedef enum {
+  TN_QUANT_F32 = 0,
+  TN_QUANT_F16 = 1,
+  TN_QUANT_Q4_0 = 2, /* 18-byte blocks: f16 d, 16 bytes; byte j = elem 2j (lo), 2j+1 (hi); w=(nib-8)*d */
+  TN_QUANT_Q8_0 = 3  /* 34-byte blocks: f16 d, 32 x int8; w = q*d */
+} tn_quant;
+
+/* what a non-last stage returns (the reference returns the last position only) */
+enum { TN_HOP_LAST = 0, TN_HOP_ALL = 1 };
+
+/* spec flags */
+#define TN_FLAG_NO_GRAPHS (1u << 0) /* never capture decode steps in CUDA graphs */
+
+/* One layer's packed buffer, tensors in web/inference-worker.js:142-159 order:
+ * attn_norm(f16) wq wk wv wo ffn_norm(f16) w_gate w_up w_down. */
+typedef struct {
+  int32_t idx;      /* absolute layer index */
+  int32_t quant;    /* tn_quant of the matrices */
+  const void* buf;  /* packed bytes (host, or device if weights_on_device) */
+  uint64_t len;
+} tn_layer_weights;
+
+/* initStage({arch, dims, layers:[lo,hi), is_first, is_last, weights, opts}) */
+typedef struct {
+  uint32_t abi_version; /* TN_ABI_VERSION */
+  /* dims (web/inference-worker.js:426-429) */
+  int32_t hidden_dim, n_heads, n_kv_heads, vocab;
+  int32_t ffn_dim;      /* 0 -> roundFfn(hidden_dim) (web/inference-worker.js:160-163) */
+  double rope_theta;
+  /* stage slice */
+  int32_t layer_lo, layer_hi, is_first, is_last;
+  /* weights (web/shard-loader.js:16-22 `weights` object) */
+  const tn_layer_weights* layers;
+  int32_t n_layers;     /* == layer_hi - layer_lo */
+  const void* embed;   uint64_t embed_len;   int32_t embed_quant;   /* first stage */
+  const void* norm;    uint64_t norm_len;                          /* last stage, f16 [H] */
+  const void* lm_head; uint64_t lm_head_len; int32_t lm_head_quant; /* last stage */
+  int32_t weights_on_device; /* 1: every weight pointer above is device memory of `device` */
+  /* runtime options (web/inference-worker.js:642 opts.max_ctx) */
+  int32_t device;
+  int32_t max_ctx;             /* KV rows per sequence; 0 -> 4096 */
+  int32_t max_seqs;            /* concurrent sequences with KV; 0 -> 16 */
+  int32_t max_tokens_per_step; /* rows fused into one step; 0 -> 512 (longer prompts are chunked) */
+  uint32_t flags;
+} tn_stage_spec;
+
+typedef struct tn_stage tn_stage;
+
+/* forward(ctx, {seq_id, token_pos, hidden?, token_ids?, temperature?, top_p?}) */
+typedef struct {
+  uint64_t seq_id;            /* the JS string seq_id mapped to an integer by the binding */
+  int32_t token_pos;          /* RoPE position of the first token in this request */
+  int32_t n_tokens;           /* positions in this request (>= 1) */
+  const int32_t* token_ids;   /* first stage: [n_tokens] */
+  const uint16_t* hidden;     /* other stages: [n_tokens * hidden_dim] fp16 bits */
+  double temperature;         /* last stage; <= 0 is greedy (web/inference-worker.js:660) */
+  double top_p;               /* last stage */
+  uint64_t rng_seed;          /* last stage, temperature > 0: seeds the uniform draw */
+  int32_t hop_mode;           /* TN_HOP_LAST (reference behaviour) or TN_HOP_ALL */
+} tn_fwd_req;
+
+typedef struct {
+  uint16_t* hidden;           /* caller-owned, capacity hidden_cap_tokens * hidden_dim */
+  int32_t hidden_cap_tokens;
+  int32_t n_hidden_tokens;    /* written: positions returned (1 for TN_HOP_LAST) */
+  int32_t token_id;           /* written on the last stage */
+} tn_fwd_out;
+
+/* web/inference-worker.js:417 initStage.  Copies and repacks every weight;
+ * the caller may free its buffers when this returns. */
+int tn_stage_init(const tn_stage_spec* spec, tn_stage** out);
+
+/* web/inference-worker.js:471 forward (and :690 forwardSafe for the last
+ * stage).  Host buffers in, host buffers out; synchronous. */
+int tn_stage_forward(tn_stage* st, const tn_fwd_req* req, tn_fwd_out* out);
+
+/* Several sequences fused into one step (micro-batching; the reference runs
+ * them as independent forward calls).  reqs[i] and outs[i] as above. */
+int tn_stage_forward_batch(tn_stage* st, const tn_fwd_req* reqs, int32_t n_reqs, tn_fwd_out* outs);
+
+/* Release one sequence's KV slot (no reference counterpart: the reference
+ * keeps every sequence's KV until freeStage, web/inference-worker.js:677-684). */
+int tn_stage_free_seq(tn_stage* st, uint64_t seq_id);
+
+/* KV rows currently cached for seq_id (0 if unknown). */
+int32_t tn_stage_kv_len(tn_stage* st, uint64_t seq_id);
+
+/* web/inference-worker.js:677 freeStage. */
+void tn_stage_free(tn_stage* st);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* tn_last_error(void);
+
+/* ---- device-resident decode step (pipeline runner, benchmarks) ----
+ * One token per sequence; inputs and outputs are device pointers on the
+ * stage's device.  Enqueued on `stream` (NULL: the stage's own stream) and
+ * returns without waiting; KV bookkeeping is advanced at enqueue time. */
+typedef struct {
+  int32_t n_seqs;
+  const uint64_t* seq_ids;     /* host [n_seqs] */
+  const int32_t* token_pos;    /* host [n_seqs] */
+  const int32_t* d_token_ids;  /* first stage: device [n_seqs] */
+  const uint16_t* d_hidden_in; /* other stages: device [n_seqs * H] fp16 bits */
+  uint16_t* d_hidden_out;      /* non-last stage: device [n_seqs * H] */
+  int32_t* d_token_out;        /* last stage: device [n_seqs] */
+  double temperature, top_p;
+  uint64_t rng_seed;
+} tn_step_desc;
+int tn_stage_step_async(tn_stage* st, const tn_step_desc* step, void* stream);
+/* the stage's own stream (cudaStream_t) */
+void* tn_stage_stream(tn_stage* st);
+
+typedef struct {
+  uint64_t weight_bytes;   /* device bytes held by repacked weights */
+  uint64_t kv_bytes;       /* device bytes of the KV arena */
+  uint64_t scratch_bytes;  /* device bytes of activations and partials */
+  uint64_t packed_bytes;   /* packed (reference-format) bytes the weights came from */
+  int32_t n_layers, head_dim, q_dim, kv_dim, ffn_dim;
+  int32_t graphs_captured; /* decode-step CUDA graphs instantiated so far */
+} tn_stage_info;
+int tn_stage_get_info(tn_stage* st, tn_stage_info* info);
+
+/* ---- single-op entry points (tests, microbenchmarks) ---- */
+
+/* A quantised [rows x cols] matrix, repacked on the device from packed bytes
+ * laid out as by dequantToF32 (web/inference-worker.js:102-129). */
+typedef struct tn_matrix tn_matrix;
+int tn_matrix_create(int32_t device, int32_t quant, int32_t rows, int32_t cols, const void* packed,
+                     uint64_t len, int32_t on_device, tn_matrix** out);
+/* y[t][r] = sum_c W[r][c] * x[t][c] for t < n_tokens (web/inference-worker.js:523-527);
+ * device pointers, f32. */
+int tn_matrix_matvec(const tn_matrix* m, int32_t n_tokens, const float* d_x, float* d_y, void* stream);
+/* the dequantised matrix, [rows][cols] f32 (bit-exact check of repack + decode) */
+int tn_matrix_dequant(const tn_matrix* m, float* d_out, void* stream);
+uint64_t tn_matrix_device_bytes(const tn_matrix* m);
+void tn_matrix_free(tn_matrix* m);
+
+/* GQA attention for query rows over an f32 KV cache laid out
+ * [n_slots][n_kv_heads][max_ctx][head_dim] (K and V separately).  Row r uses
+ * slot d_slot[r] and cached positions [0, d_len[r]); a row whose slot is
+ * outside [0, n_slots) or whose length is < 1 yields zeros, lengths above
+ * max_ctx are clamped.  Math of
+ * web/inference-worker.js:556-564; d_q, d_out: [n_rows][n_heads*head_dim].
+ * d_scratch (device, tn_attention_scratch_bytes() bytes, 256-byte aligned)
+ * holds the row table and the split-K partials. */
+uint64_t tn_attention_scratch_bytes(int32_t n_rows, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                    int32_t max_ctx);
+int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                 int32_t max_ctx, const float* d_q, const float* d_k, const float* d_v,
+                 const int32_t* d_slot, const int32_t* d_len, float* d_out, void* d_scratch,
+                 uint64_t scratch_bytes, void* stream);
+
+/* Activation hop codec, bit-exact with f32ToF16 / f16ToF32
+ * (web/inference-worker.js:68-88): round half up, subnormal mantissa masked. */
+int tn_hop_encode(const float* d_in, uint16_t* d_out, uint64_t n, void* stream);
+int tn_hop_decode(const uint16_t* d_in, float* d_out, uint64_t n, void* stream);
+uint16_t tn_hop_encode_host(float v);
+
+/* Sampling of web/inference-worker.js:658-672 over [n_rows][vocab] logits.
+ * temperature <= 0: greedy (lowest index among maxima).  Otherwise softmax
+ * at `temperature`, nucleus `top_p`, and the uniform tn_sample_uniform(seed, row)
+ * in place of Math.random(). */
+int tn_sample(float* d_logits, int32_t n_rows, int32_t vocab, double temperature, double top_p,
+              uint64_t rng_seed, int32_t* d_out, void* stream); /* temperature > 0 overwrites d_logits */
+double tn_sample_uniform(uint64_t rng_seed, uint64_t row);
+
+/* ---- synthetic model packs (seeded weights in the reference byte layout) ----
+ * Deterministic across host and device: the same seed gives the same bytes. */
+typedef struct {
+  int32_t hidden_dim, n_heads, n_kv_heads, vocab, ffn_dim;
+} tn_dims;
+enum { TN_TAG_EMBED = 1, TN_TAG_NORM = 2, TN_TAG_LM_HEAD = 3 };
+/* bytes of one packed layer (web/inference-worker.js:142-178) */
+uint64_t tn_layer_bytes(const tn_dims* dims, int32_t quant);
+/* quantBytesFor (web/inference-worker.js:130-137); 0 for an unknown quant */
+uint64_t tn_quant_bytes(uint64_t count, int32_t quant);
+/* one packed layer; `out` is host memory, or device memory when on_device */
+int tn_synth_layer(uint64_t seed, int32_t layer_idx, const tn_dims* dims, int32_t quant, void* out,
+                   int32_t on_device, void* stream);
+/* a whole-model tensor: tag TN_TAG_EMBED / TN_TAG_LM_HEAD ([vocab x H] in
+ * `quant`) or TN_TAG_NORM ([H] f16) */
+int tn_synth_tensor(uint64_t seed, int32_t tag, const tn_dims* dims, int32_t quant, void* out,
+                    int32_t on_device, void* stream);
+
+int tn_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TABNET_STAGE_H */

@@ -1,0 +1,243 @@
+"""Stage-engine parity on the GPU through the C ABI (initStage / forward /
+freeStage), against the oracle on identical seeded weights and prompts.
+
+Greedy tokens must be identical; hidden states (fp16 hop frames, decoded)
+within max|a-b| / max|b| <= 1e-3.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+HIDDEN_TOL = 1e-3
+
+
+def f16(bits):
+    return np.asarray(bits, dtype=np.uint16).view(np.float16).astype(np.float32)
+
+
+def maxrel(a, b):
+    return float(np.max(np.abs(a - b)) / max(float(np.max(np.abs(b))), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def tiny(pkg):
+    m = pkg.pack.MODELS["tiny"]
+    return m, pkg.pack.synth_weights(m, 0, m.n_layers, True, True)
+
+
+def _stage(pkg, m, w, lo, hi, first, last, **opts):
+    sub = {k: v for k, v in w.items() if k != "layers"}
+    sub["layers"] = [l for l in w["layers"] if lo <= l["idx"] < hi]
+    o = {"max_ctx": 256, "max_seqs": 8, "device": 0}
+    o.update(opts)
+    return pkg.initStage({"arch": "llama", "dims": m.dims(), "layers": [lo, hi], "is_first": first,
+                          "is_last": last, "weights": sub, "opts": o}), sub
+
+
+def test_tiny_single_stage_greedy_64(pkg, ref, tiny):
+    m, w = tiny
+    ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    oracle = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
+    prompt = pkg.pack.synth_prompt(m, 32)
+    got = pkg.forward(ctx, {"seq_id": "a", "token_pos": 0, "token_ids": prompt, "temperature": 0})["token_id"]
+    want = oracle.forward(1, 0, token_ids=prompt)
+    assert got == want["token_id"]
+    toks = [got]
+    for s in range(64):
+        pos = 32 + s
+        got = pkg.forward(ctx, {"seq_id": "a", "token_pos": pos, "token_ids": [toks[-1]], "temperature": 0})
+        want = oracle.forward(1, pos, token_ids=[toks[-1]])
+        lg = np.sort(want["logits"])[::-1]
+        assert got["token_id"] == want["token_id"], (s, "top-2 gap", lg[0] - lg[1])
+        toks.append(got["token_id"])
+    assert pkg.kv_len(ctx, "a") == 32 + 64 == oracle.kv_len(1)
+    pkg.freeStage(ctx)
+
+
+def test_tiny_two_stages_reference_hops(pkg, ref, tiny):
+    """The reference runtime's hop semantics: prefill hops only the last
+    position (web/tabnet-node.js:167-169), so stage 1's KV starts at one row."""
+    m, w = tiny
+    a, wa = _stage(pkg, m, w, 0, 2, True, False)
+    b, wb = _stage(pkg, m, w, 2, 4, False, True)
+    oa = ref.RefStage(m.dims(), 0, 2, True, False, wa)
+    ob = ref.RefStage(m.dims(), 2, 4, False, True, wb)
+    prompt = pkg.pack.synth_prompt(m, 24, seed=3)
+    ha = pkg.forward(a, {"seq_id": "s", "token_pos": 0, "token_ids": prompt})["hidden"]
+    ra = oa.forward(7, 0, token_ids=prompt)
+    assert maxrel(f16(ha), f16(ra["hidden"])) <= HIDDEN_TOL
+    pos = len(prompt) - 1
+    tok = pkg.forward(b, {"seq_id": "s", "token_pos": pos, "hidden": ha, "temperature": 0})["token_id"]
+    assert tok == ob.forward(7, pos, hidden=ha)["token_id"]
+    for step in range(16):
+        pos = len(prompt) + step
+        ha = pkg.forward(a, {"seq_id": "s", "token_pos": pos, "token_ids": [tok]})["hidden"]
+        ra = oa.forward(7, pos, token_ids=[tok])
+        assert maxrel(f16(ha), f16(ra["hidden"])) <= HIDDEN_TOL, step
+        tok2 = pkg.forward(b, {"seq_id": "s", "token_pos": pos, "hidden": ha, "temperature": 0})["token_id"]
+        assert tok2 == ob.forward(7, pos, hidden=ha)["token_id"], step
+        tok = tok2
+    pkg.freeStage(a)
+    pkg.freeStage(b)
+
+
+def test_tiny_two_stages_hop_all(pkg, ref, tiny):
+    """hop_mode all: every prompt position crosses the stage boundary, so the
+    pipeline computes what one stage over all layers computes."""
+    m, w = tiny
+    a, wa = _stage(pkg, m, w, 0, 2, True, False, hop_mode="all")
+    b, wb = _stage(pkg, m, w, 2, 4, False, True)
+    oa = ref.RefStage(m.dims(), 0, 2, True, False, wa)
+    ob = ref.RefStage(m.dims(), 2, 4, False, True, wb)
+    prompt = pkg.pack.synth_prompt(m, 20, seed=4)
+    hs = pkg.forward(a, {"seq_id": 9, "token_pos": 0, "token_ids": prompt})["hidden"]
+    assert hs.shape == (20, m.hidden_dim)
+    want = np.stack([oa.forward(9, p, token_ids=[prompt[p]])["hidden"] for p in range(20)])
+    for p in range(20):
+        assert maxrel(f16(hs[p]), f16(want[p])) <= HIDDEN_TOL, p
+    tok = pkg.forward(b, {"seq_id": 9, "token_pos": 0, "hidden": hs, "temperature": 0})["token_id"]
+    assert tok == ob.forward(9, 0, hidden=hs)["token_id"]
+    assert pkg.kv_len(b, 9) == 20
+    pkg.freeStage(a)
+    pkg.freeStage(b)
+
+
+def test_batch_equals_individual(pkg, ref, tiny):
+    m, w = tiny
+    one, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    many, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    prompts = [pkg.pack.synth_prompt(m, 5 + 3 * i, seed=10 + i) for i in range(4)]
+    solo = [pkg.forward(one, {"seq_id": i, "token_pos": 0, "token_ids": p, "temperature": 0})["token_id"]
+            for i, p in enumerate(prompts)]
+    batch = pkg.forward_batch(many, [{"seq_id": i, "token_pos": 0, "token_ids": p, "temperature": 0}
+                                     for i, p in enumerate(prompts)])
+    assert [r["token_id"] for r in batch] == solo
+    toks = list(solo)
+    for step in range(12):
+        reqs = [{"seq_id": i, "token_pos": len(prompts[i]) + step, "token_ids": [toks[i]], "temperature": 0}
+                for i in range(4)]
+        b = [r["token_id"] for r in pkg.forward_batch(many, reqs)]
+        s = [pkg.forward(one, r)["token_id"] for r in reqs]
+        assert b == s, step
+        toks = b
+    assert many.info()["graphs_captured"] >= 1
+    pkg.freeStage(one)
+    pkg.freeStage(many)
+
+
+def test_chunked_prefill_matches(pkg, ref, tiny):
+    """A prompt longer than max_tokens_per_step runs in several steps."""
+    m, w = tiny
+    ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, max_tokens_per_step=16)
+    oracle = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
+    prompt = pkg.pack.synth_prompt(m, 45, seed=6)
+    got = pkg.forward(ctx, {"seq_id": "c", "token_pos": 0, "token_ids": prompt, "temperature": 0})["token_id"]
+    assert got == oracle.forward(1, 0, token_ids=prompt)["token_id"]
+    pkg.freeStage(ctx)
+
+
+def test_temperature_sampling_matches_oracle_draw(pkg, ref, tiny):
+    m, w = tiny
+    ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    oracle = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
+    lib = pkg._lib.load()
+    prompt = pkg.pack.synth_prompt(m, 12, seed=8)
+    seed = 4242
+    got = pkg.forward(ctx, {"seq_id": "t", "token_pos": 0, "token_ids": prompt, "temperature": 0.8,
+                            "top_p": 0.9, "rng_seed": seed})["token_id"]
+    u = lib.tn_sample_uniform(seed, len(prompt) - 1)
+    want = oracle.forward(1, 0, token_ids=prompt, temperature=0.8, top_p=0.9, u=u)["token_id"]
+    assert got == want
+    pkg.freeStage(ctx)
+
+
+def test_device_step_matches_forward(pkg, ref, tiny, torch_cuda):
+    torch = torch_cuda
+    m, w = tiny
+    lib = pkg._lib.load()
+    import ctypes as C
+
+    a, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    b, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    prompts = [pkg.pack.synth_prompt(m, 6, seed=20 + i) for i in range(3)]
+    toks = [pkg.forward(a, {"seq_id": i, "token_pos": 0, "token_ids": p, "temperature": 0})["token_id"]
+            for i, p in enumerate(prompts)]
+    for i, p in enumerate(prompts):
+        pkg.forward(b, {"seq_id": i, "token_pos": 0, "token_ids": p, "temperature": 0})
+    ids = (C.c_uint64 * 3)(*[b.seq_key(i) for i in range(3)])
+    cur = list(toks)
+    for step in range(8):
+        pos = (C.c_int32 * 3)(*[6 + step] * 3)
+        din = torch.tensor(cur, dtype=torch.int32, device="cuda")
+        dout = torch.zeros(3, dtype=torch.int32, device="cuda")
+        d = pkg._lib.StepDesc(n_seqs=3, seq_ids=ids, token_pos=pos, d_token_ids=din.data_ptr(),
+                              d_token_out=dout.data_ptr(), temperature=0.0, top_p=0.95, rng_seed=0)
+        pkg._lib.check(lib.tn_stage_step_async(b.handle, C.byref(d), None))
+        torch.cuda.synchronize()
+        want = [pkg.forward(a, {"seq_id": i, "token_pos": 6 + step, "token_ids": [cur[i]], "temperature": 0})
+                ["token_id"] for i in range(3)]
+        got = dout.cpu().tolist()
+        assert got == want, step
+        cur = got
+    pkg.freeStage(a)
+    pkg.freeStage(b)
+
+
+def test_errors(pkg, tiny):
+    m, w = tiny
+    ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, max_ctx=16, max_seqs=2)
+    E = pkg._lib.TnError
+    with pytest.raises(E) as e:
+        pkg.forward(ctx, {"seq_id": 1, "token_pos": 0, "token_ids": [m.vocab]})
+    assert e.value.code == pkg._lib.TN_EINVAL
+    with pytest.raises(E) as e:
+        pkg.forward(ctx, {"seq_id": 1, "token_pos": 0, "token_ids": list(range(17))})
+    assert e.value.code == pkg._lib.TN_ECAPACITY
+    assert pkg.kv_len(ctx, 1) == 0  # a failed call leaves no KV behind
+    pkg.forward(ctx, {"seq_id": 1, "token_pos": 0, "token_ids": [1], "temperature": 0})
+    pkg.forward(ctx, {"seq_id": 2, "token_pos": 0, "token_ids": [1], "temperature": 0})
+    with pytest.raises(E) as e:
+        pkg.forward(ctx, {"seq_id": 3, "token_pos": 0, "token_ids": [1], "temperature": 0})
+    assert e.value.code == pkg._lib.TN_ECAPACITY
+    pkg.free_seq(ctx, 2)
+    pkg.forward(ctx, {"seq_id": 3, "token_pos": 0, "token_ids": [1], "temperature": 0})
+    with pytest.raises(E) as e:
+        pkg.forward(ctx, {"seq_id": 1, "token_pos": 1, "hidden": np.zeros(m.hidden_dim, np.uint16)})
+    assert e.value.code == pkg._lib.TN_ESTATE
+    pkg.freeStage(ctx)
+    bad = dict(w)
+    bad["layers"] = [dict(l, quant="q5_1") for l in w["layers"]]
+    with pytest.raises(E) as e:
+        _stage(pkg, m, bad, 0, m.n_layers, True, True)
+    assert "unsupported quant q5_1" in str(e.value)
+
+
+@pytest.mark.parametrize("name,lo,hi,first,last", [("llama8b", 0, 2, True, False), ("llama70b", 40, 41, False, False)])
+def test_large_shape_slices(pkg, ref, name, lo, hi, first, last):
+    """Layer slices of the 8B and 70B shapes: stage output hidden states
+    against the oracle over a short prefill."""
+    m = pkg.pack.MODELS[name]
+    w = {"arch": "llama", "dims": m.dims(), "quant": m.quant,
+         "layers": [{"idx": i, "buf": pkg.pack.synth_layer(m, i), "quant": m.quant} for i in range(lo, hi)]}
+    if first:
+        w["embed"] = pkg.pack.synth_tensor(m, "embed")
+        w["embedQuant"] = m.embed_quant
+    ctx = pkg.initStage({"arch": "llama", "dims": m.dims(), "layers": [lo, hi], "is_first": first,
+                         "is_last": last, "weights": w,
+                         "opts": {"max_ctx": 64, "max_seqs": 2, "device": 0, "hop_mode": "all"}})
+    oracle = ref.RefStage(m.dims(), lo, hi, first, last, w)
+    n = 6
+    if first:
+        prompt = pkg.pack.synth_prompt(m, n, seed=9)
+        got = pkg.forward(ctx, {"seq_id": 0, "token_pos": 0, "token_ids": prompt})["hidden"]
+        want = [oracle.forward(1, p, token_ids=[prompt[p]])["hidden"] for p in range(n)]
+    else:
+        rng = np.random.default_rng(11)
+        hid = rng.standard_normal((n, m.hidden_dim)).astype(np.float16).view(np.uint16)
+        got = pkg.forward(ctx, {"seq_id": 0, "token_pos": 0, "hidden": hid})["hidden"]
+        want = [oracle.forward(1, p, hidden=hid[p])["hidden"] for p in range(n)]
+    for p in range(n):
+        assert maxrel(f16(got[p]), f16(want[p])) <= HIDDEN_TOL, p
+    pkg.freeStage(ctx)
+    oracle.free()
