@@ -1,0 +1,540 @@
+#!/usr/bin/env python
+"""Decode throughput of the B200 stage engine: Llama-3-70B-shaped q4_0 model,
+8 one-sequence micro-batches in flight, 1024-token prompts.
+
+Each GPU holds one contiguous layer stage (the planner's ranges; one stage of
+all 80 layers at N=1).  A stage runs one micro-batch per tick, and a bench
+step is one round in which every micro-batch advances by one token (at N=1:
+the 8 micro-batches back to back on one GPU; at N>1: a pipeline whose
+activations hop over NCCL send/recv).  `value` is tokens per second of the
+whole job with inputs resident in HBM; `e2e` drives the same rounds through
+the host-buffer API (tn_stage_forward), host<->device copies included.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  (N>1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s (70B-shape q4_0, 8 one-sequence micro-batches in flight)"
+SCALING = "strong"  # total work (8 micro-batches x steps) is fixed as N grows
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=8, help="timed rounds (every micro-batch +1 token)")
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--model", default="llama70b")
+    p.add_argument("--microbatches", type=int, default=8)
+    p.add_argument("--prompt", type=int, default=1024)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args(argv)
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def workload_config(args, world: int) -> dict:
+    return {"workload": f"{args.model} q4_0 decode: {args.microbatches} micro-batches x 1 sequence in flight, "
+                        f"{args.prompt}-token prompts, one micro-batch per stage step",
+            "model": args.model, "microbatches": args.microbatches, "seqs_per_microbatch": 1,
+            "prompt_len": args.prompt, "stages": world, "parallelism": f"pp{world}",
+            "l2": "weights (39 GB at N=1) exceed the 126 MB L2 every step; no flush needed",
+            "sampling": "greedy (temperature 0)"}
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=self.file,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) >= 9 and f[1].replace(".", "").isdigit():
+                rows.append(f)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def physical_gpu(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v for v in vis.split(",") if v.strip()]
+        if local_rank < len(ids) and ids[local_rank].strip().isdigit():
+            return int(ids[local_rank])
+    return local_rank
+
+
+def measured_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ oracle CPU timing
+def oracle_token_time(pkg, m, n_threads: int, layer_reps: int) -> dict:
+    """The reference CPU path (oracle) on one decode token: `layer_reps`
+    single-layer steps and one final-norm + lm_head step, extrapolated to the
+    whole model: s/token = n_layers * t_layer + t_head."""
+    from oracle import ref
+
+    layer = pkg.pack.synth_layer(m, 0)
+    w = {"layers": [{"idx": 0, "buf": layer, "quant": m.quant}], "quant": m.quant}
+    mid = ref.RefStage(m.dims(), 0, 1, False, False, w, n_threads)
+    rng = np.random.default_rng(0)
+    hid = (rng.standard_normal(m.hidden_dim) * 0.5).astype(np.float16).view(np.uint16)
+    times = []
+    for r in range(layer_reps):
+        t0 = time.perf_counter()
+        mid.forward(1, r, hidden=hid)
+        times.append(time.perf_counter() - t0)
+    mid.free()
+    del layer
+    head = pkg.pack.synth_tensor(m, "lm_head")
+    x = rng.standard_normal(m.hidden_dim).astype(np.float32)
+    t0 = time.perf_counter()
+    ref.matvec(head, m.lm_head_quant, m.vocab, m.hidden_dim, x)
+    t_head = time.perf_counter() - t0
+    t_layer = statistics.mean(times)
+    s_tok = m.n_layers * t_layer + t_head
+    return {"tok_s": 1.0 / s_tok, "t_layer_s": t_layer, "t_head_s": t_head, "layer_times": times,
+            "sample": f"{layer_reps} single-token steps through one {m.name} layer + one lm_head matvec, "
+                      f"extrapolated to {m.n_layers} layers"}
+
+
+def run_reference(args):
+    """The reference CPU implementation of the path (the oracle's C
+    restatement of web/inference-worker.js), all host threads."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    import __graft_entry__ as g
+
+    pkg = g.load_package()
+    m = pkg.pack.MODELS[args.model]
+    n_threads = os.cpu_count() or 1
+    os.environ["TABNET_ORACLE_THREADS"] = str(n_threads)
+    warm = oracle_token_time(pkg, m, n_threads, max(1, args.warmup))
+    res = oracle_token_time(pkg, m, n_threads, max(1, args.steps))
+    # one reference "step" = one round: every micro-batch's sequence +1 token,
+    # run one after another as the reference engine does
+    s_round = args.microbatches / res["tok_s"]
+    value = res["tok_s"]
+    line = {"metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": s_round * 1e3, "higher_is_better": True, "scaling": SCALING,
+            "vs_baseline": None, "dtype": "f64 accumulate, f32 storage (q4_0 weights)", "data": "synthetic",
+            "impl": "reference", "config": workload_config(args, world),
+            "cpu_baseline": {"value": value, "unit": "tok/s", "cores": n_threads, "kind": "port",
+                             "sample": res["sample"]},
+            "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "detail": {"t_layer_s": res["t_layer_s"], "t_head_s": res["t_head_s"], "warm_tok_s": warm["tok_s"]}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------------ our engine
+def device_weights(pkg, torch, m, lo, hi, first, last):
+    """Seeded packed weights written straight into device memory."""
+    pack = pkg.pack
+    bufs = {"layers": []}
+    for i in range(lo, hi):
+        t = torch.empty(pack.tensor_bytes(m, i), dtype=torch.uint8, device="cuda")
+        pack.synth_device(m, i, t.data_ptr())
+        bufs["layers"].append({"idx": i, "buf": t, "quant": m.quant})
+    if first:
+        bufs["embed"] = torch.empty(pack.tensor_bytes(m, "embed"), dtype=torch.uint8, device="cuda")
+        pack.synth_device(m, "embed", bufs["embed"].data_ptr())
+        bufs["embedQuant"] = m.embed_quant
+    if last:
+        for k in ("norm", "lm_head"):
+            bufs[k] = torch.empty(pack.tensor_bytes(m, k), dtype=torch.uint8, device="cuda")
+            pack.synth_device(m, k, bufs[k].data_ptr())
+        bufs["lmHeadQuant"] = m.lm_head_quant
+    bufs["on_device"] = True
+    bufs["quant"] = m.quant
+    torch.cuda.synchronize()
+    return bufs
+
+
+class Pipeline:
+    """One stage per rank; tick schedule with all P2P ops of a tick batched.
+
+    Rank r runs step j = tau - r at tick tau (micro-batch j % M).  At the start
+    of tick tau it receives the input of step j and sends the output of step
+    j - 1 (so every send meets its receive in the same tick on the peer); the
+    last rank's token of step j reaches rank 0 at tick j + W and feeds step
+    j + M (M >= W)."""
+
+    def __init__(self, pkg, torch, ctx, rank, world, M, H):
+        self.pkg, self.torch, self.ctx = pkg, torch, ctx
+        self.rank, self.world, self.M, self.H = rank, world, M, H
+        self.lib = pkg._lib.load()
+        self.stream_ptr = self.lib.tn_stage_stream(ctx.handle)
+        self.stream = torch.cuda.ExternalStream(self.stream_ptr)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        self.tok = torch.zeros((M, 1), dtype=torch.int32, device=dev)          # rank 0 inputs / last outputs
+        self.hin = torch.zeros((M, H), dtype=torch.int16, device=dev)          # hidden inputs
+        self.hout = torch.zeros((M, H), dtype=torch.int16, device=dev)         # hidden outputs
+        self.tok_out = torch.zeros((M, 1), dtype=torch.int32, device=dev)
+        self.seq_ids = [(C.c_uint64 * 1)(ctx.seq_key(mb)) for mb in range(M)]
+        self.pos = [0] * M
+
+    def _step(self, mb):
+        lib, P = self.lib, self.pkg._lib
+        pos = (C.c_int32 * 1)(self.pos[mb])
+        d = P.StepDesc(n_seqs=1, seq_ids=self.seq_ids[mb], token_pos=pos, temperature=0.0, top_p=0.95, rng_seed=0)
+        if self.ctx.is_first:
+            d.d_token_ids = self.tok[mb].data_ptr()
+        else:
+            d.d_hidden_in = self.hin[mb].data_ptr()
+        if self.ctx.is_last:
+            d.d_token_out = (self.tok if self.world == 1 else self.tok_out)[mb].data_ptr()
+        else:
+            d.d_hidden_out = self.hout[mb].data_ptr()
+        P.check(lib.tn_stage_step_async(self.ctx.handle, C.byref(d), self.stream_ptr))
+        self.pos[mb] += 1
+
+    def rounds(self, n_rounds: int):
+        """n_rounds x M steps per rank, including pipeline fill and drain."""
+        torch, W, M, r = self.torch, self.world, self.M, self.rank
+        n = n_rounds * M
+        with torch.cuda.stream(self.stream):
+            if W == 1:
+                for j in range(n):
+                    self._step(j % M)
+                return
+            import torch.distributed as dist
+
+            for tau in range(n + W):
+                j = tau - r
+                ops = []
+                if r == 0:
+                    jt = tau - W  # token of step jt arrives now, for step jt + M
+                    if 0 <= jt < n and jt + M < n:
+                        ops.append(dist.P2POp(dist.irecv, self.tok[jt % M], W - 1))
+                elif 0 <= j < n:
+                    ops.append(dist.P2POp(dist.irecv, self.hin[j % M], r - 1))
+                if 1 <= j <= n:  # output of step j - 1
+                    if r < W - 1:
+                        ops.append(dist.P2POp(dist.isend, self.hout[(j - 1) % M], r + 1))
+                    elif j - 1 + M < n:
+                        ops.append(dist.P2POp(dist.isend, self.tok_out[(j - 1) % M], 0))
+                if ops:
+                    for w in dist.batch_isend_irecv(ops):
+                        w.wait()
+                if 0 <= j < n:
+                    self._step(j % M)
+
+
+def prefill(pkg, torch, ctx, rank, world, prompts, H):
+    """Untimed prompt prefill through the host API; every prompt position hops
+    to the next stage (hop_mode all) so each stage's KV covers the prompt."""
+    M, L = len(prompts), len(prompts[0])
+    reqs = []
+    if rank == 0:
+        reqs = [{"seq_id": mb, "token_pos": 0, "token_ids": prompts[mb], "temperature": 0, "hop_mode": "all"}
+                for mb in range(M)]
+    else:
+        import torch.distributed as dist
+
+        buf = torch.empty((M, L, H), dtype=torch.int16, device="cuda")
+        dist.recv(buf, rank - 1)
+        hid = buf.cpu().numpy().view(np.uint16)
+        reqs = [{"seq_id": mb, "token_pos": 0, "hidden": hid[mb], "temperature": 0, "hop_mode": "all"}
+                for mb in range(M)]
+    out = pkg.forward_batch(ctx, reqs)
+    if ctx.is_last:
+        first_tok = [o["token_id"] for o in out]
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.send(torch.tensor(first_tok, dtype=torch.int32, device="cuda"), 0)
+        return first_tok
+    import torch.distributed as dist
+
+    hs = np.stack([o["hidden"] for o in out]).astype(np.uint16)
+    dist.send(torch.from_numpy(hs.view(np.int16)).cuda(), rank + 1)
+    if rank == 0:
+        t = torch.empty(M, dtype=torch.int32, device="cuda")
+        dist.recv(t, world - 1)
+        return t.cpu().tolist()
+    return None
+
+
+def matvec_bytes(pkg, m, cls: str, T: int = 1) -> int:
+    """Algorithmic bytes of one matvec launch: packed weights + f32 x + f32 y
+    (read and written again for the residual epilogues)."""
+    from_pack = pkg.pack
+    H, F, V = m.hidden_dim, m.ffn_dim, m.vocab
+    hd = H // m.n_heads
+    q, kv = m.n_heads * hd, m.n_kv_heads * hd
+    qb = lambda n: from_pack.quant_bytes(n, m.quant)
+    if cls == "matvec_qkv":
+        return qb((q + 2 * kv) * H) + 4 * T * (H + q + 2 * kv)
+    if cls == "matvec_o":
+        return qb(H * q) + 4 * T * (q + 2 * H)
+    if cls == "matvec_gate_up":
+        return qb(2 * F * H) + 4 * T * (H + F)
+    if cls == "matvec_down":
+        return qb(H * F) + 4 * T * (F + 2 * H)
+    if cls == "matvec_lm_head":
+        return from_pack.quant_bytes(V * H, m.lm_head_quant) + 4 * T * (H + V)
+    raise KeyError(cls)
+
+
+def run_ours(args):
+    rank, world, local = dist_env()
+    import torch
+
+    torch.cuda.set_device(local)
+    import __graft_entry__ as g
+
+    pkg = g.load_package()
+    lib = pkg._lib.load()
+    m = pkg.pack.MODELS[args.model]
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    M = args.microbatches
+    assert M >= world, "need at least one micro-batch per stage"
+    L = pkg.pack.layer_layout(m)["total"]
+    hd = m.hidden_dim // m.n_heads
+    kv_layer = pkg.planner.kv_bytes_per_layer(m.n_kv_heads, hd, args.prompt + 64, 4) * M
+    plan = pkg.planner.plan_gpus(m.n_layers, world, L, kv_layer, pkg.pack.tensor_bytes(m, "embed"),
+                                 pkg.pack.tensor_bytes(m, "lm_head"))
+    st = plan[rank]
+    lo, hi = st["layers"]
+    n_decode = args.warmup + 3 * args.steps + 2
+    t_init = time.perf_counter()
+    w = device_weights(pkg, torch, m, lo, hi, st["is_first"], st["is_last"])
+    ctx = pkg.initStage({"arch": "llama", "dims": m.dims(), "layers": [lo, hi], "is_first": st["is_first"],
+                         "is_last": st["is_last"], "weights": w,
+                         "opts": {"device": local, "max_ctx": args.prompt + n_decode + 4, "max_seqs": M,
+                                  "max_tokens_per_step": 512}})
+    del w
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    t_init = time.perf_counter() - t_init
+    prompts = [pkg.pack.synth_prompt(m, args.prompt, seed=100 + mb) for mb in range(M)]
+    t_pre = time.perf_counter()
+    first_tok = prefill(pkg, torch, ctx, rank, world, prompts, m.hidden_dim)
+    torch.cuda.synchronize()
+    t_pre = time.perf_counter() - t_pre
+    pipe = Pipeline(pkg, torch, ctx, rank, world, M, m.hidden_dim)
+    pipe.pos = [args.prompt] * M
+    if rank == 0:
+        pipe.tok.copy_(torch.tensor(first_tok, dtype=torch.int32).view(M, 1))
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        import torch.distributed as dist
+
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # warm-up (captures the decode-step CUDA graph)
+    pipe.rounds(args.warmup)
+    barrier()
+    # ---- timed: device-resident inputs, CUDA events on the stage stream
+    clocks = ClockSampler(physical_gpu(local))
+    clocks.start()
+    time.sleep(0.3)
+    barrier()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(pipe.stream)
+    pipe.rounds(args.steps)
+    ev1.record(pipe.stream)
+    barrier()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    clk = clocks.stop()
+    info = ctx.info()
+    tokens = args.steps * M
+    value = tokens / (ms / 1e3)
+    launches = info["launches_last_step"] * tokens
+    # ---- e2e: the host-buffer API (tn_stage_forward) for every micro-batch step
+    e2e_val, h2d, d2h = None, 0, 0
+    if world == 1:
+        toks = pipe.tok.cpu().view(-1).tolist()
+        barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            for mb in range(M):
+                toks[mb] = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [toks[mb]],
+                                             "temperature": 0})["token_id"]
+                pipe.pos[mb] += 1
+        torch.cuda.synchronize()
+        e2e_s = time.perf_counter() - t0
+        e2e_val = tokens / e2e_s
+        h2d, d2h = 4 * M, 4 * M  # token ids in, token ids out, per round
+        pipe.tok.copy_(torch.tensor(toks, dtype=torch.int32).view(M, 1))
+    else:
+        e2e_val, h2d, d2h = pipeline_e2e(pkg, torch, ctx, pipe, args, rank, world, barrier, max_over_ranks)
+    # ---- profiled pass: per-kernel device time (CUDA events around each launch)
+    pkg._lib.check(lib.tn_stage_set_profile(ctx.handle, 1))
+    ctx.profile(reset=True)
+    toks = pipe.tok.cpu().view(-1).tolist() if rank == 0 else None
+    if world == 1:
+        for _ in range(args.steps):
+            for mb in range(M):
+                toks[mb] = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [toks[mb]],
+                                             "temperature": 0})["token_id"]
+                pipe.pos[mb] += 1
+    prof = ctx.profile() if world == 1 else {}
+    pkg._lib.check(lib.tn_stage_set_profile(ctx.handle, 0))
+    peak, peak_kind = measured_peaks()
+    mv = [k for k in prof if k.startswith("matvec") and prof[k][1] > 0]
+    roof = None
+    if mv:
+        tot_bytes = sum(matvec_bytes(pkg, m, k) * prof[k][1] for k in mv)
+        tot_ms = sum(prof[k][0] for k in mv)
+        n_launch = sum(prof[k][1] for k in mv)
+        achieved = tot_bytes / (tot_ms / 1e3) / 1e9
+        traffic = None
+        tf = ROOT / "profiles" / "matvec_decode_70b_traffic.json"
+        if tf.exists():
+            traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+        roof = {"kernel": "k_matvec (q4_0 register-dequant, 1 token)", "bound": "hbm",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                "traffic": traffic, "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                "algorithmic_bytes_per_launch": int(tot_bytes / n_launch), "launches": n_launch,
+                "avg_launch_us": round(tot_ms / n_launch * 1e3, 2),
+                "share_of_step_time": round(tot_ms / sum(v[0] for v in prof.values()), 4)}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        n_threads = os.cpu_count() or 1
+        os.environ["TABNET_ORACLE_THREADS"] = str(n_threads)
+        o = oracle_token_time(pkg, m, n_threads, 3)
+        cpu = {"value": o["tok_s"], "unit": "tok/s", "cores": n_threads, "kind": "port", "sample": o["sample"]}
+    step_bytes = pkg.pack.model_bytes(m) + M * m.n_layers * 2 * (args.prompt + args.warmup + args.steps) * \
+        m.n_kv_heads * hd * 4
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": SCALING, "vs_baseline": None, "dtype": "f32 (q4_0 weights, f32 activations and accumulate)",
+            "data": "synthetic (seeded weights and prompts)", "config": workload_config(args, world),
+            "e2e": {"value": round(e2e_val, 3) if e2e_val else None, "unit": "tok/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches, "clocks": clk, "roofline": roof, "cpu_baseline": cpu,
+            "detail": {"weight_roofline_tok_s": round(peak * 1e9 / pkg.pack.model_bytes(m) * world, 1),
+                       "step_bytes_whole_model": step_bytes, "init_s": round(t_init, 1), "prefill_s": round(t_pre, 1),
+                       "prefill_tok_s": round(M * args.prompt / t_pre, 1),
+                       "profile_ms": {k: [round(v[0], 3), v[1]] for k, v in prof.items()}}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    pkg.freeStage(ctx)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def pipeline_e2e(pkg, torch, ctx, pipe, args, rank, world, barrier, max_over_ranks):
+    """e2e for N>1: each stage step goes through the host-buffer API; the
+    returned fp16 frames cross to the next rank over NCCL."""
+    import torch.distributed as dist
+
+    M, H, W = pipe.M, pipe.H, world
+    n = args.steps * M
+    toks = pipe.tok.cpu().view(-1).tolist() if rank == 0 else None
+    barrier()
+    t0 = time.perf_counter()
+    for j in range(n):  # sequential hop through the stages, micro-batch by micro-batch
+        mb = j % M
+        if rank == 0:
+            out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [toks[mb]]})
+            dist.send(torch.from_numpy(out["hidden"].view(np.int16).copy()).cuda(), 1)
+            t = torch.empty(1, dtype=torch.int32, device="cuda")
+            dist.recv(t, W - 1)
+            toks[mb] = int(t.item())
+        else:
+            buf = torch.empty(H, dtype=torch.int16, device="cuda")
+            dist.recv(buf, rank - 1)
+            out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb],
+                                    "hidden": buf.cpu().numpy().view(np.uint16), "temperature": 0})
+            if ctx.is_last:
+                dist.send(torch.tensor([out["token_id"]], dtype=torch.int32, device="cuda"), 0)
+            else:
+                dist.send(torch.from_numpy(out["hidden"].view(np.int16).copy()).cuda(), rank + 1)
+        pipe.pos[mb] += 1
+    torch.cuda.synchronize()
+    s = max_over_ranks(time.perf_counter() - t0)
+    if rank == 0:
+        pipe.tok.copy_(torch.tensor(toks, dtype=torch.int32).view(M, 1))
+    return n / s, 4 * M + 2 * H * M * (W - 1), 4 * M + 2 * H * M * (W - 1)
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

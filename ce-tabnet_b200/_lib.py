@@ -19,6 +19,9 @@ STATUS_NAMES = {0: "TN_OK", -1: "TN_EINVAL", -2: "TN_ENOMEM", -3: "TN_ECUDA", -4
 QUANT = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 3}
 TN_HOP_LAST, TN_HOP_ALL = 0, 1
 TN_FLAG_NO_GRAPHS = 1
+TN_FLAG_PROFILE = 2
+PROF_CLASSES = ["matvec_qkv", "matvec_o", "matvec_gate_up", "matvec_down", "matvec_lm_head", "attention",
+                "rmsnorm", "rope_kv", "other"]
 TN_TAG_EMBED, TN_TAG_NORM, TN_TAG_LM_HEAD = 1, 2, 3
 
 
@@ -79,7 +82,7 @@ class StageInfo(C.Structure):
     _fields_ = [("weight_bytes", C.c_uint64), ("kv_bytes", C.c_uint64), ("scratch_bytes", C.c_uint64),
                 ("packed_bytes", C.c_uint64), ("n_layers", C.c_int32), ("head_dim", C.c_int32),
                 ("q_dim", C.c_int32), ("kv_dim", C.c_int32), ("ffn_dim", C.c_int32),
-                ("graphs_captured", C.c_int32)]
+                ("graphs_captured", C.c_int32), ("launches_last_step", C.c_int32)]
 
 
 class Dims(C.Structure):
@@ -99,6 +102,9 @@ SIGNATURES = [
     ("tn_stage_step_async", C.c_int, [C.c_void_p, C.POINTER(StepDesc), C.c_void_p]),
     ("tn_stage_stream", C.c_void_p, [C.c_void_p]),
     ("tn_stage_get_info", C.c_int, [C.c_void_p, C.POINTER(StageInfo)]),
+    ("tn_stage_peek", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_uint64]),
+    ("tn_stage_profile", C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64), C.c_int32]),
+    ("tn_stage_set_profile", C.c_int, [C.c_void_p, C.c_int32]),
     ("tn_matrix_create", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_void_p, C.c_uint64,
                                    C.c_int32, C.POINTER(C.c_void_p)]),
     ("tn_matrix_matvec", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),

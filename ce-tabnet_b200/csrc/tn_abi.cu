@@ -55,7 +55,7 @@ extern "C" int tn_matrix_create(int32_t device, int32_t quant, int32_t rows, int
   tn_matrix* M = new (std::nothrow) tn_matrix();
   TN_REQUIRE(M, TN_ENOMEM, "out of host memory");
   M->device = device;
-  int rc = matrix_alloc(&M->m, quant, rows, cols);
+  int rc = matrix_alloc(&M->m, quant, rows, cols, 0);
   uint8_t* staging = nullptr;
   const uint8_t* src = (const uint8_t*)packed;
   if (!rc && !on_device) {

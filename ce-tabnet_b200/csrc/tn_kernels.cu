@@ -72,6 +72,28 @@ __global__ void k_repack_q(const uint8_t* __restrict__ src, int quant, int src_r
   }
 }
 
+// same, for a 2-byte aligned source (every block then starts on an even
+// address): 16-bit loads, one or two 16-byte stores per block
+template <int QB>
+__global__ void k_repack_q16(const uint16_t* __restrict__ src, int src_rows, int nb, int dst_off,
+                             int dst_stride, uint4* __restrict__ data, uint16_t* __restrict__ scales) {
+  constexpr int BW = QB / 2 + 1;  // 16-bit words per block
+  const uint64_t total = (uint64_t)src_rows * nb;
+  for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < total;
+       k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t r = k / nb, b = k % nb;
+    const uint16_t* blk = src + k * BW;
+    const uint64_t dr = (uint64_t)dst_off + r * (uint64_t)dst_stride;
+    uint32_t w[QB / 4];
+#pragma unroll
+    for (int j = 0; j < QB / 4; j++) w[j] = (uint32_t)blk[1 + 2 * j] | ((uint32_t)blk[2 + 2 * j] << 16);
+    uint4* dq = data + (dr * nb + b) * (QB / 16);
+#pragma unroll
+    for (int v = 0; v < QB / 16; v++) dq[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
+    scales[((dr >> 3) * nb + b) * 8 + (dr & 7)] = blk[0];
+  }
+}
+
 // any source format into an MK_F32 / MK_F16 matrix (exact values)
 __global__ void k_repack_plain(const uint8_t* __restrict__ src, int quant, int src_rows, int cols,
                                int cols_pad, int dst_off, int dst_stride, int kind,
@@ -92,7 +114,7 @@ __global__ void k_repack_plain(const uint8_t* __restrict__ src, int quant, int s
 
 static void mv_prepare(Matrix* m);
 
-int matrix_alloc(Matrix* m, int src_quant, int rows, int cols) {
+int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
   TN_REQUIRE(rows > 0 && cols > 0, TN_EINVAL, "matrix: bad shape %d x %d", rows, cols);
   TN_REQUIRE(quant_bytes(1, src_quant) != 0, TN_EUNSUPPORTED, "unsupported quant %d", src_quant);
   m->rows = rows;
@@ -108,10 +130,11 @@ int matrix_alloc(Matrix* m, int src_quant, int rows, int cols) {
   const size_t dbytes = (size_t)m->rows_pad * m->nb * kind_block_bytes(m->kind);
   const size_t sbytes = (m->kind == MK_Q4 || m->kind == MK_Q8) ? (size_t)m->rows_pad * m->nb * 2 : 0;
   TN_CHECK_CUDA(cudaMalloc(&m->data, dbytes));
-  TN_CHECK_CUDA(cudaMemset(m->data, 0, dbytes));
+  // zero padding rows/columns on the stream the repack kernels will use
+  TN_CHECK_CUDA(cudaMemsetAsync(m->data, 0, dbytes, s));
   if (sbytes) {
     TN_CHECK_CUDA(cudaMalloc(&m->scales, sbytes));
-    TN_CHECK_CUDA(cudaMemset(m->scales, 0, sbytes));
+    TN_CHECK_CUDA(cudaMemsetAsync(m->scales, 0, sbytes, s));
   }
   m->bytes = dbytes + sbytes;
   num_sms();
@@ -124,7 +147,14 @@ int matrix_repack(Matrix* m, const uint8_t* d_src, int src_quant, int src_rows, 
   TN_REQUIRE(dst_off + (int64_t)(src_rows - 1) * dst_stride < m->rows, TN_EINVAL,
              "matrix_repack: rows out of range");
   const int grid = std::min(148 * 32, (int)std::max<int64_t>(1, ((int64_t)src_rows * m->nb + 255) / 256));
-  if (m->kind == MK_Q4 || m->kind == MK_Q8) {
+  const bool even = (reinterpret_cast<uintptr_t>(d_src) & 1) == 0;
+  if (m->kind == MK_Q4 && even) {
+    k_repack_q16<16><<<grid, 256, 0, s>>>((const uint16_t*)d_src, src_rows, m->nb, dst_off, dst_stride,
+                                          (uint4*)m->data, m->scales);
+  } else if (m->kind == MK_Q8 && even) {
+    k_repack_q16<32><<<grid, 256, 0, s>>>((const uint16_t*)d_src, src_rows, m->nb, dst_off, dst_stride,
+                                          (uint4*)m->data, m->scales);
+  } else if (m->kind == MK_Q4 || m->kind == MK_Q8) {
     k_repack_q<<<grid, 256, 0, s>>>(d_src, src_quant, src_rows, m->nb, dst_off, dst_stride, m->data,
                                     m->scales);
   } else {

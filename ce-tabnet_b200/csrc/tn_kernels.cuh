@@ -30,7 +30,7 @@ __host__ __device__ constexpr int kind_block_bytes(int k) {
   return k == MK_Q4 ? 16 : (k == MK_Q8 ? 32 : (k == MK_F16 ? 64 : 128));
 }
 
-int matrix_alloc(Matrix* m, int src_quant, int rows, int cols);
+int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s);
 // Repack src_rows rows of a packed tensor (device memory, reference layout,
 // `cols` columns) into rows dst_off + r * dst_stride of m.
 int matrix_repack(Matrix* m, const uint8_t* d_src, int src_quant, int src_rows, int dst_off,

@@ -55,6 +55,11 @@ static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 enum { IN_IDS = 0, IN_HIDDEN = 1 };
 constexpr int CTL_RING = 8;
 
+struct GraphEntry {
+  cudaGraphExec_t exec = nullptr;
+  int n_ev = 0, n_launch = 0;  // profiling events and kernel launches of the captured step
+};
+
 struct LayerW {
   Matrix qkv, o, gu, down;
   float* attn_norm = nullptr;
@@ -103,8 +108,15 @@ struct tn_stage {
   std::unordered_map<uint64_t, int> seq_slot;
   std::vector<int> free_slots;
   std::vector<int> kv_len;
-  std::map<std::tuple<int, int, int>, cudaGraphExec_t> graphs;
+  std::map<std::tuple<int, int, int>, GraphEntry> graphs;
   bool graphs_broken = false;
+  // per-launch timing (TN_FLAG_PROFILE): begin/end event pairs of the current step
+  bool prof = false;
+  std::vector<cudaEvent_t> ev;
+  std::vector<int> ev_class;
+  int ev_used = 0, step_launches = 0;
+  double prof_ms[TN_PROF_N] = {};
+  uint64_t prof_launches[TN_PROF_N] = {};
   uint64_t weight_bytes = 0, kv_bytes = 0, scratch_bytes = 0, packed_bytes = 0;
   std::vector<void*> allocs;  // scratch allocations
 
@@ -116,7 +128,8 @@ static void free_ptr(void* p) {
 }
 
 tn_stage::~tn_stage() {
-  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : graphs) cudaGraphExecDestroy(kv.second.exec);
+  for (cudaEvent_t e : ev) cudaEventDestroy(e);
   for (auto& L : layers) {
     matrix_free(&L.qkv);
     matrix_free(&L.o);
@@ -183,18 +196,18 @@ static int load_layer(tn_stage* st, const tn_stage_spec* sp, int li, uint8_t* st
   LayerW& W = st->layers[li];
   const int q = lw.quant;
   // wq | wk | wv fused into one [qDim + 2 kvDim, H] matrix
-  if ((rc = matrix_alloc(&W.qkv, q, st->qDim + 2 * st->kvDim, st->H))) return rc;
+  if ((rc = matrix_alloc(&W.qkv, q, st->qDim + 2 * st->kvDim, st->H, st->stream))) return rc;
   if ((rc = matrix_repack(&W.qkv, src + L.off[1], q, st->qDim, 0, 1, st->stream))) return rc;
   if ((rc = matrix_repack(&W.qkv, src + L.off[2], q, st->kvDim, st->qDim, 1, st->stream))) return rc;
   if ((rc = matrix_repack(&W.qkv, src + L.off[3], q, st->kvDim, st->qDim + st->kvDim, 1, st->stream)))
     return rc;
-  if ((rc = matrix_alloc(&W.o, q, st->H, st->qDim))) return rc;
+  if ((rc = matrix_alloc(&W.o, q, st->H, st->qDim, st->stream))) return rc;
   if ((rc = matrix_repack(&W.o, src + L.off[4], q, st->H, 0, 1, st->stream))) return rc;
   // w_gate / w_up interleaved by row: (2i, 2i+1) = (gate_i, up_i) for the SwiGLU epilogue
-  if ((rc = matrix_alloc(&W.gu, q, 2 * st->F, st->H))) return rc;
+  if ((rc = matrix_alloc(&W.gu, q, 2 * st->F, st->H, st->stream))) return rc;
   if ((rc = matrix_repack(&W.gu, src + L.off[6], q, st->F, 0, 2, st->stream))) return rc;
   if ((rc = matrix_repack(&W.gu, src + L.off[7], q, st->F, 1, 2, st->stream))) return rc;
-  if ((rc = matrix_alloc(&W.down, q, st->H, st->F))) return rc;
+  if ((rc = matrix_alloc(&W.down, q, st->H, st->F, st->stream))) return rc;
   if ((rc = matrix_repack(&W.down, src + L.off[8], q, st->H, 0, 1, st->stream))) return rc;
   // norms: f16 bits -> f32 (exact)
   TN_CHECK_CUDA(cudaMalloc(&W.attn_norm, align256(st->H * sizeof(float))));
@@ -284,7 +297,7 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   const uint8_t* src = nullptr;
   if (st->first) {
     if ((rc = stage_src(sp, sp->embed, embed_bytes, staging, &src))) return rc;
-    if ((rc = matrix_alloc(&st->embed, sp->embed_quant, st->V, st->H))) return rc;
+    if ((rc = matrix_alloc(&st->embed, sp->embed_quant, st->V, st->H, st->stream))) return rc;
     if ((rc = matrix_repack(&st->embed, src, sp->embed_quant, st->V, 0, 1, st->stream))) return rc;
     TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
     st->weight_bytes += st->embed.bytes;
@@ -292,7 +305,7 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   }
   if (st->last) {
     if ((rc = stage_src(sp, sp->lm_head, head_bytes, staging, &src))) return rc;
-    if ((rc = matrix_alloc(&st->lm_head, sp->lm_head_quant, st->V, st->H))) return rc;
+    if ((rc = matrix_alloc(&st->lm_head, sp->lm_head_quant, st->V, st->H, st->stream))) return rc;
     if ((rc = matrix_repack(&st->lm_head, src, sp->lm_head_quant, st->V, 0, 1, st->stream))) return rc;
     TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
     if ((rc = stage_src(sp, sp->norm, (uint64_t)st->H * 2, staging, &src))) return rc;
@@ -357,11 +370,51 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   }
   TN_CHECK_CUDA(cudaHostAlloc(&st->h_in, (size_t)T * st->H * sizeof(uint16_t) + 256, cudaHostAllocDefault));
   TN_CHECK_CUDA(cudaHostAlloc(&st->h_out, (size_t)T * st->H * sizeof(uint16_t) + 256, cudaHostAllocDefault));
+  if (st->flags & TN_FLAG_PROFILE) {
+    st->prof = true;
+    const int pairs = st->nL * 12 + 16;
+    st->ev.resize(2 * pairs);
+    st->ev_class.resize(pairs);
+    for (auto& e : st->ev) TN_CHECK_CUDA(cudaEventCreate(&e));
+  }
   st->kv_len.assign(st->max_seqs, 0);
   for (int i = st->max_seqs - 1; i >= 0; i--) st->free_slots.push_back(i);
   TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
   return TN_OK;
 }
+
+// record the begin event of a timed launch (no-op unless profiling)
+static int prof_begin(tn_stage* st, cudaStream_t s, int cls) {
+  if (!st->prof || st->ev_used * 2 + 1 >= (int)st->ev.size()) return -1;
+  const int i = st->ev_used++;
+  st->ev_class[i] = cls;
+  cudaEventRecord(st->ev[2 * i], s);
+  return i;
+}
+static void prof_end(tn_stage* st, cudaStream_t s, int i) {
+  if (i >= 0) cudaEventRecord(st->ev[2 * i + 1], s);
+}
+// fold the finished step's event pairs into the per-class totals (stream synchronised)
+static void prof_collect(tn_stage* st) {
+  if (!st->prof) return;
+  for (int i = 0; i < st->ev_used; i++) {
+    float ms = 0.f;
+    if (cudaEventElapsedTime(&ms, st->ev[2 * i], st->ev[2 * i + 1]) == cudaSuccess) {
+      st->prof_ms[st->ev_class[i]] += ms;
+      st->prof_launches[st->ev_class[i]] += 1;
+    }
+  }
+  st->ev_used = 0;
+}
+
+// launch `expr` (which starts `nk` kernels) as one timed unit of class `cls`
+#define TN_STEP_LAUNCH(cls, nk, expr)        \
+  do {                                       \
+    const int pi_ = prof_begin(st, s, cls);  \
+    if ((rc = (expr))) return rc;            \
+    prof_end(st, s, pi_);                    \
+    st->step_launches += (nk);               \
+  } while (0)
 
 // the layer stack for T rows already described by the control block
 static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t s) {
@@ -370,34 +423,37 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
   const double* params = (const double*)(st->d_ctl + st->ctl_params_off);
   const int H = st->H, ldqkv = st->qDim + 2 * st->kvDim;
   int rc;
-  if (input_kind == IN_IDS) rc = embed_rows(st->embed, st->ids, T, st->h, H, st->err, s);
-  else rc = hop_decode(st->hid_in, (uint64_t)T * H, st->h, s);
-  if (rc) return rc;
-  if ((rc = rope_table(rows, st->freq, st->hd / 2, T, st->cs, s))) return rc;
+  st->ev_used = 0;
+  st->step_launches = 0;
+  if (input_kind == IN_IDS)
+    TN_STEP_LAUNCH(TN_PROF_OTHER, 1, embed_rows(st->embed, st->ids, T, st->h, H, st->err, s));
+  else
+    TN_STEP_LAUNCH(TN_PROF_OTHER, 1, hop_decode(st->hid_in, (uint64_t)T * H, st->h, s));
+  TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1, rope_table(rows, st->freq, st->hd / 2, T, st->cs, s));
   const int ns = attn_splits(T, st->nKV, st->max_ctx);
   for (int l = 0; l < st->nL; l++) {
     LayerW& L = st->layers[l];
     float* kc = st->kc + (size_t)l * st->layer_stride;
     float* vc = st->vc + (size_t)l * st->layer_stride;
-    if ((rc = rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s))) return rc;
-    if ((rc = matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, s))) return rc;
-    if ((rc = rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->slot_stride, st->kvh_stride, st->nH,
-                      st->nKV, st->hd, T, s)))
-      return rc;
-    if ((rc = attention(st->q, st->qDim, kc, vc, st->slot_stride, st->kvh_stride, rows, T, st->nH, st->nKV,
-                        st->hd, ns, st->att, st->qDim, st->attn_scratch, s)))
-      return rc;
-    if ((rc = matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, s))) return rc;
-    if ((rc = rmsnorm(st->h, H, nullptr, L.ffn_norm, st->xn, H, H, T, s))) return rc;
-    if ((rc = matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, s))) return rc;
-    if ((rc = matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, s))) return rc;
+    TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
+    TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, s));
+    TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1,
+                   rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->slot_stride, st->kvh_stride, st->nH,
+                           st->nKV, st->hd, T, s));
+    TN_STEP_LAUNCH(TN_PROF_ATTENTION, 2,
+                   attention(st->q, st->qDim, kc, vc, st->slot_stride, st->kvh_stride, rows, T, st->nH, st->nKV,
+                             st->hd, ns, st->att, st->qDim, st->attn_scratch, s));
+    TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, s));
+    TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.ffn_norm, st->xn, H, H, T, s));
+    TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, s));
+    TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, s));
   }
   if (st->last) {
-    if ((rc = rmsnorm(st->h, H, outrows, st->final_norm, st->xn, H, H, n_out, s))) return rc;
-    if ((rc = matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, s))) return rc;
-    if ((rc = sample_rows(st->logits, n_out, st->V, params, st->tok_out, s))) return rc;
+    TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, outrows, st->final_norm, st->xn, H, H, n_out, s));
+    TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1, matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, s));
+    TN_STEP_LAUNCH(TN_PROF_OTHER, 1, sample_rows(st->logits, n_out, st->V, params, st->tok_out, s));
   } else {
-    if ((rc = hop_encode_rows(st->h, H, outrows, n_out, H, st->hid_out, s))) return rc;
+    TN_STEP_LAUNCH(TN_PROF_OTHER, 1, hop_encode_rows(st->h, H, outrows, n_out, H, st->hid_out, s));
   }
   return TN_OK;
 }
@@ -422,17 +478,21 @@ static int launch_step(tn_stage* st, int T, int n_out, int input_kind, bool grap
       st->graphs_broken = true;
       return run_step(st, T, n_out, input_kind, s);
     }
-    cudaGraphExec_t ex = nullptr;
-    const cudaError_t ie = cudaGraphInstantiate(&ex, g, 0);
+    GraphEntry ge;
+    ge.n_ev = st->ev_used;
+    ge.n_launch = st->step_launches;
+    const cudaError_t ie = cudaGraphInstantiate(&ge.exec, g, 0);
     cudaGraphDestroy(g);
     if (ie != cudaSuccess) {
       cudaGetLastError();
       st->graphs_broken = true;
       return run_step(st, T, n_out, input_kind, s);
     }
-    it = st->graphs.emplace(key, ex).first;
+    it = st->graphs.emplace(key, ge).first;
   }
-  TN_CHECK_CUDA(cudaGraphLaunch(it->second, s));
+  TN_CHECK_CUDA(cudaGraphLaunch(it->second.exec, s));
+  st->ev_used = it->second.n_ev;
+  st->step_launches = it->second.n_launch;
   return TN_OK;
 }
 
@@ -580,6 +640,10 @@ static int forward_impl(tn_stage* st, const tn_fwd_req* reqs, int n, tn_fwd_out*
     }
     if (n_out == 0) {
       if ((rc = run_step(st, T, 0, st->first ? IN_IDS : IN_HIDDEN, s))) return rc;
+      if (st->prof) {
+        TN_CHECK_CUDA(cudaStreamSynchronize(s));
+        prof_collect(st);
+      }
       continue;
     }
     if ((rc = launch_step(st, T, n_out, st->first ? IN_IDS : IN_HIDDEN, decode_shape, s))) return rc;
@@ -589,6 +653,7 @@ static int forward_impl(tn_stage* st, const tn_fwd_req* reqs, int n, tn_fwd_out*
       TN_CHECK_CUDA(cudaMemcpyAsync(st->h_out, st->hid_out, (size_t)n_out * H * sizeof(uint16_t),
                                     cudaMemcpyDeviceToHost, s));
     TN_CHECK_CUDA(cudaStreamSynchronize(s));
+    prof_collect(st);
     for (int o = 0; o < n_out; o++) {
       const RowRef& rr = refs[out_global[o]];
       tn_fwd_out& out = outs[rr.req];
@@ -743,6 +808,58 @@ extern "C" int tn_stage_get_info(tn_stage* st, tn_stage_info* info) {
   info->kv_dim = st->kvDim;
   info->ffn_dim = st->F;
   info->graphs_captured = (int32_t)st->graphs.size();
+  info->launches_last_step = st->step_launches;
+  return TN_OK;
+}
+
+extern "C" int tn_stage_profile(tn_stage* st, double* ms, uint64_t* launches, int32_t reset) {
+  clear_error();
+  TN_REQUIRE(st, TN_EINVAL, "null stage");
+  std::lock_guard<std::mutex> lk(st->mu);
+  TN_REQUIRE(st->prof, TN_ESTATE, "stage was created without TN_FLAG_PROFILE");
+  for (int k = 0; k < TN_PROF_N; k++) {
+    if (ms) ms[k] = st->prof_ms[k];
+    if (launches) launches[k] = st->prof_launches[k];
+    if (reset) {
+      st->prof_ms[k] = 0;
+      st->prof_launches[k] = 0;
+    }
+  }
+  return TN_OK;
+}
+
+extern "C" int tn_stage_set_profile(tn_stage* st, int32_t on) {
+  clear_error();
+  TN_REQUIRE(st, TN_EINVAL, "null stage");
+  std::lock_guard<std::mutex> lk(st->mu);
+  TN_ENTER_DEVICE(st->device);
+  TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
+  if (on && st->ev.empty()) {
+    const int pairs = st->nL * 12 + 16;
+    st->ev.resize(2 * pairs);
+    st->ev_class.resize(pairs);
+    for (auto& e : st->ev) TN_CHECK_CUDA(cudaEventCreate(&e));
+  }
+  if ((bool)on != st->prof) {
+    for (auto& kv : st->graphs) cudaGraphExecDestroy(kv.second.exec);
+    st->graphs.clear();
+  }
+  st->prof = on != 0;
+  st->ev_used = 0;
+  return TN_OK;
+}
+
+extern "C" int tn_stage_peek(tn_stage* st, int32_t what, void* host_out, uint64_t bytes) {
+  clear_error();
+  TN_REQUIRE(st && host_out, TN_EINVAL, "null argument");
+  std::lock_guard<std::mutex> lk(st->mu);
+  TN_ENTER_DEVICE(st->device);
+  TN_REQUIRE(what == TN_PEEK_HIDDEN || (what == TN_PEEK_LOGITS && st->last), TN_EINVAL, "peek: bad target %d", what);
+  const void* src = what == TN_PEEK_HIDDEN ? (const void*)st->h : (const void*)st->logits;
+  const uint64_t cap = what == TN_PEEK_HIDDEN ? (uint64_t)st->max_T * st->H * 4
+                                              : (uint64_t)std::max(1, std::min(st->max_T, st->max_seqs)) * st->V * 4;
+  TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
+  TN_CHECK_CUDA(cudaMemcpy(host_out, src, std::min(bytes, cap), cudaMemcpyDeviceToHost));
   return TN_OK;
 }
 

@@ -29,10 +29,26 @@ def _quant_code(q: str) -> int:
     return _lib.QUANT[q]
 
 
-def _as_u8(buf) -> np.ndarray:
+def _as_u8(buf):
+    """Host bytes as a uint8 array; a device tensor (weights already in GPU
+    memory) passes through with data_ptr()/nbytes."""
+    if hasattr(buf, "data_ptr"):
+        return _DevBuf(buf.data_ptr(), buf.numel() * buf.element_size())
     if isinstance(buf, np.ndarray):
         return np.ascontiguousarray(buf).view(np.uint8).reshape(-1)
     return np.frombuffer(memoryview(buf), dtype=np.uint8)
+
+
+class _DevBuf:
+    """Minimal stand-in exposing .ctypes.data / .nbytes for a device pointer."""
+
+    class _Ptr:
+        def __init__(self, p):
+            self.data = p
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.ctypes = self._Ptr(ptr)
+        self.nbytes = nbytes
 
 
 @dataclass
@@ -57,6 +73,22 @@ class StageCtx:
         if seq_id not in self._seq_ids:
             self._seq_ids[seq_id] = next(self._next_seq)
         return self._seq_ids[seq_id]
+
+    def peek(self, what: str, rows: int) -> np.ndarray:
+        """Test hook: f32 hidden rows ("hidden") or logits ("logits") of the last step."""
+        width = self.hidden_dim if what == "hidden" else int(self.dims["vocab"])
+        out = np.zeros((rows, width), dtype=np.float32)
+        code = 0 if what == "hidden" else 1
+        _lib.check(_lib.load().tn_stage_peek(self.handle, code, out.ctypes.data, out.nbytes))
+        return out
+
+    def profile(self, reset: bool = False) -> dict:
+        """{kernel class: (ms, launches)} of synchronous calls (opts.profile stages)."""
+        n = len(_lib.PROF_CLASSES)
+        ms = (C.c_double * n)()
+        cnt = (C.c_uint64 * n)()
+        _lib.check(_lib.load().tn_stage_profile(self.handle, ms, cnt, int(reset)))
+        return {k: (ms[i], int(cnt[i])) for i, k in enumerate(_lib.PROF_CLASSES)}
 
     def info(self) -> dict:
         inf = _lib.StageInfo()
@@ -115,7 +147,8 @@ def initStage(spec: dict) -> StageCtx:
     s.max_ctx = int(opts.get("max_ctx", 4096))  # :642
     s.max_seqs = int(opts.get("max_seqs", 16))
     s.max_tokens_per_step = int(opts.get("max_tokens_per_step", 512))
-    s.flags = _lib.TN_FLAG_NO_GRAPHS if opts.get("no_graphs") else 0
+    s.flags = (_lib.TN_FLAG_NO_GRAPHS if opts.get("no_graphs") else 0) | \
+        (_lib.TN_FLAG_PROFILE if opts.get("profile") else 0)
     handle = C.c_void_p()
     _lib.check(lib.tn_stage_init(C.byref(s), C.byref(handle)))
     return StageCtx(handle=handle, dims=dict(dims), layers=(lo, hi), is_first=bool(spec.get("is_first")),
@@ -129,6 +162,8 @@ def _build_req(ctx: StageCtx, req: dict, keep: list):
     if ctx.is_first:
         ids = req.get("token_ids")
         if ids is None or len(ids) == 0:
+            if req.get("token_id") is None:
+                raise _lib.TnError(_lib.TN_ESTATE, "first stage: token_ids or token_id required")
             ids = [req["token_id"]]  # :480
         a = np.ascontiguousarray(np.asarray(ids, dtype=np.int32))
         keep.append(a)

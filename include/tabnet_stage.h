@@ -50,6 +50,7 @@ enum { TN_HOP_LAST = 0, TN_HOP_ALL = 1 };
 
 /* spec flags */
 #define TN_FLAG_NO_GRAPHS (1u << 0) /* never capture decode steps in CUDA graphs */
+#define TN_FLAG_PROFILE (1u << 1)   /* time every kernel launch with CUDA events (tn_stage_profile) */
 
 /* One layer's packed buffer, tensors in web/inference-worker.js:142-159 order:
  * attn_norm(f16) wq wk wv wo ffn_norm(f16) w_gate w_up w_down. */
@@ -157,8 +158,28 @@ typedef struct {
   uint64_t packed_bytes;   /* packed (reference-format) bytes the weights came from */
   int32_t n_layers, head_dim, q_dim, kv_dim, ffn_dim;
   int32_t graphs_captured; /* decode-step CUDA graphs instantiated so far */
+  int32_t launches_last_step; /* kernels the last step launched */
 } tn_stage_info;
 int tn_stage_get_info(tn_stage* st, tn_stage_info* info);
+
+/* Per-kernel device time of the synchronous forward calls since the last
+ * reset, for stages created with TN_FLAG_PROFILE: ms[k] and launches[k] for
+ * each class k below (arrays of TN_PROF_N). */
+enum {
+  TN_PROF_MATVEC_QKV = 0, TN_PROF_MATVEC_O, TN_PROF_MATVEC_GATE_UP, TN_PROF_MATVEC_DOWN,
+  TN_PROF_MATVEC_LM_HEAD, TN_PROF_ATTENTION, TN_PROF_NORM, TN_PROF_ROPE_KV, TN_PROF_OTHER, TN_PROF_N
+};
+int tn_stage_profile(tn_stage* st, double* ms, uint64_t* launches, int32_t reset);
+/* Turn per-launch timing on or off after init (drops captured graphs, which
+ * are re-captured with or without the timing events). */
+int tn_stage_set_profile(tn_stage* st, int32_t on);
+
+/* Test hook: copy device state left by the last forward/step call into host
+ * memory (synchronises the stage's stream).  what = TN_PEEK_HIDDEN: the f32
+ * hidden rows of that step, [rows][hidden_dim]; TN_PEEK_LOGITS (last stage):
+ * the f32 logits of its output rows, [n_out][vocab].  Copies min(bytes, size). */
+enum { TN_PEEK_HIDDEN = 0, TN_PEEK_LOGITS = 1 };
+int tn_stage_peek(tn_stage* st, int32_t what, void* host_out, uint64_t bytes);
 
 /* ---- single-op entry points (tests, microbenchmarks) ---- */
 
