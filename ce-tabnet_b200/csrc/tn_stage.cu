@@ -383,16 +383,24 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   return TN_OK;
 }
 
+// an event record that survives stream capture as a graph node
+static void record_event(cudaEvent_t e, cudaStream_t s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaStreamIsCapturing(s, &cs);
+  if (cs == cudaStreamCaptureStatusActive) cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+  else cudaEventRecord(e, s);
+}
+
 // record the begin event of a timed launch (no-op unless profiling)
 static int prof_begin(tn_stage* st, cudaStream_t s, int cls) {
   if (!st->prof || st->ev_used * 2 + 1 >= (int)st->ev.size()) return -1;
   const int i = st->ev_used++;
   st->ev_class[i] = cls;
-  cudaEventRecord(st->ev[2 * i], s);
+  record_event(st->ev[2 * i], s);
   return i;
 }
 static void prof_end(tn_stage* st, cudaStream_t s, int i) {
-  if (i >= 0) cudaEventRecord(st->ev[2 * i + 1], s);
+  if (i >= 0) record_event(st->ev[2 * i + 1], s);
 }
 // fold the finished step's event pairs into the per-class totals (stream synchronised)
 static void prof_collect(tn_stage* st) {
