@@ -1,0 +1,124 @@
+"""The oracle against the hand-derived known-answer fixtures of tests/golden/
+(the reference has no golden vectors of its own), plus CPU self-consistency
+checks of the restatement (no GPU)."""
+import json
+import struct
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+GOLD = Path(__file__).resolve().parent / "golden"
+
+
+def bits_to_f32(s: str) -> float:
+    return struct.unpack("<f", struct.pack("<I", int(s, 16)))[0]
+
+
+def test_f32_to_f16_kats(ref, pkg):
+    kat = json.loads((GOLD / "kat_f16.json").read_text())
+    lib = pkg._lib.load()
+    for src, want, why in kat["f32_to_f16"]:
+        v = bits_to_f32(src)
+        assert ref.f32_to_f16(v) == int(want, 16), (src, why)
+        assert lib.tn_hop_encode_host(v) == int(want, 16), (src, why)
+
+
+def test_f16_to_f32_kats(ref):
+    kat = json.loads((GOLD / "kat_f16.json").read_text())
+    for src, want, why in kat["f16_to_f32"]:
+        got = np.float32(ref.f16_to_f32(int(src, 16))).view(np.uint32)
+        assert int(got) == int(want, 16), (src, why)
+
+
+def test_quant_kats(ref):
+    kat = json.loads((GOLD / "kat_quant.json").read_text())
+    for q in ("q4_0", "q8_0"):
+        k = kat[q]
+        got = ref.dequant(np.array(k["bytes"], dtype=np.uint8), q, k["count"])
+        assert got.tolist() == k["expected"], k["derivation"]
+    s = kat["straddle"]
+    buf = np.array(s["bytes"], dtype=np.uint8)
+    got = ref.dequant(buf, s["quant"], s["cols"], start=s["cols"])
+    assert got.tolist() == s["expected_row1"], s["derivation"]
+    # a matvec over straddling rows reads exactly those values
+    x = np.ones(s["cols"], dtype=np.float32)
+    y = ref.matvec(buf, s["quant"], s["rows"], s["cols"], x)
+    assert y[1] == np.float32(sum(s["expected_row1"]))
+
+
+def test_sizes_kats(ref, pkg):
+    kat = json.loads((GOLD / "kat_quant.json").read_text())["sizes"]
+    for n, q, want in kat["quant_bytes"]:
+        assert ref.quant_bytes(n, q) == want
+    for H, want in kat["round_ffn"]:
+        assert ref.load().ref_round_ffn(H) == want
+    for name, want in kat["layer_bytes"].items():
+        assert pkg.pack.layer_layout(pkg.pack.MODELS[name])["total"] == want
+
+
+def test_sample_kats(ref):
+    for k in json.loads((GOLD / "kat_sample.json").read_text()):
+        got = ref.sample(np.array(k["logits"], dtype=np.float32), k["temperature"], k["top_p"], k["u"])
+        assert got == k["expected"], k["derivation"]
+
+
+def test_rope_position_zero_is_identity(ref):
+    v = np.random.default_rng(0).standard_normal(4 * 64).astype(np.float32)
+    assert np.array_equal(ref.rope(v, 4, 64, 0, 10000.0), v)
+
+
+def test_rope_rotates_pairs(ref):
+    """Half-split pairing (i, i + hd/2) with angle pos * theta^(-2i/hd)."""
+    hd, pos, theta = 8, 3, 10000.0
+    v = np.arange(1, hd + 1, dtype=np.float32)
+    out = ref.rope(v, 1, hd, pos, theta)
+    for i in range(hd // 2):
+        ang = pos * theta ** (-2 * i / hd)
+        a, b = float(v[i]), float(v[i + hd // 2])
+        assert out[i] == np.float32(a * np.cos(ang) - b * np.sin(ang))
+        assert out[i + hd // 2] == np.float32(a * np.sin(ang) + b * np.cos(ang))
+
+
+def test_single_position_attention_returns_v(ref):
+    rng = np.random.default_rng(1)
+    nH, nKV, hd = 8, 2, 32
+    q = rng.standard_normal(nH * hd).astype(np.float32)
+    K = rng.standard_normal((1, nKV * hd)).astype(np.float32)
+    V = rng.standard_normal((1, nKV * hd)).astype(np.float32)
+    out = ref.attention(q, K, V, nH, nKV, hd)
+    for h in range(nH):
+        kvh = h // (nH // nKV)
+        assert np.array_equal(out[h * hd:(h + 1) * hd], V[0, kvh * hd:(kvh + 1) * hd])
+
+
+def test_stage_split_equals_whole_model_without_hops(ref, pkg):
+    """Two oracle stages joined by hidden states must reproduce a single stage
+    up to the fp16 hop rounding (the hop is the only extra rounding)."""
+    m = pkg.pack.MODELS["tiny"]
+    w = pkg.pack.synth_weights(m, 0, m.n_layers, True, True)
+    whole = ref.RefStage(m.dims(), 0, 4, True, True, w)
+    wa = dict(w, layers=w["layers"][:2])
+    wb = dict(w, layers=w["layers"][2:])
+    a = ref.RefStage(m.dims(), 0, 2, True, False, wa)
+    b = ref.RefStage(m.dims(), 2, 4, False, True, wb)
+    prompt = pkg.pack.synth_prompt(m, 6)
+    for p, t in enumerate(prompt):
+        hw = whole.forward(1, p, token_ids=[t])
+        ha = a.forward(1, p, token_ids=[t])
+        hb = b.forward(1, p, hidden=ha["hidden"])
+        err = np.max(np.abs(hw["hidden_f32"] - hb["hidden_f32"])) / np.max(np.abs(hw["hidden_f32"]))
+        assert err < 1e-2, (p, err)
+
+
+def test_tiny_greedy_fixture_matches_oracle(ref, pkg):
+    g = json.loads((GOLD / "tiny_greedy.json").read_text())
+    m = pkg.pack.MODELS["tiny"]
+    assert g["prompt"] == pkg.pack.synth_prompt(m, 32)
+    w = pkg.pack.synth_weights(m, 0, m.n_layers, True, True)
+    st = ref.RefStage(m.dims(), 0, 4, True, True, w)
+    r = st.forward(1, 0, token_ids=g["prompt"])
+    toks = [r["token_id"]]
+    for s in range(8):
+        toks.append(st.forward(1, 32 + s, token_ids=[toks[-1]])["token_id"])
+    assert toks == g["tokens"][:9]
