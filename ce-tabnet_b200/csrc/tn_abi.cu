@@ -1,5 +1,6 @@
 // tn_abi.cu -- single-op C entry points: quantised matrices, attention, the
 // activation hop codec and the sampler, for parity tests and microbenchmarks.
+#include <mutex>
 #include <vector>
 
 #include "tn_kernels.cuh"
@@ -142,6 +143,63 @@ extern "C" int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, in
   return attention(d_q, n_heads * head_dim, d_k, d_v, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows,
                    n_heads, n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out,
                    n_heads * head_dim, part, s);
+}
+
+// ---- tn_attention_static: attention with its scratch in a fixed device array,
+// for callers that cannot allocate device memory (see tabnet_stage.h).
+static __device__ __align__(256) unsigned char g_attn_static_scratch[TN_ATTENTION_STATIC_SCRATCH_BYTES];
+
+namespace tn {
+constexpr int kMaxStaticDevices = 64;
+static std::mutex g_attn_static_mu;
+static void* g_attn_static_ptr[kMaxStaticDevices];  // this array's device address, per device
+
+// Host code cannot use g_attn_static_scratch as a pointer (on the host it names
+// a stand-in, not device memory): look the address up for the current device,
+// once per device, with that device current.
+static int attn_static_scratch(void** out) {
+  int dev = -1;
+  TN_CHECK_CUDA(cudaGetDevice(&dev));
+  TN_REQUIRE(dev >= 0 && dev < kMaxStaticDevices, TN_EUNSUPPORTED, "tn_attention_static: device %d", dev);
+  std::lock_guard<std::mutex> lk(g_attn_static_mu);
+  if (!g_attn_static_ptr[dev]) {
+    void* p = nullptr;
+    TN_CHECK_CUDA(cudaGetSymbolAddress(&p, g_attn_static_scratch));
+    g_attn_static_ptr[dev] = p;
+  }
+  *out = g_attn_static_ptr[dev];
+  return TN_OK;
+}
+}  // namespace tn
+
+extern "C" int tn_attention_static(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
+                                   int32_t head_dim, int32_t max_ctx, const float* d_q, const float* d_k,
+                                   const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
+                                   void* stream) {
+  clear_error();
+  TN_REQUIRE(n_rows >= 0 && n_slots > 0 && n_heads > 0 && n_kv_heads > 0 && max_ctx > 0, TN_EINVAL,
+             "tn_attention_static: bad sizes");
+  TN_REQUIRE(d_q && d_k && d_v && d_slot && d_len && d_out, TN_EINVAL, "tn_attention_static: null pointer");
+  TN_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128, TN_EUNSUPPORTED,
+             "tn_attention_static: head_dim %d unsupported", head_dim);
+  if (n_rows == 0) return TN_OK;
+  const size_t need = attn_total_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx);
+  TN_REQUIRE(need <= TN_ATTENTION_STATIC_SCRATCH_BYTES, TN_ECAPACITY,
+             "tn_attention_static: %d rows x %d heads need %zu bytes of scratch, above the fixed %u; "
+             "use tn_attention with caller scratch",
+             n_rows, n_heads, need, (unsigned)TN_ATTENTION_STATIC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  const int rc = attn_static_scratch(&scratch);
+  if (rc) return rc;
+  cudaStream_t s = (cudaStream_t)stream;
+  RowInfo* rows = (RowInfo*)scratch;
+  void* part = (char*)scratch + (((size_t)n_rows * sizeof(RowInfo) + 255) & ~(size_t)255);
+  k_rows_from_slots<<<(n_rows + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows);
+  TN_CHECK_LAUNCH();
+  const size_t kvh_stride = (size_t)max_ctx * head_dim;
+  return attention(d_q, n_heads * head_dim, d_k, d_v, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows, n_heads,
+                   n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out, n_heads * head_dim, part,
+                   s);
 }
 
 extern "C" int tn_hop_encode(const float* d_in, uint16_t* d_out, uint64_t n, void* stream) {

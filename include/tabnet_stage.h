@@ -211,6 +211,33 @@ int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_
                  const int32_t* d_slot, const int32_t* d_len, float* d_out, void* d_scratch,
                  uint64_t scratch_bytes, void* stream);
 
+/* tn_attention without a scratch argument, for callers that cannot allocate
+ * device memory.  This entry point has no counterpart in the reference.
+ *
+ * Some callers of this library cannot call cudaMalloc: a host whose memory
+ * manager owns the whole device and forbids allocations behind its back (a
+ * framework caching allocator, or a Node-API addon that only receives buffers
+ * from JavaScript), a C binding layer that has no allocator of its own, or a
+ * serving loop that must never pay the device-wide synchronisation that
+ * cudaMalloc/cudaFree can imply.  This variant takes the same inputs and
+ * output as tn_attention but keeps its row table and split partials in a
+ * fixed array compiled into the library: TN_ATTENTION_STATIC_SCRATCH_BYTES
+ * (8 MiB) of device memory, held on every GPU that loads the library until the
+ * process exits.  Calls whose tn_attention_scratch_bytes() exceeds that size
+ * fail with TN_ECAPACITY and launch nothing; nothing here allocates.
+ *
+ * It runs on the calling thread's current device.  Its first call on a device
+ * looks up that device's address of the array (once per device), so make that
+ * first call before any stream capture.  All calls share the one array and
+ * leave their contents in it; every call writes all it reads, so nothing needs
+ * clearing, but calls whose work overlaps on the GPU (other streams, other
+ * threads) race on the array and must be serialised by the caller. */
+#define TN_ATTENTION_STATIC_SCRATCH_BYTES (8u << 20)
+int tn_attention_static(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
+                        int32_t head_dim, int32_t max_ctx, const float* d_q, const float* d_k,
+                        const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
+                        void* stream);
+
 /* Activation hop codec, bit-exact with f32ToF16 / f16ToF32
  * (web/inference-worker.js:68-88): round half up, subnormal mantissa masked. */
 int tn_hop_encode(const float* d_in, uint16_t* d_out, uint64_t n, void* stream);
