@@ -20,6 +20,7 @@ QUANT = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 3}
 TN_HOP_LAST, TN_HOP_ALL = 0, 1
 TN_FLAG_NO_GRAPHS = 1
 TN_FLAG_PROFILE = 2
+TN_FLAG_NO_FUSED_DECODE = 4
 PROF_CLASSES = ["matvec_qkv", "matvec_o", "matvec_gate_up", "matvec_down", "matvec_lm_head", "attention",
                 "rmsnorm", "rope_kv", "other"]
 TN_TAG_EMBED, TN_TAG_NORM, TN_TAG_LM_HEAD = 1, 2, 3

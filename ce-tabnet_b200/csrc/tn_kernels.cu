@@ -55,6 +55,17 @@ __device__ __forceinline__ float packed_elem(const uint8_t* src, int quant, uint
   return (float)(nib - 8) * d;
 }
 
+// Destination row of source row r: dst_off + r * dst_stride, or, for a
+// negative stride, the RoPE pair-interleaved order of heads of -dst_stride
+// rows: within a head, rows i and i + hd/2 (a rotation pair of
+// web/inference-worker.js:535-537) land next to each other at 2i and 2i + 1,
+// so one epilogue thread sees both halves of every pair.
+__host__ __device__ __forceinline__ uint64_t dst_row(uint64_t r, int dst_off, int dst_stride) {
+  if (dst_stride > 0) return (uint64_t)dst_off + r * (uint64_t)dst_stride;
+  const uint64_t hd = (uint64_t)(-dst_stride), half = hd / 2, h = r / hd, j = r % hd;
+  return (uint64_t)dst_off + h * hd + (j < half ? 2 * j : 2 * (j - half) + 1);
+}
+
 // block-aligned q4_0 / q8_0 source: one thread per (row, block)
 __global__ void k_repack_q(const uint8_t* __restrict__ src, int quant, int src_rows, int nb,
                            int dst_off, int dst_stride, uint8_t* __restrict__ data,
@@ -65,7 +76,7 @@ __global__ void k_repack_q(const uint8_t* __restrict__ src, int quant, int src_r
        k += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t r = k / nb, b = k % nb;
     const uint8_t* blk = src + k * bb;
-    const uint64_t dr = (uint64_t)dst_off + r * (uint64_t)dst_stride;
+    const uint64_t dr = dst_row(r, dst_off, dst_stride);
     uint8_t* dq = data + (dr * nb + b) * qb;
     for (int j = 0; j < qb; j++) dq[j] = blk[2 + j];
     scales[((dr >> 3) * nb + b) * 8 + (dr & 7)] = (uint16_t)(blk[0] | (blk[1] << 8));
@@ -83,7 +94,7 @@ __global__ void k_repack_q16(const uint16_t* __restrict__ src, int src_rows, int
        k += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t r = k / nb, b = k % nb;
     const uint16_t* blk = src + k * BW;
-    const uint64_t dr = (uint64_t)dst_off + r * (uint64_t)dst_stride;
+    const uint64_t dr = dst_row(r, dst_off, dst_stride);
     uint32_t w[QB / 4];
 #pragma unroll
     for (int j = 0; j < QB / 4; j++) w[j] = (uint32_t)blk[1 + 2 * j] | ((uint32_t)blk[2 + 2 * j] << 16);
@@ -102,7 +113,7 @@ __global__ void k_repack_plain(const uint8_t* __restrict__ src, int quant, int s
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < total;
        k += (uint64_t)gridDim.x * blockDim.x) {
     const uint64_t r = k / cols, c = k % cols;
-    const uint64_t dr = (uint64_t)dst_off + r * (uint64_t)dst_stride;
+    const uint64_t dr = dst_row(r, dst_off, dst_stride);
     if (kind == MK_F16) {
       const uint8_t* p = src + k * 2;
       ((uint16_t*)data)[dr * cols_pad + c] = (uint16_t)(p[0] | (p[1] << 8));
@@ -113,6 +124,7 @@ __global__ void k_repack_plain(const uint8_t* __restrict__ src, int quant, int s
 }
 
 static void mv_prepare(Matrix* m);
+static void mvd_prepare(Matrix* m);
 
 int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
   TN_REQUIRE(rows > 0 && cols > 0, TN_EINVAL, "matrix: bad shape %d x %d", rows, cols);
@@ -139,12 +151,15 @@ int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
   m->bytes = dbytes + sbytes;
   num_sms();
   mv_prepare(m);
+  mvd_prepare(m);
   return TN_OK;
 }
 
 int matrix_repack(Matrix* m, const uint8_t* d_src, int src_quant, int src_rows, int dst_off,
                   int dst_stride, cudaStream_t s) {
-  TN_REQUIRE(dst_off + (int64_t)(src_rows - 1) * dst_stride < m->rows, TN_EINVAL,
+  TN_REQUIRE(dst_stride != 0 && (dst_stride > 0 || src_rows % (-dst_stride) == 0), TN_EINVAL,
+             "matrix_repack: bad row stride %d", dst_stride);
+  TN_REQUIRE(dst_off + (int64_t)(src_rows - 1) * (dst_stride > 0 ? dst_stride : 1) < m->rows, TN_EINVAL,
              "matrix_repack: rows out of range");
   const int grid = std::min(148 * 32, (int)std::max<int64_t>(1, ((int64_t)src_rows * m->nb + 255) / 256));
   const bool even = (reinterpret_cast<uintptr_t>(d_src) & 1) == 0;
@@ -482,6 +497,387 @@ int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, i
   }
 }
 
+// ================================================================ decode matvec
+// Programmatic dependent launch: a kernel lets its successor start as soon as
+// every CTA of it is running, and the successor streams weights (which no
+// kernel writes) before it waits for its predecessor's results.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// compile-time loop: f(std::integral_constant<int, I>) for I in [B, E)
+template <int B, int E>
+struct Unroll {
+  template <class F>
+  __device__ __forceinline__ static void run(F&& f) {
+    if constexpr (B < E) {
+      f(std::integral_constant<int, B>{});
+      Unroll<B + 1, E>::run(f);
+    }
+  }
+};
+
+struct MvdArgs {
+  const uint8_t* data;
+  const uint16_t* scales;
+  int rows, rows_pad, cols, nb, T;
+  const float* x;
+  int ldx;
+  float* y;
+  int ldy, mode;
+  MvFuse f;
+};
+
+// A unit is RG rows x NBT block columns of one 8-row group, sized so one
+// buffer of its weights is 32 registers; two buffers alternate (the next
+// unit's loads are in flight while the current one is reduced).
+template <int KIND, int NBT>
+struct MvdCfg {
+  static constexpr int BB = kind_block_bytes(KIND), W = BB / 4;
+  static constexpr int RG0 = 32 / (W * NBT);
+  static constexpr int RG = RG0 < 1 ? 1 : (RG0 > 8 ? 8 : RG0);
+  static constexpr int SPG = 8 / RG;             // units per group
+  static constexpr int UPI = SPG < 2 ? 2 : SPG;  // units per unrolled iteration (even)
+  static constexpr int GPI = UPI / SPG;          // groups per iteration
+  static constexpr int ND = (RG + 1) / 2;        // 32-bit words of fp16 scales per unit column
+  static constexpr int CHG = 8;                  // groups per reduction chunk
+};
+
+template <int KIND, int NBT>
+struct MvdUnit {
+  using C = MvdCfg<KIND, NBT>;
+  uint32_t w[C::RG][NBT][C::W];
+  uint32_t d[NBT][C::ND];
+};
+
+template <int KIND, int NBT>
+__device__ __forceinline__ void mvd_load(const MvdArgs& a, int g, int rs, int tid, int NT, MvdUnit<KIND, NBT>& u) {
+  using C = MvdCfg<KIND, NBT>;
+#pragma unroll
+  for (int j = 0; j < NBT; j++) {
+    const int b = tid + j * NT;
+    if (b < a.nb) {
+#pragma unroll
+      for (int i = 0; i < C::RG; i++) {
+        const uint8_t* p = a.data + ((size_t)(g * 8 + rs + i) * a.nb + b) * C::BB;
+#pragma unroll
+        for (int v = 0; v < C::W / 4; v++) {
+          const uint4 q = ld_stream(p + 16 * v);
+          u.w[i][j][4 * v] = q.x;
+          u.w[i][j][4 * v + 1] = q.y;
+          u.w[i][j][4 * v + 2] = q.z;
+          u.w[i][j][4 * v + 3] = q.w;
+        }
+      }
+      const uint16_t* ps = a.scales + ((size_t)g * a.nb + b) * 8 + rs;
+      if constexpr (C::RG == 8) {
+        const uint4 q = *reinterpret_cast<const uint4*>(ps);
+        u.d[j][0] = q.x;
+        u.d[j][1] = q.y;
+        u.d[j][2] = q.z;
+        u.d[j][3] = q.w;
+      } else if constexpr (C::RG == 4) {
+        const uint2 q = *reinterpret_cast<const uint2*>(ps);
+        u.d[j][0] = q.x;
+        u.d[j][1] = q.y;
+      } else if constexpr (C::RG == 2) {
+        u.d[j][0] = *reinterpret_cast<const uint32_t*>(ps);
+      } else {
+        u.d[j][0] = ps[0];
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < C::ND; k++) u.d[j][k] = 0u;
+    }
+  }
+}
+
+// partial dot products of one unit into acc[RS + i][tt]
+template <int KIND, int TT, int NBT, int RS>
+__device__ __forceinline__ void mvd_compute(const MvdUnit<KIND, NBT>& u, const float (&xr)[TT][NBT][32],
+                                            const float (&xs)[TT][NBT], float (&acc)[8][TT]) {
+  using C = MvdCfg<KIND, NBT>;
+#pragma unroll
+  for (int j = 0; j < NBT; j++) {
+#pragma unroll
+    for (int i = 0; i < C::RG; i++) {
+      const uint32_t dd = u.d[j][i >> 1];
+      const float di = __half2float(__ushort_as_half((unsigned short)((i & 1) ? (dd >> 16) : (dd & 0xffffu))));
+#pragma unroll
+      for (int tt = 0; tt < TT; tt++) {
+        float s0 = 0.f, s1 = 0.f;  // two chains for ILP
+        if constexpr (KIND == MK_Q4) {
+#pragma unroll
+          for (int k = 0; k < 4; k++) {
+            const uint32_t lo = u.w[i][j][k] & 0x0F0F0F0Fu, hi = (u.w[i][j][k] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+              s0 = fmaf(q4_f(lo, m), xr[tt][j][8 * k + 2 * m], s0);
+              s1 = fmaf(q4_f(hi, m), xr[tt][j][8 * k + 2 * m + 1], s1);
+            }
+          }
+          acc[RS + i][tt] = fmaf(di, fmaf(256.f, s0 + s1, xs[tt][j]), acc[RS + i][tt]);
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; k++) {
+            const uint32_t bq = u.w[i][j][k] ^ 0x80808080u;
+            s0 = fmaf(q8_f(bq, 0) - 8388736.0f, xr[tt][j][4 * k], s0);
+            s1 = fmaf(q8_f(bq, 1) - 8388736.0f, xr[tt][j][4 * k + 1], s1);
+            s0 = fmaf(q8_f(bq, 2) - 8388736.0f, xr[tt][j][4 * k + 2], s0);
+            s1 = fmaf(q8_f(bq, 3) - 8388736.0f, xr[tt][j][4 * k + 3], s1);
+          }
+          acc[RS + i][tt] = fmaf(di, s0 + s1, acc[RS + i][tt]);
+        }
+      }
+    }
+  }
+}
+
+// epilogue of rows [row0, row0 + nrows), whose per-warp partials are in red
+template <int TT>
+__device__ __forceinline__ void mvd_epilogue(const MvdArgs& a, const float* red, int red_stride, int nw, int row0,
+                                             int nrows, int tid, int NT) {
+  for (int e = tid; e < nrows * TT; e += NT) {
+    const int r = e / TT, tt = e % TT, row = row0 + r;
+    if (row >= a.rows || tt >= a.T) continue;
+    const bool pair_second = (a.mode == EPI_SWIGLU || (a.mode == EPI_QKV_ROPE && row < a.f.q_dim + a.f.kv_dim));
+    if (pair_second && (row & 1)) continue;  // handled with its even partner
+    float s = 0.f, s2 = 0.f;
+    for (int w2 = 0; w2 < nw; w2++) {
+      s += red[w2 * red_stride + e];
+      if (pair_second) s2 += red[w2 * red_stride + e + TT];
+    }
+    if (a.mode == EPI_STORE || a.mode == EPI_RESID) {
+      float* py = a.y + (size_t)tt * a.ldy + row;
+      *py = a.mode == EPI_RESID ? *py + s : s;
+    } else if (a.mode == EPI_SWIGLU) {
+      a.y[(size_t)tt * a.ldy + (row >> 1)] = (s / (1.0f + expf(-s))) * s2;
+    } else {  // EPI_QKV_ROPE (web/inference-worker.js:528-540 and the KV push of :554)
+      const MvFuse& f = a.f;
+      const RowInfo ri = f.rinfo[tt];
+      if (row < f.q_dim + f.kv_dim) {
+        const bool isq = row < f.q_dim;
+        const int rr = isq ? row : row - f.q_dim, head = rr / f.hd, i = (rr % f.hd) >> 1, half = f.hd >> 1;
+        const double2 c = f.cs[(size_t)tt * half + i];
+        const double av = s, bv = s2;
+        const float o0 = (float)__dsub_rn(__dmul_rn(av, c.x), __dmul_rn(bv, c.y));
+        const float o1 = (float)__dadd_rn(__dmul_rn(av, c.y), __dmul_rn(bv, c.x));
+        float* dst = isq ? f.q_out + (size_t)tt * f.q_dim + head * f.hd
+                         : f.kc + ri.slot * f.slot_stride + head * f.kvh_stride + (size_t)ri.kv_idx * f.hd;
+        dst[i] = o0;
+        dst[half + i] = o1;
+      } else {
+        const int dv = row - f.q_dim - f.kv_dim;
+        f.vc[ri.slot * f.slot_stride + (dv / f.hd) * f.kvh_stride + (size_t)ri.kv_idx * f.hd + dv % f.hd] = s;
+      }
+    }
+  }
+}
+
+// CUDA-core dequant-matvec for decode (1-2 tokens).  Each thread owns NBT
+// 32-wide block columns and keeps x for them in registers; a CTA streams a
+// contiguous range of 8-row groups.  Warps never wait on each other inside a
+// 64-row chunk: each warp reduce-scatters its partial sums of a group with
+// shuffles into shared memory, and one barrier per chunk precedes the
+// cross-warp sum and the fused epilogue.
+template <int KIND, int TT, int NBT>
+__global__ void __launch_bounds__(256) k_mvd(const MvdArgs a) {
+  using C = MvdCfg<KIND, NBT>;
+  constexpr int SPG = C::SPG, UPI = C::UPI, GPI = C::GPI, CHG = C::CHG, RG = C::RG;
+  constexpr int NV = 8 * TT;
+  __shared__ float red[2][16][CHG * NV];
+  __shared__ double nsum[16][TT];
+  pdl_launch_dependents();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, NT = blockDim.x, nw = NT >> 5;
+  const int G = a.rows_pad >> 3;
+  const int g0 = (int)((int64_t)G * blockIdx.x / gridDim.x);
+  const int ng = (int)((int64_t)G * (blockIdx.x + 1) / gridDim.x) - g0;
+
+  MvdUnit<KIND, NBT> ub[2];
+  if (ng > 0) mvd_load<KIND, NBT>(a, g0, 0, tid, NT, ub[0]);
+
+  // x, produced by the predecessor kernel
+  pdl_wait();
+  float xr[TT][NBT][32];
+  float xs[TT][NBT];
+  double ss[TT];
+#pragma unroll
+  for (int tt = 0; tt < TT; tt++) {
+    ss[tt] = 0.0;
+    const bool tok = tt < a.T;
+    const float* xrow = a.x + (size_t)(a.f.rowsel && tok ? a.f.rowsel[tt] : tt) * a.ldx;
+#pragma unroll
+    for (int j = 0; j < NBT; j++) {
+      const int b = tid + j * NT;
+      const bool ok = tok && b < a.nb;
+#pragma unroll
+      for (int e = 0; e < 32; e += 4) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (ok) v = *reinterpret_cast<const float4*>(xrow + b * 32 + e);
+        xr[tt][j][e] = v.x;
+        xr[tt][j][e + 1] = v.y;
+        xr[tt][j][e + 2] = v.z;
+        xr[tt][j][e + 3] = v.w;
+        ss[tt] += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+      }
+    }
+  }
+  if (a.f.norm_w) {
+    // RMSNorm (web/inference-worker.js:516-522): the CTA's threads hold the whole row
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++) {
+      double v = ss[tt];
+      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0) nsum[warp][tt] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++) {
+      double tot = 0.0;
+      for (int w2 = 0; w2 < nw; w2++) tot += nsum[w2][tt];
+      const double inv = 1.0 / sqrt(tot / a.cols + 1e-5);
+#pragma unroll
+      for (int j = 0; j < NBT; j++) {
+        const int b = tid + j * NT;
+        if (b < a.nb) {
+#pragma unroll
+          for (int e = 0; e < 32; e++)
+            xr[tt][j][e] = (float)__dmul_rn(__dmul_rn((double)xr[tt][j][e], inv), (double)a.f.norm_w[b * 32 + e]);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int tt = 0; tt < TT; tt++)
+#pragma unroll
+    for (int j = 0; j < NBT; j++) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < 32; e++) s += xr[tt][j][e];
+      xs[tt][j] = KIND == MK_Q4 ? -136.f * s : s;
+    }
+
+  float acc[8][TT];
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++) acc[i][tt] = 0.f;
+  int rb = 0;
+  for (int gi = 0; gi < ng; gi += GPI) {
+    Unroll<0, UPI>::run([&](auto uc) {
+      constexpr int u = decltype(uc)::value;
+      const int gg = gi + u / SPG;
+      {  // prefetch the next unit into the other buffer
+        constexpr int un = u + 1;
+        const int ggn = gi + un / SPG;
+        if (ggn < ng) mvd_load<KIND, NBT>(a, g0 + ggn, (un % SPG) * RG, tid, NT, ub[un & 1]);
+      }
+      if (gg < ng) mvd_compute<KIND, TT, NBT, (u % SPG) * RG>(ub[u & 1], xr, xs, acc);
+      if constexpr (u % SPG == SPG - 1) {
+        if (gg < ng) {
+          float v[NV];
+#pragma unroll
+          for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int tt = 0; tt < TT; tt++) {
+              v[i * TT + tt] = acc[i][tt];
+              acc[i][tt] = 0.f;
+            }
+          const float r = warp_reduce_scatter<NV>(v, lane);
+          constexpr int SH = NV == 8 ? 2 : 1;
+          const int cg = gg % CHG;
+          if ((lane & ((1 << SH) - 1)) == 0) red[rb][warp][cg * NV + (lane >> SH)] = r;
+          if (cg == CHG - 1 || gg == ng - 1) {
+            __syncthreads();
+            mvd_epilogue<TT>(a, &red[rb][0][0], CHG * NV, nw, (g0 + gg - cg) * 8, (cg + 1) * 8, tid, NT);
+            rb ^= 1;
+          }
+        }
+      }
+    });
+  }
+}
+
+template <int KIND, int TT, int NBT>
+static int mvd_occupancy(const Matrix& m) {
+  const int NT = ((m.nb + NBT - 1) / NBT + 31) & ~31;
+  int o = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_mvd<KIND, TT, NBT>, NT, 0) != cudaSuccess || o <= 0)
+    o = 1;
+  return o;
+}
+
+// block columns per thread of the decode matvec: CTAs of at most 256 threads
+static int mvd_nbt(int nb) { return nb <= 256 ? 1 : (nb <= 512 ? 2 : 4); }
+
+template <int KIND>
+static void mvd_prepare_kind(Matrix* m) {
+  switch (mvd_nbt(m->nb)) {
+    case 1: m->occ_dec[0] = mvd_occupancy<KIND, 1, 1>(*m); m->occ_dec[1] = mvd_occupancy<KIND, 2, 1>(*m); break;
+    case 2: m->occ_dec[0] = mvd_occupancy<KIND, 1, 2>(*m); m->occ_dec[1] = mvd_occupancy<KIND, 2, 2>(*m); break;
+    default: m->occ_dec[0] = mvd_occupancy<KIND, 1, 4>(*m); break;
+  }
+}
+
+static void mvd_prepare(Matrix* m) {
+  if (m->nb > 1024) return;
+  if (m->kind == MK_Q4) mvd_prepare_kind<MK_Q4>(m);
+  else if (m->kind == MK_Q8) mvd_prepare_kind<MK_Q8>(m);
+}
+
+template <int KIND, int TT, int NBT>
+static int launch_mvd(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
+                      const MvFuse& f, cudaStream_t s) {
+  const int NT = ((m.nb + NBT - 1) / NBT + 31) & ~31;
+  const int occ = m.occ_dec[TT - 1] > 0 ? m.occ_dec[TT - 1] : 1;
+  const int grid = std::max(1, std::min(m.rows_pad / 8, occ * num_sms()));
+  const MvdArgs a{m.data, m.scales, m.rows, m.rows_pad, m.cols, m.nb, T, x, ldx, y, ldy, mode, f};
+  TN_CHECK_CUDA(launch_pdl(k_mvd<KIND, TT, NBT>, dim3(grid), dim3(NT), s, a));
+  return TN_OK;
+}
+
+bool matvec_dec_ok(const Matrix& m, int T) {
+  if (!(m.kind == MK_Q4 || m.kind == MK_Q8) || m.nb > 1024 || T < 1) return false;
+  return T <= (mvd_nbt(m.nb) <= 2 ? 2 : 1);
+}
+
+template <int KIND>
+static int matvec_dec_kind(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
+                           const MvFuse& f, cudaStream_t s) {
+  switch (mvd_nbt(m.nb)) {
+    case 1: return T == 1 ? launch_mvd<KIND, 1, 1>(m, T, x, ldx, y, ldy, mode, f, s)
+                          : launch_mvd<KIND, 2, 1>(m, T, x, ldx, y, ldy, mode, f, s);
+    case 2: return T == 1 ? launch_mvd<KIND, 1, 2>(m, T, x, ldx, y, ldy, mode, f, s)
+                          : launch_mvd<KIND, 2, 2>(m, T, x, ldx, y, ldy, mode, f, s);
+    default: return launch_mvd<KIND, 1, 4>(m, T, x, ldx, y, ldy, mode, f, s);
+  }
+}
+
+int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
+               cudaStream_t s) {
+  TN_REQUIRE(matvec_dec_ok(m, T), TN_EUNSUPPORTED, "matvec_dec: %d tokens of kind %d, %d columns", T, m.kind,
+             m.cols);
+  TN_REQUIRE((ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0, TN_EINVAL,
+             "matvec_dec: x rows must be 16-byte aligned");
+  TN_REQUIRE(mode != EPI_SWIGLU || (m.rows & 1) == 0, TN_EINVAL, "swiglu needs paired rows");
+  if (m.kind == MK_Q4) return matvec_dec_kind<MK_Q4>(m, T, x, ldx, y, ldy, mode, f, s);
+  return matvec_dec_kind<MK_Q8>(m, T, x, ldx, y, ldy, mode, f, s);
+}
+
 // ================================================================ rmsnorm
 // web/inference-worker.js:516-522, sum of squares and the scale in double.
 __global__ void k_rmsnorm(const float* __restrict__ h, int ldh, const int* __restrict__ rowsel,
@@ -577,8 +973,9 @@ __global__ void k_rope_kv(const float* __restrict__ qkv, int ldqkv, const RowInf
       const bool isq = k < nq;
       const int kk = isq ? k : k - nq;
       const int head = kk / half, i = kk % half;
+      // q and k rows are stored pair-interleaved (dst_row): pair i at 2i, 2i + 1
       const float* base = src + (isq ? 0 : qDim) + head * hd;
-      const double a = base[i], b = base[half + i];
+      const double a = base[2 * i], b = base[2 * i + 1];
       const double2 r = c[i];
       const float o0 = (float)__dsub_rn(__dmul_rn(a, r.x), __dmul_rn(b, r.y));
       const float o1 = (float)__dadd_rn(__dmul_rn(a, r.y), __dmul_rn(b, r.x));

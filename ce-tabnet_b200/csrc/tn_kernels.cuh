@@ -22,7 +22,8 @@ struct Matrix {
   uint8_t* data = nullptr;
   uint16_t* scales = nullptr;
   size_t bytes = 0;
-  int occ[2] = {0, 0};  // resident CTAs per SM of the matvec launch shapes (1 and 2 tokens per tile)
+  int occ[2] = {0, 0};      // resident CTAs per SM of the matvec launch shapes (1 and 2 tokens per tile)
+  int occ_dec[2] = {0, 0};  // the same for the decode matvec (1 and 2 tokens)
 };
 
 // bytes per 32-element block of the data plane
@@ -38,7 +39,7 @@ int matrix_repack(Matrix* m, const uint8_t* d_src, int src_quant, int src_rows, 
 void matrix_free(Matrix* m);
 int matrix_dequant(const Matrix& m, float* out, cudaStream_t s);
 
-enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
+enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV_ROPE = 3 };
 // y = W x for T tokens.  STORE: y[t*ldy + r] = v.  RESID: y[t*ldy + r] += v.
 // SWIGLU: rows (2i, 2i+1) hold (gate_i, up_i); y[t*ldy + i] = silu(gate) * up.
 int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
@@ -51,6 +52,34 @@ struct RowInfo {
 
 int rmsnorm(const float* h, int ldh, const int* rowsel, const float* w, float* out, int ldo, int H,
             int T, cudaStream_t s);
+
+// Fusions of the decode matvec (matvec_dec):
+//   prologue: x rows are the raw hidden state (row t at rowsel[t] if given),
+//             normalised in the kernel with RMSNorm weights norm_w;
+//   EPI_QKV_ROPE: rows [0, q_dim) and [q_dim, q_dim + kv_dim) hold q and k in
+//             RoPE pair-interleaved order; the epilogue rotates each pair
+//             (cos/sin table cs) and writes q_out and the K cache, and writes
+//             the V rows to the V cache, at each token's RowInfo slot / index.
+struct MvFuse {
+  const float* norm_w = nullptr;
+  const int* rowsel = nullptr;
+  const RowInfo* rinfo = nullptr;
+  const double2* cs = nullptr;
+  float* q_out = nullptr;
+  float* kc = nullptr;
+  float* vc = nullptr;
+  size_t slot_stride = 0, kvh_stride = 0;
+  int q_dim = 0, kv_dim = 0, hd = 0;
+};
+// the decode matvec handles up to 2 tokens of q4_0 / q8_0 matrices
+bool matvec_dec_ok(const Matrix& m, int T);
+int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
+               cudaStream_t s);
+// split-K decode attention with the split merge done by the last CTA of each
+// (row, KV head); counters: T * nKV ints, zero between calls
+int attention_dec(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
+                  size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, int n_splits,
+                  float* out, int ldo, void* scratch, int* counters, cudaStream_t s);
 int embed_rows(const Matrix& emb, const int* ids, int T, float* out, int ldo, int* d_err,
                cudaStream_t s);
 int rope_table(const RowInfo* rows, const double* freq, int half, int T, double2* cs, cudaStream_t s);

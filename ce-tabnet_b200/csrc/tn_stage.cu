@@ -197,8 +197,9 @@ static int load_layer(tn_stage* st, const tn_stage_spec* sp, int li, uint8_t* st
   const int q = lw.quant;
   // wq | wk | wv fused into one [qDim + 2 kvDim, H] matrix
   if ((rc = matrix_alloc(&W.qkv, q, st->qDim + 2 * st->kvDim, st->H, st->stream))) return rc;
-  if ((rc = matrix_repack(&W.qkv, src + L.off[1], q, st->qDim, 0, 1, st->stream))) return rc;
-  if ((rc = matrix_repack(&W.qkv, src + L.off[2], q, st->kvDim, st->qDim, 1, st->stream))) return rc;
+  // (q and k rows pair-interleaved per head for the RoPE epilogue: stride -hd)
+  if ((rc = matrix_repack(&W.qkv, src + L.off[1], q, st->qDim, 0, -st->hd, st->stream))) return rc;
+  if ((rc = matrix_repack(&W.qkv, src + L.off[2], q, st->kvDim, st->qDim, -st->hd, st->stream))) return rc;
   if ((rc = matrix_repack(&W.qkv, src + L.off[3], q, st->kvDim, st->qDim + st->kvDim, 1, st->stream)))
     return rc;
   if ((rc = matrix_alloc(&W.o, q, st->H, st->qDim, st->stream))) return rc;
@@ -443,22 +444,63 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
     LayerW& L = st->layers[l];
     float* kc = st->kc + (size_t)l * st->layer_stride;
     float* vc = st->vc + (size_t)l * st->layer_stride;
-    TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
-    TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, s));
-    TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1,
-                   rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->slot_stride, st->kvh_stride, st->nH,
-                           st->nKV, st->hd, T, s));
+    // decode-sized steps use the fused decode matvec (RMSNorm prologue,
+    // RoPE + KV epilogue, programmatic dependent launches); other steps and
+    // matrix formats it does not cover run the separate kernels
+    const bool fuse = !(st->flags & TN_FLAG_NO_FUSED_DECODE);
+    if (fuse && matvec_dec_ok(L.qkv, T)) {
+      MvFuse f;
+      f.norm_w = L.attn_norm;
+      f.rinfo = rows;
+      f.cs = st->cs;
+      f.q_out = st->q;
+      f.kc = kc;
+      f.vc = vc;
+      f.slot_stride = st->slot_stride;
+      f.kvh_stride = st->kvh_stride;
+      f.q_dim = st->qDim;
+      f.kv_dim = st->kvDim;
+      f.hd = st->hd;
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec_dec(L.qkv, T, st->h, H, st->qkv, ldqkv, EPI_QKV_ROPE, f, s));
+    } else {
+      TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, s));
+      TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1,
+                     rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->slot_stride, st->kvh_stride, st->nH,
+                             st->nKV, st->hd, T, s));
+    }
     TN_STEP_LAUNCH(TN_PROF_ATTENTION, 2,
                    attention(st->q, st->qDim, kc, vc, st->slot_stride, st->kvh_stride, rows, T, st->nH, st->nKV,
                              st->hd, ns, st->att, st->qDim, st->attn_scratch, s));
-    TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, s));
-    TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.ffn_norm, st->xn, H, H, T, s));
-    TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, s));
-    TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, s));
+    if (fuse && matvec_dec_ok(L.o, T))
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), s));
+    else
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, s));
+    if (fuse && matvec_dec_ok(L.gu, T)) {
+      MvFuse f;
+      f.norm_w = L.ffn_norm;
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec_dec(L.gu, T, st->h, H, st->act, st->F, EPI_SWIGLU, f, s));
+    } else {
+      TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.ffn_norm, st->xn, H, H, T, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, s));
+    }
+    if (fuse && matvec_dec_ok(L.down, T))
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec_dec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, MvFuse(), s));
+    else
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, s));
   }
   if (st->last) {
-    TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, outrows, st->final_norm, st->xn, H, H, n_out, s));
-    TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1, matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, s));
+    if (!(st->flags & TN_FLAG_NO_FUSED_DECODE) && matvec_dec_ok(st->lm_head, n_out)) {
+      MvFuse f;
+      f.norm_w = st->final_norm;
+      f.rowsel = outrows;
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1,
+                     matvec_dec(st->lm_head, n_out, st->h, H, st->logits, st->V, EPI_STORE, f, s));
+    } else {
+      TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, outrows, st->final_norm, st->xn, H, H, n_out, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1,
+                     matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, s));
+    }
     TN_STEP_LAUNCH(TN_PROF_OTHER, 1, sample_rows(st->logits, n_out, st->V, params, st->tok_out, s));
   } else {
     TN_STEP_LAUNCH(TN_PROF_OTHER, 1, hop_encode_rows(st->h, H, outrows, n_out, H, st->hid_out, s));

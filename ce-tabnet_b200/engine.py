@@ -148,7 +148,8 @@ def initStage(spec: dict) -> StageCtx:
     s.max_seqs = int(opts.get("max_seqs", 16))
     s.max_tokens_per_step = int(opts.get("max_tokens_per_step", 512))
     s.flags = (_lib.TN_FLAG_NO_GRAPHS if opts.get("no_graphs") else 0) | \
-        (_lib.TN_FLAG_PROFILE if opts.get("profile") else 0)
+        (_lib.TN_FLAG_PROFILE if opts.get("profile") else 0) | \
+        (_lib.TN_FLAG_NO_FUSED_DECODE if opts.get("fused_decode") is False else 0)
     handle = C.c_void_p()
     _lib.check(lib.tn_stage_init(C.byref(s), C.byref(handle)))
     return StageCtx(handle=handle, dims=dict(dims), layers=(lo, hi), is_first=bool(spec.get("is_first")),

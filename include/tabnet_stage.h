@@ -51,6 +51,7 @@ enum { TN_HOP_LAST = 0, TN_HOP_ALL = 1 };
 /* spec flags */
 #define TN_FLAG_NO_GRAPHS (1u << 0) /* never capture decode steps in CUDA graphs */
 #define TN_FLAG_PROFILE (1u << 1)   /* time every kernel launch with CUDA events (tn_stage_profile) */
+#define TN_FLAG_NO_FUSED_DECODE (1u << 2) /* decode steps use the separate norm / matvec / RoPE kernels */
 
 /* One layer's packed buffer, tensors in web/inference-worker.js:142-159 order:
  * attn_norm(f16) wq wk wv wo ffn_norm(f16) w_gate w_up w_down. */

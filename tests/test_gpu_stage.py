@@ -35,9 +35,10 @@ def _stage(pkg, m, w, lo, hi, first, last, **opts):
                           "is_last": last, "weights": sub, "opts": o}), sub
 
 
-def test_tiny_single_stage_greedy_64(pkg, ref, tiny):
+@pytest.mark.parametrize("fused", [True, False])
+def test_tiny_single_stage_greedy_64(pkg, ref, tiny, fused):
     m, w = tiny
-    ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, fused_decode=fused)
     oracle = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
     prompt = pkg.pack.synth_prompt(m, 32)
     got = pkg.forward(ctx, {"seq_id": "a", "token_pos": 0, "token_ids": prompt, "temperature": 0})["token_id"]
@@ -103,11 +104,12 @@ def test_tiny_two_stages_hop_all(pkg, ref, tiny):
     pkg.freeStage(b)
 
 
-def test_batch_equals_individual(pkg, ref, tiny):
+@pytest.mark.parametrize("n_seqs", [2, 4])
+def test_batch_equals_individual(pkg, ref, tiny, n_seqs):
     m, w = tiny
     one, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
     many, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
-    prompts = [pkg.pack.synth_prompt(m, 5 + 3 * i, seed=10 + i) for i in range(4)]
+    prompts = [pkg.pack.synth_prompt(m, 5 + 3 * i, seed=10 + i) for i in range(n_seqs)]
     solo = [pkg.forward(one, {"seq_id": i, "token_pos": 0, "token_ids": p, "temperature": 0})["token_id"]
             for i, p in enumerate(prompts)]
     batch = pkg.forward_batch(many, [{"seq_id": i, "token_pos": 0, "token_ids": p, "temperature": 0}
@@ -116,7 +118,7 @@ def test_batch_equals_individual(pkg, ref, tiny):
     toks = list(solo)
     for step in range(12):
         reqs = [{"seq_id": i, "token_pos": len(prompts[i]) + step, "token_ids": [toks[i]], "temperature": 0}
-                for i in range(4)]
+                for i in range(n_seqs)]
         b = [r["token_id"] for r in pkg.forward_batch(many, reqs)]
         s = [pkg.forward(one, r)["token_id"] for r in reqs]
         assert b == s, step
@@ -239,5 +241,17 @@ def test_large_shape_slices(pkg, ref, name, lo, hi, first, last):
         want = [oracle.forward(1, p, hidden=hid[p])["hidden"] for p in range(n)]
     for p in range(n):
         assert maxrel(f16(got[p]), f16(want[p])) <= HIDDEN_TOL, p
+    # single-token decode steps (the fused decode kernels) continue the sequence
+    for step in range(3):
+        pos = n + step
+        if first:
+            tok = int((step * 7919 + 11) % m.vocab)
+            got = pkg.forward(ctx, {"seq_id": 0, "token_pos": pos, "token_ids": [tok]})["hidden"]
+            want = oracle.forward(1, pos, token_ids=[tok])["hidden"]
+        else:
+            h1 = (np.random.default_rng(pos).standard_normal(m.hidden_dim)).astype(np.float16).view(np.uint16)
+            got = pkg.forward(ctx, {"seq_id": 0, "token_pos": pos, "hidden": h1})["hidden"]
+            want = oracle.forward(1, pos, hidden=h1)["hidden"]
+        assert maxrel(f16(got), f16(want)) <= HIDDEN_TOL, ("decode", step)
     pkg.freeStage(ctx)
     oracle.free()
