@@ -39,6 +39,7 @@ using namespace tn;
 struct tn_matrix {
   Matrix m;
   int device = 0;
+  int* d_err = nullptr;  // bounded-wait flag of the decode kernel
 };
 
 extern "C" int tn_matrix_create(int32_t device, int32_t quant, int32_t rows, int32_t cols, const void* packed,
@@ -57,6 +58,10 @@ extern "C" int tn_matrix_create(int32_t device, int32_t quant, int32_t rows, int
   TN_REQUIRE(M, TN_ENOMEM, "out of host memory");
   M->device = device;
   int rc = matrix_alloc(&M->m, quant, rows, cols, 0);
+  if (!rc && (cudaMalloc(&M->d_err, sizeof(int)) != cudaSuccess || cudaMemset(M->d_err, 0, sizeof(int)) != cudaSuccess)) {
+    set_error("tn_matrix_create: error flag allocation failed");
+    rc = TN_ENOMEM;
+  }
   uint8_t* staging = nullptr;
   const uint8_t* src = (const uint8_t*)packed;
   if (!rc && !on_device) {
@@ -75,6 +80,7 @@ extern "C" int tn_matrix_create(int32_t device, int32_t quant, int32_t rows, int
   if (staging) cudaFree(staging);
   if (rc) {
     matrix_free(&M->m);
+    if (M->d_err) cudaFree(M->d_err);
     delete M;
     return rc;
   }
@@ -87,6 +93,10 @@ extern "C" int tn_matrix_matvec(const tn_matrix* m, int32_t n_tokens, const floa
   clear_error();
   TN_REQUIRE(m && d_x && d_y && n_tokens >= 0, TN_EINVAL, "tn_matrix_matvec: bad argument");
   DevSwitch g(m->device);
+  // one or two tokens: the bulk-copy decode kernel; more: the multi-token kernel
+  if (matvec_dec_ok(m->m, n_tokens) && (reinterpret_cast<uintptr_t>(d_x) & 15) == 0)
+    return matvec_dec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, MvFuse(), m->d_err,
+                      (cudaStream_t)stream);
   return matvec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, (cudaStream_t)stream);
 }
 
@@ -103,6 +113,7 @@ extern "C" void tn_matrix_free(tn_matrix* m) {
   if (!m) return;
   DevSwitch g(m->device);
   matrix_free(&m->m);
+  if (m->d_err) cudaFree(m->d_err);
   delete m;
 }
 

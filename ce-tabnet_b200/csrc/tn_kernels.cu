@@ -79,7 +79,7 @@ __global__ void k_repack_q(const uint8_t* __restrict__ src, int quant, int src_r
     const uint64_t dr = dst_row(r, dst_off, dst_stride);
     uint8_t* dq = data + (dr * nb + b) * qb;
     for (int j = 0; j < qb; j++) dq[j] = blk[2 + j];
-    scales[((dr >> 3) * nb + b) * 8 + (dr & 7)] = (uint16_t)(blk[0] | (blk[1] << 8));
+    scales[dr * nb + b] = (uint16_t)(blk[0] | (blk[1] << 8));
   }
 }
 
@@ -101,7 +101,7 @@ __global__ void k_repack_q16(const uint16_t* __restrict__ src, int src_rows, int
     uint4* dq = data + (dr * nb + b) * (QB / 16);
 #pragma unroll
     for (int v = 0; v < QB / 16; v++) dq[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
-    scales[((dr >> 3) * nb + b) * 8 + (dr & 7)] = blk[0];
+    scales[dr * nb + b] = blk[0];
   }
 }
 
@@ -131,7 +131,7 @@ int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
   TN_REQUIRE(quant_bytes(1, src_quant) != 0, TN_EUNSUPPORTED, "unsupported quant %d", src_quant);
   m->rows = rows;
   m->cols = cols;
-  m->rows_pad = (rows + 7) & ~7;
+  m->rows_pad = (rows + 15) & ~15;
   m->cols_pad = (cols + 31) & ~31;
   m->nb = m->cols_pad / 32;
   const bool aligned = (cols % 32) == 0;
@@ -194,7 +194,7 @@ __device__ __forceinline__ float mat_elem(int kind, const uint8_t* data, const u
   if (kind == MK_F32) return ((const float*)data)[r * cols_pad + c];
   if (kind == MK_F16) return f16_to_f32(((const uint16_t*)data)[r * cols_pad + c]);
   const int b = c >> 5, j = c & 31;
-  const float d = f16_to_f32(scales[((r >> 3) * nb + b) * 8 + (r & 7)]);
+  const float d = f16_to_f32(scales[r * nb + b]);
   if (kind == MK_Q8) return (float)(int8_t)data[(r * nb + b) * 32 + j] * d;
   const uint8_t byte = data[(r * nb + b) * 16 + (j >> 1)];
   return (float)(((j & 1) ? (byte >> 4) : (byte & 15)) - 8) * d;
@@ -341,9 +341,9 @@ __global__ void __launch_bounds__(512) k_matvec(const uint8_t* __restrict__ data
             }
             float d[RG];
             if (KIND == MK_Q4 || KIND == MK_Q8) {
-              const uint16_t* ps = scales + ((size_t)g * nb + b) * 8 + rs;
 #pragma unroll
-              for (int i = 0; i < RG; i++) d[i] = __half2float(__ushort_as_half(ps[i]));
+              for (int i = 0; i < RG; i++)
+                d[i] = __half2float(__ushort_as_half(scales[(size_t)(g * 8 + rs + i) * nb + b]));
             }
 #pragma unroll
             for (int i = 0; i < RG; i++) {
@@ -505,11 +505,12 @@ __device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepc
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, Args... args) {
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
-  cfg.dynamicSmemBytes = 0;
+  cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -519,17 +520,51 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cud
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
-// compile-time loop: f(std::integral_constant<int, I>) for I in [B, E)
-template <int B, int E>
-struct Unroll {
-  template <class F>
-  __device__ __forceinline__ static void run(F&& f) {
-    if constexpr (B < E) {
-      f(std::integral_constant<int, B>{});
-      Unroll<B + 1, E>::run(f);
+// ---- mbarrier + bulk-copy (TMA) primitives
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after ~2 s (or when another thread of the CTA gave
+// up), raising the CTA's abort flag; callers then stop and report an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const long long t0 = clock64();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 255u) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > 4000000000ll) {
+        *abort_flag = 1;
+        return false;
+      }
     }
   }
-};
+}
+// global -> shared bulk copy completing on an mbarrier (16-byte aligned, size % 16 == 0)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
 
 struct MvdArgs {
   const uint8_t* data;
@@ -539,113 +574,11 @@ struct MvdArgs {
   int ldx;
   float* y;
   int ldy, mode;
+  int stages;       // shared-memory ring depth
+  uint32_t stage_bytes;
+  int* err;         // set to 1 if a bounded wait gave up
   MvFuse f;
 };
-
-// A unit is RG rows x NBT block columns of one 8-row group, sized so one
-// buffer of its weights is 32 registers; two buffers alternate (the next
-// unit's loads are in flight while the current one is reduced).
-template <int KIND, int NBT>
-struct MvdCfg {
-  static constexpr int BB = kind_block_bytes(KIND), W = BB / 4;
-  static constexpr int RG0 = 32 / (W * NBT);
-  static constexpr int RG = RG0 < 1 ? 1 : (RG0 > 8 ? 8 : RG0);
-  static constexpr int SPG = 8 / RG;             // units per group
-  static constexpr int UPI = SPG < 2 ? 2 : SPG;  // units per unrolled iteration (even)
-  static constexpr int GPI = UPI / SPG;          // groups per iteration
-  static constexpr int ND = (RG + 1) / 2;        // 32-bit words of fp16 scales per unit column
-  static constexpr int CHG = 8;                  // groups per reduction chunk
-};
-
-template <int KIND, int NBT>
-struct MvdUnit {
-  using C = MvdCfg<KIND, NBT>;
-  uint32_t w[C::RG][NBT][C::W];
-  uint32_t d[NBT][C::ND];
-};
-
-template <int KIND, int NBT>
-__device__ __forceinline__ void mvd_load(const MvdArgs& a, int g, int rs, int tid, int NT, MvdUnit<KIND, NBT>& u) {
-  using C = MvdCfg<KIND, NBT>;
-#pragma unroll
-  for (int j = 0; j < NBT; j++) {
-    const int b = tid + j * NT;
-    if (b < a.nb) {
-#pragma unroll
-      for (int i = 0; i < C::RG; i++) {
-        const uint8_t* p = a.data + ((size_t)(g * 8 + rs + i) * a.nb + b) * C::BB;
-#pragma unroll
-        for (int v = 0; v < C::W / 4; v++) {
-          const uint4 q = ld_stream(p + 16 * v);
-          u.w[i][j][4 * v] = q.x;
-          u.w[i][j][4 * v + 1] = q.y;
-          u.w[i][j][4 * v + 2] = q.z;
-          u.w[i][j][4 * v + 3] = q.w;
-        }
-      }
-      const uint16_t* ps = a.scales + ((size_t)g * a.nb + b) * 8 + rs;
-      if constexpr (C::RG == 8) {
-        const uint4 q = *reinterpret_cast<const uint4*>(ps);
-        u.d[j][0] = q.x;
-        u.d[j][1] = q.y;
-        u.d[j][2] = q.z;
-        u.d[j][3] = q.w;
-      } else if constexpr (C::RG == 4) {
-        const uint2 q = *reinterpret_cast<const uint2*>(ps);
-        u.d[j][0] = q.x;
-        u.d[j][1] = q.y;
-      } else if constexpr (C::RG == 2) {
-        u.d[j][0] = *reinterpret_cast<const uint32_t*>(ps);
-      } else {
-        u.d[j][0] = ps[0];
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < C::ND; k++) u.d[j][k] = 0u;
-    }
-  }
-}
-
-// partial dot products of one unit into acc[RS + i][tt]
-template <int KIND, int TT, int NBT, int RS>
-__device__ __forceinline__ void mvd_compute(const MvdUnit<KIND, NBT>& u, const float (&xr)[TT][NBT][32],
-                                            const float (&xs)[TT][NBT], float (&acc)[8][TT]) {
-  using C = MvdCfg<KIND, NBT>;
-#pragma unroll
-  for (int j = 0; j < NBT; j++) {
-#pragma unroll
-    for (int i = 0; i < C::RG; i++) {
-      const uint32_t dd = u.d[j][i >> 1];
-      const float di = __half2float(__ushort_as_half((unsigned short)((i & 1) ? (dd >> 16) : (dd & 0xffffu))));
-#pragma unroll
-      for (int tt = 0; tt < TT; tt++) {
-        float s0 = 0.f, s1 = 0.f;  // two chains for ILP
-        if constexpr (KIND == MK_Q4) {
-#pragma unroll
-          for (int k = 0; k < 4; k++) {
-            const uint32_t lo = u.w[i][j][k] & 0x0F0F0F0Fu, hi = (u.w[i][j][k] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-            for (int m = 0; m < 4; m++) {
-              s0 = fmaf(q4_f(lo, m), xr[tt][j][8 * k + 2 * m], s0);
-              s1 = fmaf(q4_f(hi, m), xr[tt][j][8 * k + 2 * m + 1], s1);
-            }
-          }
-          acc[RS + i][tt] = fmaf(di, fmaf(256.f, s0 + s1, xs[tt][j]), acc[RS + i][tt]);
-        } else {
-#pragma unroll
-          for (int k = 0; k < 8; k++) {
-            const uint32_t bq = u.w[i][j][k] ^ 0x80808080u;
-            s0 = fmaf(q8_f(bq, 0) - 8388736.0f, xr[tt][j][4 * k], s0);
-            s1 = fmaf(q8_f(bq, 1) - 8388736.0f, xr[tt][j][4 * k + 1], s1);
-            s0 = fmaf(q8_f(bq, 2) - 8388736.0f, xr[tt][j][4 * k + 2], s0);
-            s1 = fmaf(q8_f(bq, 3) - 8388736.0f, xr[tt][j][4 * k + 3], s1);
-          }
-          acc[RS + i][tt] = fmaf(di, s0 + s1, acc[RS + i][tt]);
-        }
-      }
-    }
-  }
-}
 
 // epilogue of rows [row0, row0 + nrows), whose per-warp partials are in red
 template <int TT>
@@ -654,12 +587,12 @@ __device__ __forceinline__ void mvd_epilogue(const MvdArgs& a, const float* red,
   for (int e = tid; e < nrows * TT; e += NT) {
     const int r = e / TT, tt = e % TT, row = row0 + r;
     if (row >= a.rows || tt >= a.T) continue;
-    const bool pair_second = (a.mode == EPI_SWIGLU || (a.mode == EPI_QKV_ROPE && row < a.f.q_dim + a.f.kv_dim));
-    if (pair_second && (row & 1)) continue;  // handled with its even partner
+    const bool paired = (a.mode == EPI_SWIGLU || (a.mode == EPI_QKV_ROPE && row < a.f.q_dim + a.f.kv_dim));
+    if (paired && (row & 1)) continue;  // handled with its even partner
     float s = 0.f, s2 = 0.f;
     for (int w2 = 0; w2 < nw; w2++) {
       s += red[w2 * red_stride + e];
-      if (pair_second) s2 += red[w2 * red_stride + e + TT];
+      if (paired) s2 += red[w2 * red_stride + e + TT];
     }
     if (a.mode == EPI_STORE || a.mode == EPI_RESID) {
       float* py = a.y + (size_t)tt * a.ldy + row;
@@ -688,30 +621,68 @@ __device__ __forceinline__ void mvd_epilogue(const MvdArgs& a, const float* red,
   }
 }
 
-// CUDA-core dequant-matvec for decode (1-2 tokens).  Each thread owns NBT
-// 32-wide block columns and keeps x for them in registers; a CTA streams a
-// contiguous range of 8-row groups.  Warps never wait on each other inside a
-// 64-row chunk: each warp reduce-scatters its partial sums of a group with
-// shuffles into shared memory, and one barrier per chunk precedes the
-// cross-warp sum and the fused epilogue.
-template <int KIND, int TT, int NBT>
-__global__ void __launch_bounds__(256) k_mvd(const MvdArgs a) {
-  using C = MvdCfg<KIND, NBT>;
-  constexpr int SPG = C::SPG, UPI = C::UPI, GPI = C::GPI, CHG = C::CHG, RG = C::RG;
-  constexpr int NV = 8 * TT;
-  __shared__ float red[2][16][CHG * NV];
-  __shared__ double nsum[16][TT];
+// CUDA-core dequant-matvec for decode (1-2 tokens), fed by TMA bulk copies.
+// A CTA owns a contiguous run of R-row units.  Thread 0 streams each unit's
+// weights and scales (two contiguous bulk copies) into a ring of shared-memory
+// stages guarded by full/empty mbarriers, refilling a stage as soon as every
+// warp has released it, so ~5 units per SM are always in flight.  All threads
+// consume: each owns NBT 32-wide block columns,
+// keep x for them in registers, decode q4_0 / q8_0 from shared memory and
+// reduce-scatter every unit's partial sums across the warp; one consumer
+// barrier per 64 rows precedes the cross-warp sum and the fused epilogue.
+//
+// q4_0 decode without integer->float conversions: a nibble n placed in bits
+// 16..19 of the float 0x3F000000 is 0.5 + n/256 (one PRMT), so per block
+//   sum_j (n_j - 8) x_j = 256 * sum_j f_j x_j - 136 * sum_j x_j
+// and sum_j x_j is computed once.
+template <int KIND, int TT, int NBT, int R>
+__global__ void __launch_bounds__(256, 1) k_mvt(const MvdArgs a) {
+  constexpr int BB = kind_block_bytes(KIND), W = BB / 4;
+  constexpr int NV = R * TT;                    // values reduced per unit
+  constexpr int LOGNV = NV == 2 ? 1 : (NV == 4 ? 2 : (NV == 8 ? 3 : (NV == 16 ? 4 : 5)));
+  constexpr int SH = 5 - LOGNV;
+  constexpr int CHU = 64 / R;                   // units per 64-row reduction chunk
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ float red[2][8][64 * TT];
+  __shared__ double nsum[8][TT];
+  __shared__ volatile int abort_flag;
+  const int NT = blockDim.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = NT >> 5;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.stages * a.stage_bytes);
+  uint64_t* empty = full + a.stages;
+  const int NU = a.rows_pad / R;
+  const int u0 = (int)((int64_t)NU * blockIdx.x / gridDim.x);
+  const int nu = (int)((int64_t)NU * (blockIdx.x + 1) / gridDim.x) - u0;
+  const uint32_t wbytes = (uint32_t)R * a.nb * BB, sbytes = (uint32_t)R * a.nb * 2;
+
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < a.stages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], nw);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
   pdl_launch_dependents();
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, NT = blockDim.x, nw = NT >> 5;
-  const int G = a.rows_pad >> 3;
-  const int g0 = (int)((int64_t)G * blockIdx.x / gridDim.x);
-  const int ng = (int)((int64_t)G * (blockIdx.x + 1) / gridDim.x) - g0;
 
-  MvdUnit<KIND, NBT> ub[2];
-  if (ng > 0) mvd_load<KIND, NBT>(a, g0, 0, tid, NT, ub[0]);
+  // issue unit k into its stage (thread 0 only)
+  auto produce = [&](int k) {
+    const int st = k % a.stages;
+    uint8_t* dst = smem + (size_t)st * a.stage_bytes;
+    const size_t row0 = (size_t)(u0 + k) * R;
+    mbar_expect_tx(&full[st], wbytes + sbytes);
+    bulk_g2s(dst, a.data + row0 * a.nb * BB, wbytes, &full[st]);
+    bulk_g2s(dst + wbytes, a.scales + row0 * a.nb, sbytes, &full[st]);
+  };
+  int issued = 0;
+  if (tid == 0) {
+    // weights do not depend on the previous kernel: start streaming at once
+    for (; issued < nu && issued < a.stages; issued++) produce(issued);
+  }
 
-  // x, produced by the predecessor kernel
-  pdl_wait();
+  // ---------------- consumers
+  pdl_wait();  // x is produced by the predecessor kernel
   float xr[TT][NBT][32];
   float xs[TT][NBT];
   double ss[TT];
@@ -737,14 +708,14 @@ __global__ void __launch_bounds__(256) k_mvd(const MvdArgs a) {
     }
   }
   if (a.f.norm_w) {
-    // RMSNorm (web/inference-worker.js:516-522): the CTA's threads hold the whole row
+    // RMSNorm (web/inference-worker.js:516-522): the consumers hold the whole row
 #pragma unroll
     for (int tt = 0; tt < TT; tt++) {
       double v = ss[tt];
       for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       if (lane == 0) nsum[warp][tt] = v;
     }
-    __syncthreads();
+    consumer_sync(NT);
 #pragma unroll
     for (int tt = 0; tt < TT; tt++) {
       double tot = 0.0;
@@ -771,111 +742,193 @@ __global__ void __launch_bounds__(256) k_mvd(const MvdArgs a) {
       xs[tt][j] = KIND == MK_Q4 ? -136.f * s : s;
     }
 
-  float acc[8][TT];
-#pragma unroll
-  for (int i = 0; i < 8; i++)
-#pragma unroll
-    for (int tt = 0; tt < TT; tt++) acc[i][tt] = 0.f;
+  // Every thread runs every iteration and barrier even after an abort (then
+  // it only skips the math), so no thread can be left waiting at bar.sync.
   int rb = 0;
-  for (int gi = 0; gi < ng; gi += GPI) {
-    Unroll<0, UPI>::run([&](auto uc) {
-      constexpr int u = decltype(uc)::value;
-      const int gg = gi + u / SPG;
-      {  // prefetch the next unit into the other buffer
-        constexpr int un = u + 1;
-        const int ggn = gi + un / SPG;
-        if (ggn < ng) mvd_load<KIND, NBT>(a, g0 + ggn, (un % SPG) * RG, tid, NT, ub[un & 1]);
-      }
-      if (gg < ng) mvd_compute<KIND, TT, NBT, (u % SPG) * RG>(ub[u & 1], xr, xs, acc);
-      if constexpr (u % SPG == SPG - 1) {
-        if (gg < ng) {
-          float v[NV];
+  for (int k = 0; k < nu; k++) {
+    const int st = k % a.stages;
+    const bool ready = mbar_wait(&full[st], (k / a.stages) & 1, &abort_flag);
+    const uint8_t* wsm = smem + (size_t)st * a.stage_bytes;
+    const uint16_t* ssm = reinterpret_cast<const uint16_t*>(wsm + wbytes);
+    float acc[R][TT];
 #pragma unroll
-          for (int i = 0; i < 8; i++)
+    for (int i = 0; i < R; i++) {
 #pragma unroll
-            for (int tt = 0; tt < TT; tt++) {
-              v[i * TT + tt] = acc[i][tt];
-              acc[i][tt] = 0.f;
+      for (int tt = 0; tt < TT; tt++) acc[i][tt] = 0.f;
+#pragma unroll
+      for (int j = 0; j < NBT; j++) {
+        const int b = tid + j * NT;
+        if (ready && b < a.nb) {
+          uint32_t w[W];
+#pragma unroll
+          for (int v = 0; v < W / 4; v++) {
+            const uint4 q = *reinterpret_cast<const uint4*>(wsm + ((size_t)i * a.nb + b) * BB + 16 * v);
+            w[4 * v] = q.x;
+            w[4 * v + 1] = q.y;
+            w[4 * v + 2] = q.z;
+            w[4 * v + 3] = q.w;
+          }
+          const float di = __half2float(__ushort_as_half(ssm[i * a.nb + b]));
+#pragma unroll
+          for (int tt = 0; tt < TT; tt++) {
+            float s0 = 0.f, s1 = 0.f;  // two chains for ILP
+            if constexpr (KIND == MK_Q4) {
+#pragma unroll
+              for (int kk = 0; kk < 4; kk++) {
+                const uint32_t lo = w[kk] & 0x0F0F0F0Fu, hi = (w[kk] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                for (int m = 0; m < 4; m++) {
+                  s0 = fmaf(q4_f(lo, m), xr[tt][j][8 * kk + 2 * m], s0);
+                  s1 = fmaf(q4_f(hi, m), xr[tt][j][8 * kk + 2 * m + 1], s1);
+                }
+              }
+              acc[i][tt] = fmaf(di, fmaf(256.f, s0 + s1, xs[tt][j]), acc[i][tt]);
+            } else {
+#pragma unroll
+              for (int kk = 0; kk < 8; kk++) {
+                const uint32_t bq = w[kk] ^ 0x80808080u;
+                s0 = fmaf(q8_f(bq, 0) - 8388736.0f, xr[tt][j][4 * kk], s0);
+                s1 = fmaf(q8_f(bq, 1) - 8388736.0f, xr[tt][j][4 * kk + 1], s1);
+                s0 = fmaf(q8_f(bq, 2) - 8388736.0f, xr[tt][j][4 * kk + 2], s0);
+                s1 = fmaf(q8_f(bq, 3) - 8388736.0f, xr[tt][j][4 * kk + 3], s1);
+              }
+              acc[i][tt] = fmaf(di, s0 + s1, acc[i][tt]);
             }
-          const float r = warp_reduce_scatter<NV>(v, lane);
-          constexpr int SH = NV == 8 ? 2 : 1;
-          const int cg = gg % CHG;
-          if ((lane & ((1 << SH) - 1)) == 0) red[rb][warp][cg * NV + (lane >> SH)] = r;
-          if (cg == CHG - 1 || gg == ng - 1) {
-            __syncthreads();
-            mvd_epilogue<TT>(a, &red[rb][0][0], CHG * NV, nw, (g0 + gg - cg) * 8, (cg + 1) * 8, tid, NT);
-            rb ^= 1;
           }
         }
       }
-    });
+    }
+    // this warp has read the stage: release it; thread 0 refills it once all
+    // warps have, with the unit `stages` ahead
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (tid == 0 && issued < nu && !abort_flag) {
+      if (mbar_wait(&empty[st], (k / a.stages) & 1, &abort_flag)) produce(issued++);
+    }
+    float v[NV];
+#pragma unroll
+    for (int i = 0; i < R; i++)
+#pragma unroll
+      for (int tt = 0; tt < TT; tt++) v[i * TT + tt] = acc[i][tt];
+    const float r = warp_reduce_scatter<NV>(v, lane);
+    const int cu = k % CHU;
+    if ((lane & ((1 << SH) - 1)) == 0) red[rb][warp][cu * NV + (lane >> SH)] = r;
+    if (cu == CHU - 1 || k == nu - 1) {
+      consumer_sync(NT);
+      if (!abort_flag)
+        mvd_epilogue<TT>(a, &red[rb][0][0], 64 * TT, nw, (u0 + k - cu) * R, (cu + 1) * R, tid, NT);
+      rb ^= 1;
+    }
+  }
+  if (tid == 0 && abort_flag) {
+    // no copy may still be landing when the CTA exits
+    for (int j = issued - a.stages > 0 ? issued - a.stages : 0; j < issued; j++) {
+      abort_flag = 0;
+      if (!mbar_wait(&full[j % a.stages], (j / a.stages) & 1, &abort_flag)) break;
+    }
+    atomicExch(a.err, 1);
   }
 }
 
-template <int KIND, int TT, int NBT>
-static int mvd_occupancy(const Matrix& m) {
-  const int NT = ((m.nb + NBT - 1) / NBT + 31) & ~31;
-  int o = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_mvd<KIND, TT, NBT>, NT, 0) != cudaSuccess || o <= 0)
-    o = 1;
-  return o;
+// ---- launch configuration of the decode matvec of one matrix
+static int mvt_nbt(int nb) { return nb <= 256 ? 1 : (nb <= 512 ? 2 : 4); }
+static int mvt_rows(const Matrix& m) {  // R: rows per unit, ~48 KB of weights per stage
+  const int bb = kind_block_bytes(m.kind) + 2;
+  int r = 16;
+  while (r > 2 && (size_t)r * m.nb * bb > 49152) r >>= 1;
+  return r;
 }
 
-// block columns per thread of the decode matvec: CTAs of at most 256 threads
-static int mvd_nbt(int nb) { return nb <= 256 ? 1 : (nb <= 512 ? 2 : 4); }
+template <int KIND, int TT, int NBT, int R>
+static void mvt_set_smem(int bytes) {
+  cudaFuncSetAttribute(k_mvt<KIND, TT, NBT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
 
-template <int KIND>
-static void mvd_prepare_kind(Matrix* m) {
-  switch (mvd_nbt(m->nb)) {
-    case 1: m->occ_dec[0] = mvd_occupancy<KIND, 1, 1>(*m); m->occ_dec[1] = mvd_occupancy<KIND, 2, 1>(*m); break;
-    case 2: m->occ_dec[0] = mvd_occupancy<KIND, 1, 2>(*m); m->occ_dec[1] = mvd_occupancy<KIND, 2, 2>(*m); break;
-    default: m->occ_dec[0] = mvd_occupancy<KIND, 1, 4>(*m); break;
+template <int KIND, int TT, int NBT>
+static void mvt_set_smem_r(int R, int bytes) {
+  switch (R) {
+    case 2: mvt_set_smem<KIND, TT, NBT, 2>(bytes); break;
+    case 4: mvt_set_smem<KIND, TT, NBT, 4>(bytes); break;
+    case 8: mvt_set_smem<KIND, TT, NBT, 8>(bytes); break;
+    default: mvt_set_smem<KIND, TT, NBT, 16>(bytes); break;
   }
 }
 
 static void mvd_prepare(Matrix* m) {
-  if (m->nb > 1024) return;
-  if (m->kind == MK_Q4) mvd_prepare_kind<MK_Q4>(m);
-  else if (m->kind == MK_Q8) mvd_prepare_kind<MK_Q8>(m);
+  if (!(m->kind == MK_Q4 || m->kind == MK_Q8) || m->nb > 1024) return;
+  const int R = mvt_rows(*m), nbt = mvt_nbt(m->nb);
+  // every unit's scale run must start on a 16-byte boundary and be a multiple
+  // of 16 bytes for the bulk copy (the weight run always is): else no decode kernel
+  if (((size_t)R * m->nb * 2) % 16 != 0) return;
+  const uint32_t stage = (uint32_t)(((size_t)R * m->nb * (kind_block_bytes(m->kind) + 2) + 127) & ~(size_t)127);
+  int stages = (int)std::min<size_t>(6, (200 * 1024) / stage);
+  if (stages < 2) stages = 2;
+  m->mvt_rows = R;
+  m->mvt_stages = stages;
+  m->mvt_stage_bytes = stage;
+  m->mvt_smem = (int)(stages * stage + 2 * stages * sizeof(uint64_t));
+  // (set once, outside any stream capture)
+  if (m->kind == MK_Q4) {
+    if (nbt == 1) { mvt_set_smem_r<MK_Q4, 1, 1>(R, m->mvt_smem); mvt_set_smem_r<MK_Q4, 2, 1>(R, m->mvt_smem); }
+    else if (nbt == 2) { mvt_set_smem_r<MK_Q4, 1, 2>(R, m->mvt_smem); mvt_set_smem_r<MK_Q4, 2, 2>(R, m->mvt_smem); }
+    else mvt_set_smem_r<MK_Q4, 1, 4>(R, m->mvt_smem);
+  } else {
+    if (nbt == 1) { mvt_set_smem_r<MK_Q8, 1, 1>(R, m->mvt_smem); mvt_set_smem_r<MK_Q8, 2, 1>(R, m->mvt_smem); }
+    else if (nbt == 2) { mvt_set_smem_r<MK_Q8, 1, 2>(R, m->mvt_smem); mvt_set_smem_r<MK_Q8, 2, 2>(R, m->mvt_smem); }
+    else mvt_set_smem_r<MK_Q8, 1, 4>(R, m->mvt_smem);
+  }
 }
 
-template <int KIND, int TT, int NBT>
-static int launch_mvd(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
-                      const MvFuse& f, cudaStream_t s) {
+template <int KIND, int TT, int NBT, int R>
+static int launch_mvt(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
+                      const MvFuse& f, int* err, cudaStream_t s) {
   const int NT = ((m.nb + NBT - 1) / NBT + 31) & ~31;
-  const int occ = m.occ_dec[TT - 1] > 0 ? m.occ_dec[TT - 1] : 1;
-  const int grid = std::max(1, std::min(m.rows_pad / 8, occ * num_sms()));
-  const MvdArgs a{m.data, m.scales, m.rows, m.rows_pad, m.cols, m.nb, T, x, ldx, y, ldy, mode, f};
-  TN_CHECK_CUDA(launch_pdl(k_mvd<KIND, TT, NBT>, dim3(grid), dim3(NT), s, a));
+  const int NU = m.rows_pad / R;
+  const int grid = std::max(1, std::min(NU, num_sms()));
+  const MvdArgs a{m.data, m.scales, m.rows, m.rows_pad, m.cols, m.nb, T, x, ldx, y, ldy, mode,
+                  m.mvt_stages, m.mvt_stage_bytes, err, f};
+  TN_CHECK_CUDA(launch_pdl(k_mvt<KIND, TT, NBT, R>, dim3(grid), dim3(NT), (size_t)m.mvt_smem, s, a));
   return TN_OK;
 }
 
+template <int KIND, int TT, int NBT>
+static int launch_mvt_r(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
+                        const MvFuse& f, int* err, cudaStream_t s) {
+  switch (m.mvt_rows) {
+    case 2: return launch_mvt<KIND, TT, NBT, 2>(m, T, x, ldx, y, ldy, mode, f, err, s);
+    case 4: return launch_mvt<KIND, TT, NBT, 4>(m, T, x, ldx, y, ldy, mode, f, err, s);
+    case 8: return launch_mvt<KIND, TT, NBT, 8>(m, T, x, ldx, y, ldy, mode, f, err, s);
+    default: return launch_mvt<KIND, TT, NBT, 16>(m, T, x, ldx, y, ldy, mode, f, err, s);
+  }
+}
+
 bool matvec_dec_ok(const Matrix& m, int T) {
-  if (!(m.kind == MK_Q4 || m.kind == MK_Q8) || m.nb > 1024 || T < 1) return false;
-  return T <= (mvd_nbt(m.nb) <= 2 ? 2 : 1);
+  if (!(m.kind == MK_Q4 || m.kind == MK_Q8) || m.nb > 1024 || T < 1 || m.mvt_rows == 0) return false;
+  return T <= (mvt_nbt(m.nb) <= 2 ? 2 : 1);
 }
 
 template <int KIND>
 static int matvec_dec_kind(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
-                           const MvFuse& f, cudaStream_t s) {
-  switch (mvd_nbt(m.nb)) {
-    case 1: return T == 1 ? launch_mvd<KIND, 1, 1>(m, T, x, ldx, y, ldy, mode, f, s)
-                          : launch_mvd<KIND, 2, 1>(m, T, x, ldx, y, ldy, mode, f, s);
-    case 2: return T == 1 ? launch_mvd<KIND, 1, 2>(m, T, x, ldx, y, ldy, mode, f, s)
-                          : launch_mvd<KIND, 2, 2>(m, T, x, ldx, y, ldy, mode, f, s);
-    default: return launch_mvd<KIND, 1, 4>(m, T, x, ldx, y, ldy, mode, f, s);
+                           const MvFuse& f, int* err, cudaStream_t s) {
+  switch (mvt_nbt(m.nb)) {
+    case 1: return T == 1 ? launch_mvt_r<KIND, 1, 1>(m, T, x, ldx, y, ldy, mode, f, err, s)
+                          : launch_mvt_r<KIND, 2, 1>(m, T, x, ldx, y, ldy, mode, f, err, s);
+    case 2: return T == 1 ? launch_mvt_r<KIND, 1, 2>(m, T, x, ldx, y, ldy, mode, f, err, s)
+                          : launch_mvt_r<KIND, 2, 2>(m, T, x, ldx, y, ldy, mode, f, err, s);
+    default: return launch_mvt_r<KIND, 1, 4>(m, T, x, ldx, y, ldy, mode, f, err, s);
   }
 }
 
 int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
-               cudaStream_t s) {
+               int* err, cudaStream_t s) {
   TN_REQUIRE(matvec_dec_ok(m, T), TN_EUNSUPPORTED, "matvec_dec: %d tokens of kind %d, %d columns", T, m.kind,
              m.cols);
   TN_REQUIRE((ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0, TN_EINVAL,
              "matvec_dec: x rows must be 16-byte aligned");
   TN_REQUIRE(mode != EPI_SWIGLU || (m.rows & 1) == 0, TN_EINVAL, "swiglu needs paired rows");
-  if (m.kind == MK_Q4) return matvec_dec_kind<MK_Q4>(m, T, x, ldx, y, ldy, mode, f, s);
-  return matvec_dec_kind<MK_Q8>(m, T, x, ldx, y, ldy, mode, f, s);
+  TN_REQUIRE(err, TN_EINVAL, "matvec_dec: error flag required");
+  if (m.kind == MK_Q4) return matvec_dec_kind<MK_Q4>(m, T, x, ldx, y, ldy, mode, f, err, s);
+  return matvec_dec_kind<MK_Q8>(m, T, x, ldx, y, ldy, mode, f, err, s);
 }
 
 // ================================================================ rmsnorm

@@ -11,8 +11,9 @@ namespace tn {
 //   MK_F16: data [rows_pad][cols_pad]  fp16 bits (zero padded)
 //   MK_F32: data [rows_pad][cols_pad]  f32 (zero padded); also holds exactly dequantised
 //           q4_0/q8_0 tensors whose rows do not start on a block boundary
-//   scales (MK_Q4 / MK_Q8): [rows_pad/8][nb][8] fp16 bits -- the 8 rows of a row group
-//           that share a block column sit in one 16-byte vector.
+//   scales (MK_Q4 / MK_Q8): [rows_pad][nb] fp16 bits, so R consecutive rows are
+//           one contiguous run of the data plane plus one of the scale plane
+//   rows_pad is a multiple of 16.
 enum MatKind { MK_Q4 = 0, MK_Q8 = 1, MK_F16 = 2, MK_F32 = 3 };
 
 struct Matrix {
@@ -23,7 +24,9 @@ struct Matrix {
   uint16_t* scales = nullptr;
   size_t bytes = 0;
   int occ[2] = {0, 0};      // resident CTAs per SM of the matvec launch shapes (1 and 2 tokens per tile)
-  int occ_dec[2] = {0, 0};  // the same for the decode matvec (1 and 2 tokens)
+  // decode matvec launch shape: rows per bulk-copied unit, ring depth, bytes
+  int mvt_rows = 0, mvt_stages = 0, mvt_smem = 0;
+  uint32_t mvt_stage_bytes = 0;
 };
 
 // bytes per 32-element block of the data plane
@@ -73,8 +76,9 @@ struct MvFuse {
 };
 // the decode matvec handles up to 2 tokens of q4_0 / q8_0 matrices
 bool matvec_dec_ok(const Matrix& m, int T);
+// err: device int set to 1 if a bounded wait inside the kernel gave up
 int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
-               cudaStream_t s);
+               int* err, cudaStream_t s);
 // split-K decode attention with the split merge done by the last CTA of each
 // (row, KV head); counters: T * nKV ints, zero between calls
 int attention_dec(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,

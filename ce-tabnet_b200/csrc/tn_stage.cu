@@ -92,6 +92,7 @@ struct tn_stage {
         *logits = nullptr;
   uint16_t *hid_in = nullptr, *hid_out = nullptr;
   int *ids = nullptr, *tok_out = nullptr, *err = nullptr;
+  int* kerr = nullptr;  // set by a kernel whose bounded wait gave up
   double2* cs = nullptr;
   double* freq = nullptr;
   void* attn_scratch = nullptr;
@@ -345,6 +346,7 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   if ((rc = dalloc(st, &st->ids, (size_t)T))) return rc;
   if ((rc = dalloc(st, &st->tok_out, (size_t)T))) return rc;
   if ((rc = dalloc(st, &st->err, 1))) return rc;
+  if ((rc = dalloc(st, &st->kerr, 1))) return rc;
   if ((rc = dalloc(st, &st->cs, (size_t)T * (st->hd / 2)))) return rc;
   if ((rc = dalloc(st, &st->freq, (size_t)(st->hd / 2)))) return rc;
   size_t att_bytes = 0;
@@ -461,7 +463,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       f.q_dim = st->qDim;
       f.kv_dim = st->kvDim;
       f.hd = st->hd;
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec_dec(L.qkv, T, st->h, H, st->qkv, ldqkv, EPI_QKV_ROPE, f, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec_dec(L.qkv, T, st->h, H, st->qkv, ldqkv, EPI_QKV_ROPE, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
       TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, s));
@@ -473,19 +475,19 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
                    attention(st->q, st->qDim, kc, vc, st->slot_stride, st->kvh_stride, rows, T, st->nH, st->nKV,
                              st->hd, ns, st->att, st->qDim, st->attn_scratch, s));
     if (fuse && matvec_dec_ok(L.o, T))
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
       TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, s));
     if (fuse && matvec_dec_ok(L.gu, T)) {
       MvFuse f;
       f.norm_w = L.ffn_norm;
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec_dec(L.gu, T, st->h, H, st->act, st->F, EPI_SWIGLU, f, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec_dec(L.gu, T, st->h, H, st->act, st->F, EPI_SWIGLU, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.ffn_norm, st->xn, H, H, T, s));
       TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, s));
     }
     if (fuse && matvec_dec_ok(L.down, T))
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec_dec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, MvFuse(), s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec_dec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
       TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, s));
   }
@@ -495,7 +497,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       f.norm_w = st->final_norm;
       f.rowsel = outrows;
       TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1,
-                     matvec_dec(st->lm_head, n_out, st->h, H, st->logits, st->V, EPI_STORE, f, s));
+                     matvec_dec(st->lm_head, n_out, st->h, H, st->logits, st->V, EPI_STORE, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, outrows, st->final_norm, st->xn, H, H, n_out, s));
       TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1,
@@ -719,6 +721,15 @@ static int forward_impl(tn_stage* st, const tn_fwd_req* reqs, int n, tn_fwd_out*
     }
   }
   TN_CHECK_CUDA(cudaStreamSynchronize(s));
+  {
+    int kerr = 0;
+    TN_CHECK_CUDA(cudaMemcpy(&kerr, st->kerr, sizeof(int), cudaMemcpyDeviceToHost));
+    if (kerr) {
+      TN_CHECK_CUDA(cudaMemset(st->kerr, 0, sizeof(int)));
+      set_error("a kernel's bounded wait on its copy pipeline gave up; the step's outputs are invalid");
+      return TN_ETIMEOUT;
+    }
+  }
   for (int i = 0; i < n; i++) {
     st->kv_len[slot[i]] += reqs[i].n_tokens;
     if (st->last) outs[i].n_hidden_tokens = 0;
