@@ -635,8 +635,18 @@ __device__ __forceinline__ void mvd_epilogue(const MvdArgs& a, const float* red,
 // 16..19 of the float 0x3F000000 is 0.5 + n/256 (one PRMT), so per block
 //   sum_j (n_j - 8) x_j = 256 * sum_j f_j x_j - 136 * sum_j x_j
 // and sum_j x_j is computed once.
+// d0 += a0 * b0, d1 += a1 * b1 with one packed f32x2 FMA (sm_100)
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n .reg .b64 ra, rb, rc;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%0, %1};\n"
+      " fma.rn.f32x2 rc, ra, rb, rc;\n mov.b64 {%0, %1}, rc;\n}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
+constexpr int kMvtMaxStages = 8;
+
 template <int KIND, int TT, int NBT, int R>
-__global__ void __launch_bounds__(256, 1) k_mvt(const MvdArgs a) {
+__global__ void __launch_bounds__(256, NBT == 1 ? 2 : 1) k_mvt(const MvdArgs a) {
   constexpr int BB = kind_block_bytes(KIND), W = BB / 4;
   constexpr int NV = R * TT;                    // values reduced per unit
   constexpr int LOGNV = NV == 2 ? 1 : (NV == 4 ? 2 : (NV == 8 ? 3 : (NV == 16 ? 4 : 5)));
@@ -645,11 +655,12 @@ __global__ void __launch_bounds__(256, 1) k_mvt(const MvdArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ float red[2][8][64 * TT];
   __shared__ double nsum[8][TT];
+  __shared__ int released[kMvtMaxStages];       // warps done with each stage's current unit
+  __shared__ int last_unit[kMvtMaxStages];      // unit last issued into each stage
   __shared__ volatile int abort_flag;
   const int NT = blockDim.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = NT >> 5;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.stages * a.stage_bytes);
-  uint64_t* empty = full + a.stages;
   const int NU = a.rows_pad / R;
   const int u0 = (int)((int64_t)NU * blockIdx.x / gridDim.x);
   const int nu = (int)((int64_t)NU * (blockIdx.x + 1) / gridDim.x) - u0;
@@ -659,26 +670,27 @@ __global__ void __launch_bounds__(256, 1) k_mvt(const MvdArgs a) {
     abort_flag = 0;
     for (int s = 0; s < a.stages; s++) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], nw);
+      released[s] = 0;
+      last_unit[s] = -1;
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
   pdl_launch_dependents();
 
-  // issue unit k into its stage (thread 0 only)
+  // issue unit k into its stage
   auto produce = [&](int k) {
     const int st = k % a.stages;
     uint8_t* dst = smem + (size_t)st * a.stage_bytes;
     const size_t row0 = (size_t)(u0 + k) * R;
+    last_unit[st] = k;
     mbar_expect_tx(&full[st], wbytes + sbytes);
     bulk_g2s(dst, a.data + row0 * a.nb * BB, wbytes, &full[st]);
     bulk_g2s(dst + wbytes, a.scales + row0 * a.nb, sbytes, &full[st]);
   };
-  int issued = 0;
   if (tid == 0) {
     // weights do not depend on the previous kernel: start streaming at once
-    for (; issued < nu && issued < a.stages; issued++) produce(issued);
+    for (int k = 0; k < nu && k < a.stages; k++) produce(k);
   }
 
   // ---------------- consumers
@@ -771,26 +783,25 @@ __global__ void __launch_bounds__(256, 1) k_mvt(const MvdArgs a) {
           const float di = __half2float(__ushort_as_half(ssm[i * a.nb + b]));
 #pragma unroll
           for (int tt = 0; tt < TT; tt++) {
-            float s0 = 0.f, s1 = 0.f;  // two chains for ILP
+            // even / odd elements in the two halves of packed f32x2 FMAs
+            float s0 = 0.f, s1 = 0.f;
             if constexpr (KIND == MK_Q4) {
 #pragma unroll
               for (int kk = 0; kk < 4; kk++) {
                 const uint32_t lo = w[kk] & 0x0F0F0F0Fu, hi = (w[kk] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-                for (int m = 0; m < 4; m++) {
-                  s0 = fmaf(q4_f(lo, m), xr[tt][j][8 * kk + 2 * m], s0);
-                  s1 = fmaf(q4_f(hi, m), xr[tt][j][8 * kk + 2 * m + 1], s1);
-                }
+                for (int m = 0; m < 4; m++)
+                  ffma2(s0, s1, q4_f(lo, m), q4_f(hi, m), xr[tt][j][8 * kk + 2 * m], xr[tt][j][8 * kk + 2 * m + 1]);
               }
               acc[i][tt] = fmaf(di, fmaf(256.f, s0 + s1, xs[tt][j]), acc[i][tt]);
             } else {
 #pragma unroll
               for (int kk = 0; kk < 8; kk++) {
                 const uint32_t bq = w[kk] ^ 0x80808080u;
-                s0 = fmaf(q8_f(bq, 0) - 8388736.0f, xr[tt][j][4 * kk], s0);
-                s1 = fmaf(q8_f(bq, 1) - 8388736.0f, xr[tt][j][4 * kk + 1], s1);
-                s0 = fmaf(q8_f(bq, 2) - 8388736.0f, xr[tt][j][4 * kk + 2], s0);
-                s1 = fmaf(q8_f(bq, 3) - 8388736.0f, xr[tt][j][4 * kk + 3], s1);
+                ffma2(s0, s1, q8_f(bq, 0) - 8388736.0f, q8_f(bq, 1) - 8388736.0f, xr[tt][j][4 * kk],
+                      xr[tt][j][4 * kk + 1]);
+                ffma2(s0, s1, q8_f(bq, 2) - 8388736.0f, q8_f(bq, 3) - 8388736.0f, xr[tt][j][4 * kk + 2],
+                      xr[tt][j][4 * kk + 3]);
               }
               acc[i][tt] = fmaf(di, s0 + s1, acc[i][tt]);
             }
@@ -798,12 +809,21 @@ __global__ void __launch_bounds__(256, 1) k_mvt(const MvdArgs a) {
         }
       }
     }
-    // this warp has read the stage: release it; thread 0 refills it once all
-    // warps have, with the unit `stages` ahead
+    // this warp has read the stage: the last warp to release it refills it
+    // with the unit `stages` ahead (nobody waits for the slowest warp)
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
-    if (tid == 0 && issued < nu && !abort_flag) {
-      if (mbar_wait(&empty[st], (k / a.stages) & 1, &abort_flag)) produce(issued++);
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&released[st], 1) == nw - 1) {
+        __threadfence_block();
+        released[st] = 0;
+        const int kn = k + a.stages;
+        if (kn < nu && !abort_flag) {
+          // order every warp's reads of the stage before the copy that overwrites it
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          produce(kn);
+        }
+      }
     }
     float v[NV];
 #pragma unroll
@@ -820,11 +840,14 @@ __global__ void __launch_bounds__(256, 1) k_mvt(const MvdArgs a) {
       rb ^= 1;
     }
   }
+  consumer_sync(NT);
   if (tid == 0 && abort_flag) {
     // no copy may still be landing when the CTA exits
-    for (int j = issued - a.stages > 0 ? issued - a.stages : 0; j < issued; j++) {
+    for (int s = 0; s < a.stages; s++) {
+      const int j = last_unit[s];
+      if (j < 0) continue;
       abort_flag = 0;
-      if (!mbar_wait(&full[j % a.stages], (j / a.stages) & 1, &abort_flag)) break;
+      if (!mbar_wait(&full[s], (j / a.stages) & 1, &abort_flag)) break;
     }
     atomicExch(a.err, 1);
   }
@@ -832,11 +855,23 @@ __global__ void __launch_bounds__(256, 1) k_mvt(const MvdArgs a) {
 
 // ---- launch configuration of the decode matvec of one matrix
 static int mvt_nbt(int nb) { return nb <= 256 ? 1 : (nb <= 512 ? 2 : 4); }
-static int mvt_rows(const Matrix& m) {  // R: rows per unit, ~48 KB of weights per stage
+// One block column per thread: 2 CTAs per SM, ~24 KB stages in ~96 KB rings;
+// wider rows (more x registers per thread): 1 CTA per SM, ~48 KB stages.
+static int mvt_ctas_target(int nb) { return mvt_nbt(nb) == 1 ? 2 : 1; }
+static int mvt_rows(const Matrix& m) {  // R: rows per unit
   const int bb = kind_block_bytes(m.kind) + 2;
+  const size_t cap = mvt_ctas_target(m.nb) == 2 ? 24576 : 49152;
   int r = 16;
-  while (r > 2 && (size_t)r * m.nb * bb > 49152) r >>= 1;
+  while (r > 2 && (size_t)r * m.nb * bb > cap) r >>= 1;
   return r;
+}
+
+template <int KIND, int TT, int NBT, int R>
+static int mvt_occ(int threads, int smem) {
+  int o = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_mvt<KIND, TT, NBT, R>, threads, smem) != cudaSuccess)
+    o = 1;
+  return o < 1 ? 1 : o;
 }
 
 template <int KIND, int TT, int NBT, int R>
@@ -844,13 +879,14 @@ static void mvt_set_smem(int bytes) {
   cudaFuncSetAttribute(k_mvt<KIND, TT, NBT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
+// sets the dynamic shared memory limit; returns resident CTAs per SM
 template <int KIND, int TT, int NBT>
-static void mvt_set_smem_r(int R, int bytes) {
+static int mvt_set_smem_r(int R, int bytes, int threads) {
   switch (R) {
-    case 2: mvt_set_smem<KIND, TT, NBT, 2>(bytes); break;
-    case 4: mvt_set_smem<KIND, TT, NBT, 4>(bytes); break;
-    case 8: mvt_set_smem<KIND, TT, NBT, 8>(bytes); break;
-    default: mvt_set_smem<KIND, TT, NBT, 16>(bytes); break;
+    case 2: mvt_set_smem<KIND, TT, NBT, 2>(bytes); return mvt_occ<KIND, TT, NBT, 2>(threads, bytes);
+    case 4: mvt_set_smem<KIND, TT, NBT, 4>(bytes); return mvt_occ<KIND, TT, NBT, 4>(threads, bytes);
+    case 8: mvt_set_smem<KIND, TT, NBT, 8>(bytes); return mvt_occ<KIND, TT, NBT, 8>(threads, bytes);
+    default: mvt_set_smem<KIND, TT, NBT, 16>(bytes); return mvt_occ<KIND, TT, NBT, 16>(threads, bytes);
   }
 }
 
@@ -861,22 +897,26 @@ static void mvd_prepare(Matrix* m) {
   // of 16 bytes for the bulk copy (the weight run always is): else no decode kernel
   if (((size_t)R * m->nb * 2) % 16 != 0) return;
   const uint32_t stage = (uint32_t)(((size_t)R * m->nb * (kind_block_bytes(m->kind) + 2) + 127) & ~(size_t)127);
-  int stages = (int)std::min<size_t>(6, (200 * 1024) / stage);
-  if (stages < 2) stages = 2;
+  const size_t ring = mvt_ctas_target(m->nb) == 2 ? 96 * 1024 : 200 * 1024;
+  const int stages = (int)std::max<size_t>(2, std::min<size_t>(kMvtMaxStages, ring / stage));
   m->mvt_rows = R;
   m->mvt_stages = stages;
   m->mvt_stage_bytes = stage;
-  m->mvt_smem = (int)(stages * stage + 2 * stages * sizeof(uint64_t));
+  m->mvt_smem = (int)(stages * stage + stages * sizeof(uint64_t));
+  const int NT = ((m->nb + nbt - 1) / nbt + 31) & ~31;
   // (set once, outside any stream capture)
+  int o1 = 1, o2 = 1;
   if (m->kind == MK_Q4) {
-    if (nbt == 1) { mvt_set_smem_r<MK_Q4, 1, 1>(R, m->mvt_smem); mvt_set_smem_r<MK_Q4, 2, 1>(R, m->mvt_smem); }
-    else if (nbt == 2) { mvt_set_smem_r<MK_Q4, 1, 2>(R, m->mvt_smem); mvt_set_smem_r<MK_Q4, 2, 2>(R, m->mvt_smem); }
-    else mvt_set_smem_r<MK_Q4, 1, 4>(R, m->mvt_smem);
+    if (nbt == 1) { o1 = mvt_set_smem_r<MK_Q4, 1, 1>(R, m->mvt_smem, NT); o2 = mvt_set_smem_r<MK_Q4, 2, 1>(R, m->mvt_smem, NT); }
+    else if (nbt == 2) { o1 = mvt_set_smem_r<MK_Q4, 1, 2>(R, m->mvt_smem, NT); o2 = mvt_set_smem_r<MK_Q4, 2, 2>(R, m->mvt_smem, NT); }
+    else o1 = o2 = mvt_set_smem_r<MK_Q4, 1, 4>(R, m->mvt_smem, NT);
   } else {
-    if (nbt == 1) { mvt_set_smem_r<MK_Q8, 1, 1>(R, m->mvt_smem); mvt_set_smem_r<MK_Q8, 2, 1>(R, m->mvt_smem); }
-    else if (nbt == 2) { mvt_set_smem_r<MK_Q8, 1, 2>(R, m->mvt_smem); mvt_set_smem_r<MK_Q8, 2, 2>(R, m->mvt_smem); }
-    else mvt_set_smem_r<MK_Q8, 1, 4>(R, m->mvt_smem);
+    if (nbt == 1) { o1 = mvt_set_smem_r<MK_Q8, 1, 1>(R, m->mvt_smem, NT); o2 = mvt_set_smem_r<MK_Q8, 2, 1>(R, m->mvt_smem, NT); }
+    else if (nbt == 2) { o1 = mvt_set_smem_r<MK_Q8, 1, 2>(R, m->mvt_smem, NT); o2 = mvt_set_smem_r<MK_Q8, 2, 2>(R, m->mvt_smem, NT); }
+    else o1 = o2 = mvt_set_smem_r<MK_Q8, 1, 4>(R, m->mvt_smem, NT);
   }
+  m->mvt_ctas[0] = o1;
+  m->mvt_ctas[1] = o2;
 }
 
 template <int KIND, int TT, int NBT, int R>
@@ -884,7 +924,7 @@ static int launch_mvt(const Matrix& m, int T, const float* x, int ldx, float* y,
                       const MvFuse& f, int* err, cudaStream_t s) {
   const int NT = ((m.nb + NBT - 1) / NBT + 31) & ~31;
   const int NU = m.rows_pad / R;
-  const int grid = std::max(1, std::min(NU, num_sms()));
+  const int grid = std::max(1, std::min(NU, m.mvt_ctas[TT - 1] * num_sms()));
   const MvdArgs a{m.data, m.scales, m.rows, m.rows_pad, m.cols, m.nb, T, x, ldx, y, ldy, mode,
                   m.mvt_stages, m.mvt_stage_bytes, err, f};
   TN_CHECK_CUDA(launch_pdl(k_mvt<KIND, TT, NBT, R>, dim3(grid), dim3(NT), (size_t)m.mvt_smem, s, a));

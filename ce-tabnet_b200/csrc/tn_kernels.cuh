@@ -26,6 +26,7 @@ struct Matrix {
   int occ[2] = {0, 0};      // resident CTAs per SM of the matvec launch shapes (1 and 2 tokens per tile)
   // decode matvec launch shape: rows per bulk-copied unit, ring depth, bytes
   int mvt_rows = 0, mvt_stages = 0, mvt_smem = 0;
+  int mvt_ctas[2] = {1, 1};  // resident CTAs per SM (1 and 2 tokens)
   uint32_t mvt_stage_bytes = 0;
 };
 
