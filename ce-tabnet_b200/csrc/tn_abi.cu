@@ -93,11 +93,7 @@ extern "C" int tn_matrix_matvec(const tn_matrix* m, int32_t n_tokens, const floa
   clear_error();
   TN_REQUIRE(m && d_x && d_y && n_tokens >= 0, TN_EINVAL, "tn_matrix_matvec: bad argument");
   DevSwitch g(m->device);
-  // one or two tokens: the bulk-copy decode kernel; more: the multi-token kernel
-  if (matvec_dec_ok(m->m, n_tokens) && (reinterpret_cast<uintptr_t>(d_x) & 15) == 0)
-    return matvec_dec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, MvFuse(), m->d_err,
-                      (cudaStream_t)stream);
-  return matvec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, (cudaStream_t)stream);
+  return matvec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, m->d_err, (cudaStream_t)stream);
 }
 
 extern "C" int tn_matrix_dequant(const tn_matrix* m, float* d_out, void* stream) {

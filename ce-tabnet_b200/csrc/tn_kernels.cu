@@ -66,42 +66,83 @@ __host__ __device__ __forceinline__ uint64_t dst_row(uint64_t r, int dst_off, in
   return (uint64_t)dst_off + h * hd + (j < half ? 2 * j : 2 * (j - half) + 1);
 }
 
-// block-aligned q4_0 / q8_0 source: one thread per (row, block)
-__global__ void k_repack_q(const uint8_t* __restrict__ src, int quant, int src_rows, int nb,
-                           int dst_off, int dst_stride, uint8_t* __restrict__ data,
-                           uint16_t* __restrict__ scales) {
-  const uint64_t total = (uint64_t)src_rows * nb;
-  const int bb = quant == TN_QUANT_Q8_0 ? 34 : 18, qb = bb - 2;
-  for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < total;
-       k += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t r = k / nb, b = k % nb;
-    const uint8_t* blk = src + k * bb;
-    const uint64_t dr = dst_row(r, dst_off, dst_stride);
-    uint8_t* dq = data + (dr * nb + b) * qb;
-    for (int j = 0; j < qb; j++) dq[j] = blk[2 + j];
-    scales[dr * nb + b] = (uint16_t)(blk[0] | (blk[1] << 8));
+// Source row that dst_row maps onto destination row d, or -1 if none of this
+// repack's rows lands there.
+__device__ __forceinline__ int64_t src_row_of(int64_t d, int dst_off, int dst_stride, int src_rows) {
+  const int64_t rel = d - dst_off;
+  if (rel < 0) return -1;
+  int64_t r;
+  if (dst_stride > 0) {
+    if (rel % dst_stride) return -1;
+    r = rel / dst_stride;
+  } else {
+    const int64_t hd = -dst_stride, half = hd / 2, h = rel / hd, j = rel % hd;
+    r = h * hd + ((j & 1) ? half + (j >> 1) : (j >> 1));
   }
+  return r < src_rows ? r : -1;
 }
 
-// same, for a 2-byte aligned source (every block then starts on an even
-// address): 16-bit loads, one or two 16-byte stores per block
-template <int QB>
-__global__ void k_repack_q16(const uint16_t* __restrict__ src, int src_rows, int nb, int dst_off,
-                             int dst_stride, uint4* __restrict__ data, uint16_t* __restrict__ scales) {
-  constexpr int BW = QB / 2 + 1;  // 16-bit words per block
-  const uint64_t total = (uint64_t)src_rows * nb;
+// Block-aligned q4_0 / q8_0 source into the fragment-ordered records: one
+// thread per (tile, g, pair) writes the 4 lane slots 4g .. 4g + 3 and the
+// scale words of rows g and g + 8.  Rows of the tile that another repack call
+// owns keep their bytes (read-modify-write; calls are stream ordered).
+template <int KIND>
+__global__ void k_repack_tile(const uint8_t* __restrict__ src, int src_rows, int nb, int pairs, int tiles,
+                              int dst_off, int dst_stride, uint8_t* __restrict__ data) {
+  constexpr int BB = KIND == MK_Q4 ? 18 : 34;
+  constexpr int AB = tile_a_bytes(KIND), REC = tile_rec_bytes(KIND), LB = AB / 32;
+  const uint64_t total = (uint64_t)tiles * 8 * pairs;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < total;
        k += (uint64_t)gridDim.x * blockDim.x) {
-    const uint64_t r = k / nb, b = k % nb;
-    const uint16_t* blk = src + k * BW;
-    const uint64_t dr = dst_row(r, dst_off, dst_stride);
-    uint32_t w[QB / 4];
+    const int p = (int)(k % pairs);
+    const uint64_t tg = k / pairs;
+    const int g = (int)(tg & 7);
+    const int64_t t = (int64_t)(tg >> 3);
+    const int64_t rs[2] = {src_row_of(t * 16 + g, dst_off, dst_stride, src_rows),
+                           src_row_of(t * 16 + g + 8, dst_off, dst_stride, src_rows)};
+    if (rs[0] < 0 && rs[1] < 0) continue;
+    const uint8_t* blk[2][2];  // [u = row g / g + 8][q]
 #pragma unroll
-    for (int j = 0; j < QB / 4; j++) w[j] = (uint32_t)blk[1 + 2 * j] | ((uint32_t)blk[2 + 2 * j] << 16);
-    uint4* dq = data + (dr * nb + b) * (QB / 16);
+    for (int u = 0; u < 2; u++)
 #pragma unroll
-    for (int v = 0; v < QB / 16; v++) dq[v] = make_uint4(w[4 * v], w[4 * v + 1], w[4 * v + 2], w[4 * v + 3]);
-    scales[dr * nb + b] = blk[0];
+      for (int q = 0; q < 2; q++)
+        blk[u][q] = (rs[u] >= 0 && 2 * p + q < nb) ? src + ((size_t)rs[u] * nb + 2 * p + q) * BB : nullptr;
+    uint8_t* rec = data + ((size_t)t * pairs + p) * REC;
+#pragma unroll
+    for (int c = 0; c < 4; c++) {
+      uint8_t* lane = rec + (4 * g + c) * LB;
+#pragma unroll
+      for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int q = 0; q < 2; q++)
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const int e = 16 * h + 4 * c + i;
+            if (KIND == MK_Q4) {
+              uint8_t* byte = lane + (2 * h + q) * 4 + i;
+              uint8_t v = *byte;
+              if (blk[0][q]) {
+                const uint8_t sb = blk[0][q][2 + (e >> 1)];
+                v = (uint8_t)((v & 0x0F) | ((((e & 1) ? sb >> 4 : sb & 15) ^ 8) << 4));
+              }
+              if (blk[1][q]) {
+                const uint8_t sb = blk[1][q][2 + (e >> 1)];
+                v = (uint8_t)((v & 0xF0) | (((e & 1) ? sb >> 4 : sb & 15) ^ 8));
+              }
+              *byte = v;
+            } else {
+#pragma unroll
+              for (int u = 0; u < 2; u++)
+                if (blk[u][q]) lane[(4 * h + 2 * q + u) * 4 + i] = blk[u][q][2 + e];
+            }
+          }
+    }
+    uint16_t* sc = reinterpret_cast<uint16_t*>(rec + AB);
+#pragma unroll
+    for (int q = 0; q < 2; q++)
+#pragma unroll
+      for (int u = 0; u < 2; u++)
+        if (blk[u][q]) sc[(2 * g + q) * 2 + u] = (uint16_t)(blk[u][q][0] | (blk[u][q][1] << 8));
   }
 }
 
@@ -124,7 +165,6 @@ __global__ void k_repack_plain(const uint8_t* __restrict__ src, int quant, int s
 }
 
 static void mv_prepare(Matrix* m);
-static void mvd_prepare(Matrix* m);
 
 int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
   TN_REQUIRE(rows > 0 && cols > 0, TN_EINVAL, "matrix: bad shape %d x %d", rows, cols);
@@ -139,19 +179,32 @@ int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
   else if (src_quant == TN_QUANT_Q8_0 && aligned) m->kind = MK_Q8;
   else if (src_quant == TN_QUANT_F16) m->kind = MK_F16;
   else m->kind = MK_F32;
-  const size_t dbytes = (size_t)m->rows_pad * m->nb * kind_block_bytes(m->kind);
-  const size_t sbytes = (m->kind == MK_Q4 || m->kind == MK_Q8) ? (size_t)m->rows_pad * m->nb * 2 : 0;
+  size_t dbytes;
+  if (m->kind == MK_Q4 || m->kind == MK_Q8) {
+    m->tiles = m->rows_pad / 16;
+    m->pairs = (m->nb + 1) / 2;
+    dbytes = (size_t)m->tiles * m->pairs * tile_rec_bytes(m->kind);
+  } else {
+    dbytes = (size_t)m->rows_pad * m->nb * kind_block_bytes(m->kind);
+  }
   TN_CHECK_CUDA(cudaMalloc(&m->data, dbytes));
   // zero padding rows/columns on the stream the repack kernels will use
   TN_CHECK_CUDA(cudaMemsetAsync(m->data, 0, dbytes, s));
-  if (sbytes) {
-    TN_CHECK_CUDA(cudaMalloc(&m->scales, sbytes));
-    TN_CHECK_CUDA(cudaMemsetAsync(m->scales, 0, sbytes, s));
-  }
-  m->bytes = dbytes + sbytes;
+  m->bytes = dbytes;
   num_sms();
-  mv_prepare(m);
-  mvd_prepare(m);
+  if (m->kind == MK_Q4 || m->kind == MK_Q8) {
+    const int rc = mm_prepare(m);
+    if (rc != TN_OK) return rc;
+    if (m->ws_floats) {
+      const size_t wsb = m->ws_floats * sizeof(float);
+      TN_CHECK_CUDA(cudaMalloc(&m->ws, wsb));
+      TN_CHECK_CUDA(cudaMalloc(&m->cnt, (size_t)m->tiles * sizeof(int)));
+      TN_CHECK_CUDA(cudaMemsetAsync(m->cnt, 0, (size_t)m->tiles * sizeof(int), s));
+      m->bytes += wsb + (size_t)m->tiles * sizeof(int);
+    }
+  } else {
+    mv_prepare(m);
+  }
   return TN_OK;
 }
 
@@ -161,18 +214,17 @@ int matrix_repack(Matrix* m, const uint8_t* d_src, int src_quant, int src_rows, 
              "matrix_repack: bad row stride %d", dst_stride);
   TN_REQUIRE(dst_off + (int64_t)(src_rows - 1) * (dst_stride > 0 ? dst_stride : 1) < m->rows, TN_EINVAL,
              "matrix_repack: rows out of range");
-  const int grid = std::min(148 * 32, (int)std::max<int64_t>(1, ((int64_t)src_rows * m->nb + 255) / 256));
-  const bool even = (reinterpret_cast<uintptr_t>(d_src) & 1) == 0;
-  if (m->kind == MK_Q4 && even) {
-    k_repack_q16<16><<<grid, 256, 0, s>>>((const uint16_t*)d_src, src_rows, m->nb, dst_off, dst_stride,
-                                          (uint4*)m->data, m->scales);
-  } else if (m->kind == MK_Q8 && even) {
-    k_repack_q16<32><<<grid, 256, 0, s>>>((const uint16_t*)d_src, src_rows, m->nb, dst_off, dst_stride,
-                                          (uint4*)m->data, m->scales);
-  } else if (m->kind == MK_Q4 || m->kind == MK_Q8) {
-    k_repack_q<<<grid, 256, 0, s>>>(d_src, src_quant, src_rows, m->nb, dst_off, dst_stride, m->data,
-                                    m->scales);
+  if (m->kind == MK_Q4 || m->kind == MK_Q8) {
+    const int64_t work = (int64_t)m->tiles * 8 * m->pairs;
+    const int grid = (int)std::min<int64_t>(148 * 32, std::max<int64_t>(1, (work + 255) / 256));
+    if (m->kind == MK_Q4)
+      k_repack_tile<MK_Q4><<<grid, 256, 0, s>>>(d_src, src_rows, m->nb, m->pairs, m->tiles, dst_off, dst_stride,
+                                                m->data);
+    else
+      k_repack_tile<MK_Q8><<<grid, 256, 0, s>>>(d_src, src_rows, m->nb, m->pairs, m->tiles, dst_off, dst_stride,
+                                                m->data);
   } else {
+    const int grid = std::min(148 * 32, (int)std::max<int64_t>(1, ((int64_t)src_rows * m->nb + 255) / 256));
     k_repack_plain<<<grid, 256, 0, s>>>(d_src, src_quant, src_rows, m->cols, m->cols_pad, dst_off,
                                         dst_stride, m->kind, m->data);
   }
@@ -182,51 +234,55 @@ int matrix_repack(Matrix* m, const uint8_t* d_src, int src_quant, int src_rows, 
 
 void matrix_free(Matrix* m) {
   if (m->data) cudaFree(m->data);
-  if (m->scales) cudaFree(m->scales);
+  if (m->ws) cudaFree(m->ws);
+  if (m->cnt) cudaFree(m->cnt);
   m->data = nullptr;
-  m->scales = nullptr;
+  m->ws = nullptr;
+  m->cnt = nullptr;
   m->bytes = 0;
 }
 
-// value of element (r, c) of a repacked matrix
-__device__ __forceinline__ float mat_elem(int kind, const uint8_t* data, const uint16_t* scales,
-                                          int nb, int cols_pad, uint64_t r, int c) {
-  if (kind == MK_F32) return ((const float*)data)[r * cols_pad + c];
-  if (kind == MK_F16) return f16_to_f32(((const uint16_t*)data)[r * cols_pad + c]);
-  const int b = c >> 5, j = c & 31;
-  const float d = f16_to_f32(scales[r * nb + b]);
-  if (kind == MK_Q8) return (float)(int8_t)data[(r * nb + b) * 32 + j] * d;
-  const uint8_t byte = data[(r * nb + b) * 16 + (j >> 1)];
-  return (float)(((j & 1) ? (byte >> 4) : (byte & 15)) - 8) * d;
+void matrix_reset_counters(const Matrix& m, cudaStream_t s) {
+  if (m.cnt) cudaMemsetAsync(m.cnt, 0, (size_t)m.tiles * sizeof(int), s);
 }
 
-__global__ void k_dequant(int kind, const uint8_t* data, const uint16_t* scales, int rows, int cols,
-                          int nb, int cols_pad, float* out) {
+// value of element (r, c) of a repacked matrix
+__device__ __forceinline__ float mat_elem(int kind, const uint8_t* data, int nb, int cols_pad, uint64_t r,
+                                          int c) {
+  if (kind == MK_F32) return ((const float*)data)[r * cols_pad + c];
+  if (kind == MK_F16) return f16_to_f32(((const uint16_t*)data)[r * cols_pad + c]);
+  const int pairs = (nb + 1) >> 1, rr = (int)(r & 15), g = rr & 7, u = rr >> 3;
+  const int b = c >> 5, e = c & 31, p = b >> 1, q = b & 1, h = e >> 4, cc = (e & 15) >> 2, i = e & 3;
+  const int ab = kind == MK_Q4 ? 512 : 1024;
+  const uint8_t* rec = data + ((r >> 4) * pairs + p) * (uint64_t)(ab + 64);
+  const float d = f16_to_f32(reinterpret_cast<const uint16_t*>(rec + ab)[(2 * g + q) * 2 + u]);
+  if (kind == MK_Q8) return (float)(int8_t)rec[(4 * g + cc) * 32 + (4 * h + 2 * q + u) * 4 + i] * d;
+  const uint8_t byte = rec[(4 * g + cc) * 16 + (2 * h + q) * 4 + i];
+  const int s = u ? (byte & 15) : (byte >> 4);
+  return (float)((s ^ 8) - 8) * d;
+}
+
+__global__ void k_dequant(int kind, const uint8_t* data, int rows, int cols, int nb, int cols_pad, float* out) {
   const uint64_t total = (uint64_t)rows * cols;
   for (uint64_t k = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; k < total;
        k += (uint64_t)gridDim.x * blockDim.x)
-    out[k] = mat_elem(kind, data, scales, nb, cols_pad, k / cols, (int)(k % cols));
+    out[k] = mat_elem(kind, data, nb, cols_pad, k / cols, (int)(k % cols));
 }
 
 int matrix_dequant(const Matrix& m, float* out, cudaStream_t s) {
   const int grid = std::min(148 * 32, (int)std::max<int64_t>(1, ((int64_t)m.rows * m.cols + 255) / 256));
-  k_dequant<<<grid, 256, 0, s>>>(m.kind, m.data, m.scales, m.rows, m.cols, m.nb, m.cols_pad, out);
+  k_dequant<<<grid, 256, 0, s>>>(m.kind, m.data, m.rows, m.cols, m.nb, m.cols_pad, out);
   TN_CHECK_LAUNCH();
   return TN_OK;
 }
 
-// ================================================================ matvec
-// CUDA-core dequant-matvec for few tokens (decode).  Each thread of a CTA
-// owns NBT 32-wide block columns of K and keeps x for them in registers; the
-// CTA walks a contiguous range of 8-row groups, streaming weights with 128-bit
-// loads (rows are contiguous in K, so a warp's loads are 512 contiguous bytes),
-// and reduces each group's 8 x TT partial dot products with a warp
-// reduce-scatter plus one shared-memory pass.
-//
-// q4_0 decode without integer->float conversions: a nibble n placed in bits
-// 16..19 of the float 0x3F000000 is 0.5 + n/256 (one PRMT), so per block
-//   sum_j (n_j - 8) x_j = 256 * sum_j f_j x_j - 136 * sum_j x_j
-// and sum_j x_j is computed once per x tile.
+// ================================================================ matvec (f16 / f32)
+// CUDA-core matvec of the row-major kinds (f16 / f32 tensors, and q4_0 /
+// q8_0 tensors whose rows straddle blocks, held dequantised).  Each thread of
+// a CTA owns NBT 32-wide block columns of K and keeps x for them in
+// registers; the CTA walks a contiguous range of 8-row groups, streaming
+// weights with 128-bit loads, and reduces each group's 8 x TT partial dot
+// products with a warp reduce-scatter plus one shared-memory pass.
 template <int KIND, int NBT>
 struct MvCfg {
   static constexpr int W = kind_block_bytes(KIND) / 4;  // 32-bit words per block
@@ -254,21 +310,11 @@ __device__ __forceinline__ float warp_reduce_scatter(float (&v)[N], int lane) {
   return r;
 }
 
-__device__ __forceinline__ float q4_f(uint32_t bytes4, int m) {
-  // byte m of bytes4 (a nibble value) into bits 16..23 of 0x3F000000
-  return __uint_as_float(__byte_perm(bytes4, 0x3F000000u, 0x7044u | ((uint32_t)m << 8)));
-}
-__device__ __forceinline__ float q8_f(uint32_t biased4, int m) {
-  // byte m of (q ^ 0x80) as the low byte of 0x4B000000 -> 2^23 + q + 128
-  return __uint_as_float(__byte_perm(biased4, 0x4B000000u, 0x7440u | (uint32_t)m));
-}
-
 template <int KIND, int TT, int NBT>
-__global__ void __launch_bounds__(512) k_matvec(const uint8_t* __restrict__ data,
-                                                const uint16_t* __restrict__ scales, int rows,
-                                                int rows_pad, int cols, int nb, int T,
-                                                const float* __restrict__ x, int ldx,
-                                                float* __restrict__ y, int ldy, int mode) {
+__global__ void __launch_bounds__(512) k_matvec(const uint8_t* __restrict__ data, int rows, int rows_pad,
+                                                int cols, int nb, int T, const float* __restrict__ x,
+                                                int ldx, float* __restrict__ y, int ldy, int mode) {
+  static_assert(KIND == MK_F16 || KIND == MK_F32, "row-major kinds only");
   using C = MvCfg<KIND, NBT>;
   constexpr int W = C::W, RG = C::RG, N = 8 * TT;
   constexpr int BB = kind_block_bytes(KIND);
@@ -281,14 +327,12 @@ __global__ void __launch_bounds__(512) k_matvec(const uint8_t* __restrict__ data
 
   for (int t0 = 0; t0 < T; t0 += TT) {
     float xr[TT][NBT][32];
-    float xs[TT][NBT];
 #pragma unroll
     for (int tt = 0; tt < TT; tt++)
 #pragma unroll
       for (int j = 0; j < NBT; j++) {
         const int b = tid + j * blockDim.x;
         const bool ok = b < nb && t0 + tt < T;
-        float s = 0.f;
 #pragma unroll
         for (int e = 0; e < 32; e += 4) {
           float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -308,9 +352,7 @@ __global__ void __launch_bounds__(512) k_matvec(const uint8_t* __restrict__ data
           xr[tt][j][e + 1] = v.y;
           xr[tt][j][e + 2] = v.z;
           xr[tt][j][e + 3] = v.w;
-          s += (v.x + v.y) + (v.z + v.w);
         }
-        xs[tt][j] = (KIND == MK_Q4) ? -136.f * s : s;
       }
 
     for (int g = g0; g < g1; g++) {
@@ -339,38 +381,12 @@ __global__ void __launch_bounds__(512) k_matvec(const uint8_t* __restrict__ data
                 w[i][4 * v + 3] = q.w;
               }
             }
-            float d[RG];
-            if (KIND == MK_Q4 || KIND == MK_Q8) {
-#pragma unroll
-              for (int i = 0; i < RG; i++)
-                d[i] = __half2float(__ushort_as_half(scales[(size_t)(g * 8 + rs + i) * nb + b]));
-            }
 #pragma unroll
             for (int i = 0; i < RG; i++) {
 #pragma unroll
               for (int tt = 0; tt < TT; tt++) {
                 float s = 0.f;
-                if (KIND == MK_Q4) {
-#pragma unroll
-                  for (int k = 0; k < 4; k++) {
-                    const uint32_t lo = w[i][k] & 0x0F0F0F0Fu, hi = (w[i][k] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-                    for (int m = 0; m < 4; m++) {
-                      s = fmaf(q4_f(lo, m), xr[tt][j][8 * k + 2 * m], s);
-                      s = fmaf(q4_f(hi, m), xr[tt][j][8 * k + 2 * m + 1], s);
-                    }
-                  }
-                  acc[rs + i][tt] = fmaf(d[i], fmaf(256.f, s, xs[tt][j]), acc[rs + i][tt]);
-                } else if (KIND == MK_Q8) {
-#pragma unroll
-                  for (int k = 0; k < 8; k++) {
-                    const uint32_t bq = w[i][k] ^ 0x80808080u;
-#pragma unroll
-                    for (int m = 0; m < 4; m++)
-                      s = fmaf(q8_f(bq, m) - 8388736.0f, xr[tt][j][4 * k + m], s);
-                  }
-                  acc[rs + i][tt] = fmaf(d[i], s, acc[rs + i][tt]);
-                } else if (KIND == MK_F16) {
+                if (KIND == MK_F16) {
 #pragma unroll
                   for (int k = 0; k < 16; k++) {
                     const __half2 h2 = *reinterpret_cast<const __half2*>(&w[i][k]);
@@ -446,8 +462,8 @@ static int launch_mv(const Matrix& m, int T, const float* x, int ldx, float* y, 
   const int G = m.rows_pad / 8;
   const int occ = m.occ[TT - 1] > 0 ? m.occ[TT - 1] : 1;
   const int grid = std::max(1, std::min(G, occ * num_sms()));
-  k_matvec<KIND, TT, NBT><<<grid, mv_threads<KIND, TT, NBT>(m), 0, s>>>(m.data, m.scales, m.rows, m.rows_pad,
-                                                                          m.cols, m.nb, T, x, ldx, y, ldy, mode);
+  k_matvec<KIND, TT, NBT><<<grid, mv_threads<KIND, TT, NBT>(m), 0, s>>>(m.data, m.rows, m.rows_pad, m.cols, m.nb,
+                                                                          T, x, ldx, y, ldy, mode);
   TN_CHECK_LAUNCH();
   return TN_OK;
 }
@@ -465,12 +481,8 @@ static void mv_prepare_kind(Matrix* m) {
 }
 
 static void mv_prepare(Matrix* m) {
-  switch (m->kind) {
-    case MK_Q4: mv_prepare_kind<MK_Q4>(m); break;
-    case MK_Q8: mv_prepare_kind<MK_Q8>(m); break;
-    case MK_F16: mv_prepare_kind<MK_F16>(m); break;
-    default: mv_prepare_kind<MK_F32>(m); break;
-  }
+  if (m->kind == MK_F16) mv_prepare_kind<MK_F16>(m);
+  else mv_prepare_kind<MK_F32>(m);
 }
 
 template <int KIND>
@@ -485,490 +497,16 @@ static int matvec_kind(const Matrix& m, int T, const float* x, int ldx, float* y
   return TN_EUNSUPPORTED;
 }
 
-int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
+int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, int* err,
            cudaStream_t s) {
   if (T <= 0) return TN_OK;
   if (mode == EPI_SWIGLU) TN_REQUIRE((m.rows & 1) == 0, TN_EINVAL, "swiglu needs paired rows");
   switch (m.kind) {
-    case MK_Q4: return matvec_kind<MK_Q4>(m, T, x, ldx, y, ldy, mode, s);
-    case MK_Q8: return matvec_kind<MK_Q8>(m, T, x, ldx, y, ldy, mode, s);
+    case MK_Q4:
+    case MK_Q8: return matvec_dec(m, T, x, ldx, y, ldy, mode, MvFuse(), err, s);
     case MK_F16: return matvec_kind<MK_F16>(m, T, x, ldx, y, ldy, mode, s);
     default: return matvec_kind<MK_F32>(m, T, x, ldx, y, ldy, mode, s);
   }
-}
-
-// ================================================================ decode matvec
-// Programmatic dependent launch: a kernel lets its successor start as soon as
-// every CTA of it is running, and the successor streams weights (which no
-// kernel writes) before it waits for its predecessor's results.
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-template <typename... KArgs, typename... Args>
-static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
-                              Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
-}
-
-// ---- mbarrier + bulk-copy (TMA) primitives
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: gives up after ~2 s (or when another thread of the CTA gave
-// up), raising the CTA's abort flag; callers then stop and report an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  const long long t0 = clock64();
-  for (uint32_t it = 0;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u) {
-      if (*abort_flag) return false;
-      if (clock64() - t0 > 4000000000ll) {
-        *abort_flag = 1;
-        return false;
-      }
-    }
-  }
-}
-// global -> shared bulk copy completing on an mbarrier (16-byte aligned, size % 16 == 0)
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                   smem_u32(dst)),
-               "l"(src), "r"(bytes), "r"(smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void consumer_sync(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-}
-
-struct MvdArgs {
-  const uint8_t* data;
-  const uint16_t* scales;
-  int rows, rows_pad, cols, nb, T;
-  const float* x;
-  int ldx;
-  float* y;
-  int ldy, mode;
-  int stages;       // shared-memory ring depth
-  uint32_t stage_bytes;
-  int* err;         // set to 1 if a bounded wait gave up
-  MvFuse f;
-};
-
-// epilogue of rows [row0, row0 + nrows), whose per-warp partials are in red
-template <int TT>
-__device__ __forceinline__ void mvd_epilogue(const MvdArgs& a, const float* red, int red_stride, int nw, int row0,
-                                             int nrows, int tid, int NT) {
-  for (int e = tid; e < nrows * TT; e += NT) {
-    const int r = e / TT, tt = e % TT, row = row0 + r;
-    if (row >= a.rows || tt >= a.T) continue;
-    const bool paired = (a.mode == EPI_SWIGLU || (a.mode == EPI_QKV_ROPE && row < a.f.q_dim + a.f.kv_dim));
-    if (paired && (row & 1)) continue;  // handled with its even partner
-    float s = 0.f, s2 = 0.f;
-    for (int w2 = 0; w2 < nw; w2++) {
-      s += red[w2 * red_stride + e];
-      if (paired) s2 += red[w2 * red_stride + e + TT];
-    }
-    if (a.mode == EPI_STORE || a.mode == EPI_RESID) {
-      float* py = a.y + (size_t)tt * a.ldy + row;
-      *py = a.mode == EPI_RESID ? *py + s : s;
-    } else if (a.mode == EPI_SWIGLU) {
-      a.y[(size_t)tt * a.ldy + (row >> 1)] = (s / (1.0f + expf(-s))) * s2;
-    } else {  // EPI_QKV_ROPE (web/inference-worker.js:528-540 and the KV push of :554)
-      const MvFuse& f = a.f;
-      const RowInfo ri = f.rinfo[tt];
-      if (row < f.q_dim + f.kv_dim) {
-        const bool isq = row < f.q_dim;
-        const int rr = isq ? row : row - f.q_dim, head = rr / f.hd, i = (rr % f.hd) >> 1, half = f.hd >> 1;
-        const double2 c = f.cs[(size_t)tt * half + i];
-        const double av = s, bv = s2;
-        const float o0 = (float)__dsub_rn(__dmul_rn(av, c.x), __dmul_rn(bv, c.y));
-        const float o1 = (float)__dadd_rn(__dmul_rn(av, c.y), __dmul_rn(bv, c.x));
-        float* dst = isq ? f.q_out + (size_t)tt * f.q_dim + head * f.hd
-                         : f.kc + ri.slot * f.slot_stride + head * f.kvh_stride + (size_t)ri.kv_idx * f.hd;
-        dst[i] = o0;
-        dst[half + i] = o1;
-      } else {
-        const int dv = row - f.q_dim - f.kv_dim;
-        f.vc[ri.slot * f.slot_stride + (dv / f.hd) * f.kvh_stride + (size_t)ri.kv_idx * f.hd + dv % f.hd] = s;
-      }
-    }
-  }
-}
-
-// CUDA-core dequant-matvec for decode (1-2 tokens), fed by TMA bulk copies.
-// A CTA owns a contiguous run of R-row units.  Thread 0 streams each unit's
-// weights and scales (two contiguous bulk copies) into a ring of shared-memory
-// stages guarded by full/empty mbarriers, refilling a stage as soon as every
-// warp has released it, so ~5 units per SM are always in flight.  All threads
-// consume: each owns NBT 32-wide block columns,
-// keep x for them in registers, decode q4_0 / q8_0 from shared memory and
-// reduce-scatter every unit's partial sums across the warp; one consumer
-// barrier per 64 rows precedes the cross-warp sum and the fused epilogue.
-//
-// q4_0 decode without integer->float conversions: a nibble n placed in bits
-// 16..19 of the float 0x3F000000 is 0.5 + n/256 (one PRMT), so per block
-//   sum_j (n_j - 8) x_j = 256 * sum_j f_j x_j - 136 * sum_j x_j
-// and sum_j x_j is computed once.
-// d0 += a0 * b0, d1 += a1 * b1 with one packed f32x2 FMA (sm_100)
-__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
-  asm("{\n .reg .b64 ra, rb, rc;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%0, %1};\n"
-      " fma.rn.f32x2 rc, ra, rb, rc;\n mov.b64 {%0, %1}, rc;\n}"
-      : "+f"(d0), "+f"(d1)
-      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
-}
-
-constexpr int kMvtMaxStages = 8;
-
-template <int KIND, int TT, int NBT, int R>
-__global__ void __launch_bounds__(256, NBT == 1 ? 2 : 1) k_mvt(const MvdArgs a) {
-  constexpr int BB = kind_block_bytes(KIND), W = BB / 4;
-  constexpr int NV = R * TT;                    // values reduced per unit
-  constexpr int LOGNV = NV == 2 ? 1 : (NV == 4 ? 2 : (NV == 8 ? 3 : (NV == 16 ? 4 : 5)));
-  constexpr int SH = 5 - LOGNV;
-  constexpr int CHU = 64 / R;                   // units per 64-row reduction chunk
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ float red[2][8][64 * TT];
-  __shared__ double nsum[8][TT];
-  __shared__ int released[kMvtMaxStages];       // warps done with each stage's current unit
-  __shared__ int last_unit[kMvtMaxStages];      // unit last issued into each stage
-  __shared__ volatile int abort_flag;
-  const int NT = blockDim.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = NT >> 5;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)a.stages * a.stage_bytes);
-  const int NU = a.rows_pad / R;
-  const int u0 = (int)((int64_t)NU * blockIdx.x / gridDim.x);
-  const int nu = (int)((int64_t)NU * (blockIdx.x + 1) / gridDim.x) - u0;
-  const uint32_t wbytes = (uint32_t)R * a.nb * BB, sbytes = (uint32_t)R * a.nb * 2;
-
-  if (tid == 0) {
-    abort_flag = 0;
-    for (int s = 0; s < a.stages; s++) {
-      mbar_init(&full[s], 1);
-      released[s] = 0;
-      last_unit[s] = -1;
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-
-  // issue unit k into its stage
-  auto produce = [&](int k) {
-    const int st = k % a.stages;
-    uint8_t* dst = smem + (size_t)st * a.stage_bytes;
-    const size_t row0 = (size_t)(u0 + k) * R;
-    last_unit[st] = k;
-    mbar_expect_tx(&full[st], wbytes + sbytes);
-    bulk_g2s(dst, a.data + row0 * a.nb * BB, wbytes, &full[st]);
-    bulk_g2s(dst + wbytes, a.scales + row0 * a.nb, sbytes, &full[st]);
-  };
-  if (tid == 0) {
-    // weights do not depend on the previous kernel: start streaming at once
-    for (int k = 0; k < nu && k < a.stages; k++) produce(k);
-  }
-
-  // ---------------- consumers
-  pdl_wait();  // x is produced by the predecessor kernel
-  float xr[TT][NBT][32];
-  float xs[TT][NBT];
-  double ss[TT];
-#pragma unroll
-  for (int tt = 0; tt < TT; tt++) {
-    ss[tt] = 0.0;
-    const bool tok = tt < a.T;
-    const float* xrow = a.x + (size_t)(a.f.rowsel && tok ? a.f.rowsel[tt] : tt) * a.ldx;
-#pragma unroll
-    for (int j = 0; j < NBT; j++) {
-      const int b = tid + j * NT;
-      const bool ok = tok && b < a.nb;
-#pragma unroll
-      for (int e = 0; e < 32; e += 4) {
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (ok) v = *reinterpret_cast<const float4*>(xrow + b * 32 + e);
-        xr[tt][j][e] = v.x;
-        xr[tt][j][e + 1] = v.y;
-        xr[tt][j][e + 2] = v.z;
-        xr[tt][j][e + 3] = v.w;
-        ss[tt] += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
-      }
-    }
-  }
-  if (a.f.norm_w) {
-    // RMSNorm (web/inference-worker.js:516-522): the consumers hold the whole row
-#pragma unroll
-    for (int tt = 0; tt < TT; tt++) {
-      double v = ss[tt];
-      for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0) nsum[warp][tt] = v;
-    }
-    consumer_sync(NT);
-#pragma unroll
-    for (int tt = 0; tt < TT; tt++) {
-      double tot = 0.0;
-      for (int w2 = 0; w2 < nw; w2++) tot += nsum[w2][tt];
-      const double inv = 1.0 / sqrt(tot / a.cols + 1e-5);
-#pragma unroll
-      for (int j = 0; j < NBT; j++) {
-        const int b = tid + j * NT;
-        if (b < a.nb) {
-#pragma unroll
-          for (int e = 0; e < 32; e++)
-            xr[tt][j][e] = (float)__dmul_rn(__dmul_rn((double)xr[tt][j][e], inv), (double)a.f.norm_w[b * 32 + e]);
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int tt = 0; tt < TT; tt++)
-#pragma unroll
-    for (int j = 0; j < NBT; j++) {
-      float s = 0.f;
-#pragma unroll
-      for (int e = 0; e < 32; e++) s += xr[tt][j][e];
-      xs[tt][j] = KIND == MK_Q4 ? -136.f * s : s;
-    }
-
-  // Every thread runs every iteration and barrier even after an abort (then
-  // it only skips the math), so no thread can be left waiting at bar.sync.
-  int rb = 0;
-  for (int k = 0; k < nu; k++) {
-    const int st = k % a.stages;
-    const bool ready = mbar_wait(&full[st], (k / a.stages) & 1, &abort_flag);
-    const uint8_t* wsm = smem + (size_t)st * a.stage_bytes;
-    const uint16_t* ssm = reinterpret_cast<const uint16_t*>(wsm + wbytes);
-    float acc[R][TT];
-#pragma unroll
-    for (int i = 0; i < R; i++) {
-#pragma unroll
-      for (int tt = 0; tt < TT; tt++) acc[i][tt] = 0.f;
-#pragma unroll
-      for (int j = 0; j < NBT; j++) {
-        const int b = tid + j * NT;
-        if (ready && b < a.nb) {
-          uint32_t w[W];
-#pragma unroll
-          for (int v = 0; v < W / 4; v++) {
-            const uint4 q = *reinterpret_cast<const uint4*>(wsm + ((size_t)i * a.nb + b) * BB + 16 * v);
-            w[4 * v] = q.x;
-            w[4 * v + 1] = q.y;
-            w[4 * v + 2] = q.z;
-            w[4 * v + 3] = q.w;
-          }
-          const float di = __half2float(__ushort_as_half(ssm[i * a.nb + b]));
-#pragma unroll
-          for (int tt = 0; tt < TT; tt++) {
-            // even / odd elements in the two halves of packed f32x2 FMAs
-            float s0 = 0.f, s1 = 0.f;
-            if constexpr (KIND == MK_Q4) {
-#pragma unroll
-              for (int kk = 0; kk < 4; kk++) {
-                const uint32_t lo = w[kk] & 0x0F0F0F0Fu, hi = (w[kk] >> 4) & 0x0F0F0F0Fu;
-#pragma unroll
-                for (int m = 0; m < 4; m++)
-                  ffma2(s0, s1, q4_f(lo, m), q4_f(hi, m), xr[tt][j][8 * kk + 2 * m], xr[tt][j][8 * kk + 2 * m + 1]);
-              }
-              acc[i][tt] = fmaf(di, fmaf(256.f, s0 + s1, xs[tt][j]), acc[i][tt]);
-            } else {
-#pragma unroll
-              for (int kk = 0; kk < 8; kk++) {
-                const uint32_t bq = w[kk] ^ 0x80808080u;
-                ffma2(s0, s1, q8_f(bq, 0) - 8388736.0f, q8_f(bq, 1) - 8388736.0f, xr[tt][j][4 * kk],
-                      xr[tt][j][4 * kk + 1]);
-                ffma2(s0, s1, q8_f(bq, 2) - 8388736.0f, q8_f(bq, 3) - 8388736.0f, xr[tt][j][4 * kk + 2],
-                      xr[tt][j][4 * kk + 3]);
-              }
-              acc[i][tt] = fmaf(di, s0 + s1, acc[i][tt]);
-            }
-          }
-        }
-      }
-    }
-    // this warp has read the stage: the last warp to release it refills it
-    // with the unit `stages` ahead (nobody waits for the slowest warp)
-    __syncwarp();
-    if (lane == 0) {
-      __threadfence_block();
-      if (atomicAdd(&released[st], 1) == nw - 1) {
-        __threadfence_block();
-        released[st] = 0;
-        const int kn = k + a.stages;
-        if (kn < nu && !abort_flag) {
-          // order every warp's reads of the stage before the copy that overwrites it
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          produce(kn);
-        }
-      }
-    }
-    float v[NV];
-#pragma unroll
-    for (int i = 0; i < R; i++)
-#pragma unroll
-      for (int tt = 0; tt < TT; tt++) v[i * TT + tt] = acc[i][tt];
-    const float r = warp_reduce_scatter<NV>(v, lane);
-    const int cu = k % CHU;
-    if ((lane & ((1 << SH) - 1)) == 0) red[rb][warp][cu * NV + (lane >> SH)] = r;
-    if (cu == CHU - 1 || k == nu - 1) {
-      consumer_sync(NT);
-      if (!abort_flag)
-        mvd_epilogue<TT>(a, &red[rb][0][0], 64 * TT, nw, (u0 + k - cu) * R, (cu + 1) * R, tid, NT);
-      rb ^= 1;
-    }
-  }
-  consumer_sync(NT);
-  if (tid == 0 && abort_flag) {
-    // no copy may still be landing when the CTA exits
-    for (int s = 0; s < a.stages; s++) {
-      const int j = last_unit[s];
-      if (j < 0) continue;
-      abort_flag = 0;
-      if (!mbar_wait(&full[s], (j / a.stages) & 1, &abort_flag)) break;
-    }
-    atomicExch(a.err, 1);
-  }
-}
-
-// ---- launch configuration of the decode matvec of one matrix
-static int mvt_nbt(int nb) { return nb <= 256 ? 1 : (nb <= 512 ? 2 : 4); }
-// One block column per thread: 2 CTAs per SM, ~24 KB stages in ~96 KB rings;
-// wider rows (more x registers per thread): 1 CTA per SM, ~48 KB stages.
-static int mvt_ctas_target(int nb) { return mvt_nbt(nb) == 1 ? 2 : 1; }
-static int mvt_rows(const Matrix& m) {  // R: rows per unit
-  const int bb = kind_block_bytes(m.kind) + 2;
-  const size_t cap = mvt_ctas_target(m.nb) == 2 ? 24576 : 49152;
-  int r = 16;
-  while (r > 2 && (size_t)r * m.nb * bb > cap) r >>= 1;
-  return r;
-}
-
-template <int KIND, int TT, int NBT, int R>
-static int mvt_occ(int threads, int smem) {
-  int o = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_mvt<KIND, TT, NBT, R>, threads, smem) != cudaSuccess)
-    o = 1;
-  return o < 1 ? 1 : o;
-}
-
-template <int KIND, int TT, int NBT, int R>
-static void mvt_set_smem(int bytes) {
-  cudaFuncSetAttribute(k_mvt<KIND, TT, NBT, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-}
-
-// sets the dynamic shared memory limit; returns resident CTAs per SM
-template <int KIND, int TT, int NBT>
-static int mvt_set_smem_r(int R, int bytes, int threads) {
-  switch (R) {
-    case 2: mvt_set_smem<KIND, TT, NBT, 2>(bytes); return mvt_occ<KIND, TT, NBT, 2>(threads, bytes);
-    case 4: mvt_set_smem<KIND, TT, NBT, 4>(bytes); return mvt_occ<KIND, TT, NBT, 4>(threads, bytes);
-    case 8: mvt_set_smem<KIND, TT, NBT, 8>(bytes); return mvt_occ<KIND, TT, NBT, 8>(threads, bytes);
-    default: mvt_set_smem<KIND, TT, NBT, 16>(bytes); return mvt_occ<KIND, TT, NBT, 16>(threads, bytes);
-  }
-}
-
-static void mvd_prepare(Matrix* m) {
-  if (!(m->kind == MK_Q4 || m->kind == MK_Q8) || m->nb > 1024) return;
-  const int R = mvt_rows(*m), nbt = mvt_nbt(m->nb);
-  // every unit's scale run must start on a 16-byte boundary and be a multiple
-  // of 16 bytes for the bulk copy (the weight run always is): else no decode kernel
-  if (((size_t)R * m->nb * 2) % 16 != 0) return;
-  const uint32_t stage = (uint32_t)(((size_t)R * m->nb * (kind_block_bytes(m->kind) + 2) + 127) & ~(size_t)127);
-  const size_t ring = mvt_ctas_target(m->nb) == 2 ? 96 * 1024 : 200 * 1024;
-  const int stages = (int)std::max<size_t>(2, std::min<size_t>(kMvtMaxStages, ring / stage));
-  m->mvt_rows = R;
-  m->mvt_stages = stages;
-  m->mvt_stage_bytes = stage;
-  m->mvt_smem = (int)(stages * stage + stages * sizeof(uint64_t));
-  const int NT = ((m->nb + nbt - 1) / nbt + 31) & ~31;
-  // (set once, outside any stream capture)
-  int o1 = 1, o2 = 1;
-  if (m->kind == MK_Q4) {
-    if (nbt == 1) { o1 = mvt_set_smem_r<MK_Q4, 1, 1>(R, m->mvt_smem, NT); o2 = mvt_set_smem_r<MK_Q4, 2, 1>(R, m->mvt_smem, NT); }
-    else if (nbt == 2) { o1 = mvt_set_smem_r<MK_Q4, 1, 2>(R, m->mvt_smem, NT); o2 = mvt_set_smem_r<MK_Q4, 2, 2>(R, m->mvt_smem, NT); }
-    else o1 = o2 = mvt_set_smem_r<MK_Q4, 1, 4>(R, m->mvt_smem, NT);
-  } else {
-    if (nbt == 1) { o1 = mvt_set_smem_r<MK_Q8, 1, 1>(R, m->mvt_smem, NT); o2 = mvt_set_smem_r<MK_Q8, 2, 1>(R, m->mvt_smem, NT); }
-    else if (nbt == 2) { o1 = mvt_set_smem_r<MK_Q8, 1, 2>(R, m->mvt_smem, NT); o2 = mvt_set_smem_r<MK_Q8, 2, 2>(R, m->mvt_smem, NT); }
-    else o1 = o2 = mvt_set_smem_r<MK_Q8, 1, 4>(R, m->mvt_smem, NT);
-  }
-  m->mvt_ctas[0] = o1;
-  m->mvt_ctas[1] = o2;
-}
-
-template <int KIND, int TT, int NBT, int R>
-static int launch_mvt(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
-                      const MvFuse& f, int* err, cudaStream_t s) {
-  const int NT = ((m.nb + NBT - 1) / NBT + 31) & ~31;
-  const int NU = m.rows_pad / R;
-  const int grid = std::max(1, std::min(NU, m.mvt_ctas[TT - 1] * num_sms()));
-  const MvdArgs a{m.data, m.scales, m.rows, m.rows_pad, m.cols, m.nb, T, x, ldx, y, ldy, mode,
-                  m.mvt_stages, m.mvt_stage_bytes, err, f};
-  TN_CHECK_CUDA(launch_pdl(k_mvt<KIND, TT, NBT, R>, dim3(grid), dim3(NT), (size_t)m.mvt_smem, s, a));
-  return TN_OK;
-}
-
-template <int KIND, int TT, int NBT>
-static int launch_mvt_r(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
-                        const MvFuse& f, int* err, cudaStream_t s) {
-  switch (m.mvt_rows) {
-    case 2: return launch_mvt<KIND, TT, NBT, 2>(m, T, x, ldx, y, ldy, mode, f, err, s);
-    case 4: return launch_mvt<KIND, TT, NBT, 4>(m, T, x, ldx, y, ldy, mode, f, err, s);
-    case 8: return launch_mvt<KIND, TT, NBT, 8>(m, T, x, ldx, y, ldy, mode, f, err, s);
-    default: return launch_mvt<KIND, TT, NBT, 16>(m, T, x, ldx, y, ldy, mode, f, err, s);
-  }
-}
-
-bool matvec_dec_ok(const Matrix& m, int T) {
-  if (!(m.kind == MK_Q4 || m.kind == MK_Q8) || m.nb > 1024 || T < 1 || m.mvt_rows == 0) return false;
-  return T <= (mvt_nbt(m.nb) <= 2 ? 2 : 1);
-}
-
-template <int KIND>
-static int matvec_dec_kind(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
-                           const MvFuse& f, int* err, cudaStream_t s) {
-  switch (mvt_nbt(m.nb)) {
-    case 1: return T == 1 ? launch_mvt_r<KIND, 1, 1>(m, T, x, ldx, y, ldy, mode, f, err, s)
-                          : launch_mvt_r<KIND, 2, 1>(m, T, x, ldx, y, ldy, mode, f, err, s);
-    case 2: return T == 1 ? launch_mvt_r<KIND, 1, 2>(m, T, x, ldx, y, ldy, mode, f, err, s)
-                          : launch_mvt_r<KIND, 2, 2>(m, T, x, ldx, y, ldy, mode, f, err, s);
-    default: return launch_mvt_r<KIND, 1, 4>(m, T, x, ldx, y, ldy, mode, f, err, s);
-  }
-}
-
-int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
-               int* err, cudaStream_t s) {
-  TN_REQUIRE(matvec_dec_ok(m, T), TN_EUNSUPPORTED, "matvec_dec: %d tokens of kind %d, %d columns", T, m.kind,
-             m.cols);
-  TN_REQUIRE((ldx & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0, TN_EINVAL,
-             "matvec_dec: x rows must be 16-byte aligned");
-  TN_REQUIRE(mode != EPI_SWIGLU || (m.rows & 1) == 0, TN_EINVAL, "swiglu needs paired rows");
-  TN_REQUIRE(err, TN_EINVAL, "matvec_dec: error flag required");
-  if (m.kind == MK_Q4) return matvec_dec_kind<MK_Q4>(m, T, x, ldx, y, ldy, mode, f, err, s);
-  return matvec_dec_kind<MK_Q8>(m, T, x, ldx, y, ldy, mode, f, err, s);
 }
 
 // ================================================================ rmsnorm
@@ -1009,22 +547,20 @@ int rmsnorm(const float* h, int ldh, const int* rowsel, const float* w, float* o
 
 // ================================================================ embed
 // embedLookup (web/inference-worker.js:509-515) from the repacked embed table
-__global__ void k_embed(int kind, const uint8_t* data, const uint16_t* scales, int vocab, int H, int nb,
-                        int cols_pad, const int* __restrict__ ids, float* __restrict__ out, int ldo,
-                        int* err) {
+__global__ void k_embed(int kind, const uint8_t* data, int vocab, int H, int nb, int cols_pad,
+                        const int* __restrict__ ids, float* __restrict__ out, int ldo, int* err) {
   const int t = blockIdx.x;
   const int id = ids[t];
   const bool ok = id >= 0 && id < vocab;
   if (!ok && threadIdx.x == 0) atomicExch(err, 1);
   for (int c = threadIdx.x; c < H; c += blockDim.x)
-    out[(size_t)t * ldo + c] = ok ? mat_elem(kind, data, scales, nb, cols_pad, (uint64_t)id, c) : 0.f;
+    out[(size_t)t * ldo + c] = ok ? mat_elem(kind, data, nb, cols_pad, (uint64_t)id, c) : 0.f;
 }
 
 int embed_rows(const Matrix& emb, const int* ids, int T, float* out, int ldo, int* d_err,
                cudaStream_t s) {
   if (T <= 0) return TN_OK;
-  k_embed<<<T, 256, 0, s>>>(emb.kind, emb.data, emb.scales, emb.rows, emb.cols, emb.nb, emb.cols_pad,
-                            ids, out, ldo, d_err);
+  k_embed<<<T, 256, 0, s>>>(emb.kind, emb.data, emb.rows, emb.cols, emb.nb, emb.cols_pad, ids, out, ldo, d_err);
   TN_CHECK_LAUNCH();
   return TN_OK;
 }

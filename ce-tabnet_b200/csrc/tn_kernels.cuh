@@ -6,36 +6,64 @@
 namespace tn {
 
 // Device layouts of a [rows x cols] weight matrix after the init-time repack.
-//   MK_Q4 : data [rows_pad][nb][16 B]  nibbles in reference order (byte j = elems 2j, 2j+1)
-//   MK_Q8 : data [rows_pad][nb][32 B]  int8
+//   MK_Q4 / MK_Q8: tensor-core fragment order.  Rows are cut into tiles of 16
+//           and the 32-element blocks of a row into pairs (2p, 2p + 1); every
+//           (tile, pair) is one record of tile_a_bytes(kind) weight bytes plus
+//           64 bytes of fp16 scales, tiles major, pairs minor.  Within a record,
+//           lane l = 4 g + c (g = 0..7, c = 0..3) owns 16 (q4) / 32 (q8)
+//           contiguous bytes: exactly the A operands of the two
+//           mma.m16n8k32 (half h = 0, 1) that cover rows g and g + 8 of the
+//           tile, A columns 0..15 being elements 16 h .. 16 h + 15 of block 2p
+//           and columns 16..31 the same elements of block 2p + 1.
+//             q4: word 2h + q, byte i = (s(row g) << 4) | s(row g + 8) for
+//                 element 16 h + 4 c + i of block 2p + q, where s = nibble ^ 8
+//                 is the weight's (n - 8) as a 4-bit two's complement value;
+//             q8: word 4h + 2q + u, byte i = q8 value of row g + 8u, same element.
+//           Scales: u32 (2 g + q) of the scale area = (row g, row g + 8) of block 2p + q.
+//           Padding rows and blocks are zero, i.e. weight 0.
 //   MK_F16: data [rows_pad][cols_pad]  fp16 bits (zero padded)
 //   MK_F32: data [rows_pad][cols_pad]  f32 (zero padded); also holds exactly dequantised
 //           q4_0/q8_0 tensors whose rows do not start on a block boundary
-//   scales (MK_Q4 / MK_Q8): [rows_pad][nb] fp16 bits, so R consecutive rows are
-//           one contiguous run of the data plane plus one of the scale plane
 //   rows_pad is a multiple of 16.
 enum MatKind { MK_Q4 = 0, MK_Q8 = 1, MK_F16 = 2, MK_F32 = 3 };
+
+__host__ __device__ constexpr int tile_a_bytes(int k) { return k == MK_Q4 ? 512 : 1024; }
+__host__ __device__ constexpr int tile_rec_bytes(int k) { return tile_a_bytes(k) + 64; }
+
+// Launch shape of the tensor-core matvec for one token count (1 or 2): K is
+// cut into ks chunks of ckp block pairs (a chunk's activation digits fill one
+// shared-memory table), a chunk into nsc sub-chunks of scp pairs (one
+// shared-memory stage each).
+struct MmShape {
+  int ks = 0, ckp = 0, nsc = 0, scp = 0;
+  int stages = 0, smem = 0, ctas = 1;  // ring depth, dynamic shared memory, resident CTAs per SM
+  uint32_t stage_bytes = 0;
+};
 
 struct Matrix {
   int kind = MK_F32;
   int rows = 0, cols = 0;
   int rows_pad = 0, cols_pad = 0, nb = 0;
+  int tiles = 0, pairs = 0;  // MK_Q4 / MK_Q8 record grid
   uint8_t* data = nullptr;
-  uint16_t* scales = nullptr;
   size_t bytes = 0;
-  int occ[2] = {0, 0};      // resident CTAs per SM of the matvec launch shapes (1 and 2 tokens per tile)
-  // decode matvec launch shape: rows per bulk-copied unit, ring depth, bytes
-  int mvt_rows = 0, mvt_stages = 0, mvt_smem = 0;
-  int mvt_ctas[2] = {1, 1};  // resident CTAs per SM (1 and 2 tokens)
-  uint32_t mvt_stage_bytes = 0;
+  int occ[2] = {0, 0};       // resident CTAs per SM of the CUDA-core matvec (MK_F16 / MK_F32)
+  MmShape mm[2];             // tensor-core matvec (MK_Q4 / MK_Q8), 1 and 2 tokens
+  // cross-CTA partial sums [chunk][tile][part 0 / 1][32] and per-tile arrival
+  // counters (zero between launches: the CTA that completes a tile resets it)
+  size_t ws_floats = 0;
+  float* ws = nullptr;
+  int* cnt = nullptr;
 };
 
-// bytes per 32-element block of the data plane
+// bytes per 32-element block of the data plane (row-major kinds)
 __host__ __device__ constexpr int kind_block_bytes(int k) {
   return k == MK_Q4 ? 16 : (k == MK_Q8 ? 32 : (k == MK_F16 ? 64 : 128));
 }
 
 int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s);
+// launch shape of the tensor-core matvec of a q4_0 / q8_0 matrix (at allocation)
+int mm_prepare(Matrix* m);
 // Repack src_rows rows of a packed tensor (device memory, reference layout,
 // `cols` columns) into rows dst_off + r * dst_stride of m.
 int matrix_repack(Matrix* m, const uint8_t* d_src, int src_quant, int src_rows, int dst_off,
@@ -46,7 +74,8 @@ int matrix_dequant(const Matrix& m, float* out, cudaStream_t s);
 enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV_ROPE = 3 };
 // y = W x for T tokens.  STORE: y[t*ldy + r] = v.  RESID: y[t*ldy + r] += v.
 // SWIGLU: rows (2i, 2i+1) hold (gate_i, up_i); y[t*ldy + i] = silu(gate) * up.
-int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
+// err: device int set to 1 if a bounded wait inside a kernel gave up.
+int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, int* err,
            cudaStream_t s);
 
 // per-row bookkeeping of a step: KV slot, RoPE position, KV write index, attention length
@@ -75,11 +104,13 @@ struct MvFuse {
   size_t slot_stride = 0, kvh_stride = 0;
   int q_dim = 0, kv_dim = 0, hd = 0;
 };
-// the decode matvec handles up to 2 tokens of q4_0 / q8_0 matrices
+// the fused decode matvec handles q4_0 / q8_0 matrices; tokens are taken two at a time
 bool matvec_dec_ok(const Matrix& m, int T);
 // err: device int set to 1 if a bounded wait inside the kernel gave up
 int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
                int* err, cudaStream_t s);
+// zero the split-K arrival counters (after a launch gave up part way)
+void matrix_reset_counters(const Matrix& m, cudaStream_t s);
 // split-K decode attention with the split merge done by the last CTA of each
 // (row, KV head); counters: T * nKV ints, zero between calls
 int attention_dec(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,

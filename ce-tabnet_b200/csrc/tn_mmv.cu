@@ -1,0 +1,814 @@
+// tn_mmv.cu -- tensor-core dequant-matvec of q4_0 / q8_0 matrices (decode).
+//
+// The matvec of web/inference-worker.js:523-527 / :545-552 / :567-583
+// (dequantised weight rows dotted with an f32 activation row), with the
+// weights kept in their 4.5 / 8.5-bit form and the products formed by
+// mma.sync m16n8k32 s8 x s8 -> s32 tensor-core instructions:
+//
+//   A (weights): 16 rows x 32 columns per instruction, the columns being 16
+//     elements of block 2p and the same 16 elements of block 2p + 1.  A q4_0
+//     weight (n - 8) is stored as the 4-bit two's complement n ^ 8, so
+//     masking a byte's high nibble (or shifting the low one up) yields
+//     16 (n - 8) as an s8 with one LOP3 / SHF per four weights.  q8_0 bytes
+//     are the A operands as stored.
+//   B (activations): an f32 row x is scaled by 2^s per chunk of K so its
+//     largest magnitude lies in [2^26, 2^27), rounded to the integer X and
+//     split into four base-128 digits X = d0 + 2^7 d1 + 2^14 d2 + 2^21 d3
+//     (d0..d2 in [0, 127], d3 signed), one B column per digit.  With one
+//     token the 8 columns are (block parity, digit); with two tokens each
+//     block parity gets its own instruction and the columns are (token, digit).
+//   C starts at the bit pattern of 1.5 * 2^23: every per-block column sum
+//   |S| < 2^19, so the s32 result read as f32 is exactly 1.5 * 2^23 + S and
+//   one FADD recovers S without an integer->float conversion.  S times the
+//   block's fp16 scale is accumulated in f32 per (row, column); the digit
+//   columns are recombined (x 2^(7 digit)) and scaled back by 2^-s when a
+//   tile is done.  The only rounding against an f32 dot product is that of
+//   x to 27 bits relative to its chunk maximum.
+//
+// Work split: K is cut into chunks of up to 8192 elements (one token; 4096
+// for two) whose activation digits fill a 33 KB shared-memory table built by
+// every CTA when it enters the chunk; a chunk of a 16-row tile into
+// sub-chunks of up to 32 (q4) / 16 (q8) block pairs, one ring stage each.
+// Units (chunk, tile, sub-chunk) are handed out in contiguous runs per CTA,
+// so a tile's chunk is usually summed inside one CTA.  A producer warp
+// streams each unit's records (one contiguous bulk copy) into the ring (full /
+// empty mbarriers; a stage is handed back as soon as the consumers hold its
+// operands in registers); eight consumer warps split every unit's pairs,
+// accumulate a tile's chunk in registers and hand the per-warp row sums to an
+// epilogue warp through mbarrier-guarded buffers.  The epilogue warp sums the
+// eight warps in fixed order; a tile whose chunk is whole in this CTA and the
+// only chunk is final at once (fused epilogue: store / residual add / SwiGLU /
+// RoPE + KV append); other pieces go to a workspace, arrivals are counted per
+// tile with release-atomics (batched over four pieces), and the arrival that
+// completes a tile sums its pieces in (chunk, part) order -- deterministic --
+// and runs the fused epilogue.
+#include <cfloat>
+#include <type_traits>
+
+#include "tn_kernels.cuh"
+
+namespace tn {
+
+// Programmatic dependent launch: a kernel lets its successor start as soon as
+// every CTA of it is running, and the successor streams weights (which no
+// kernel writes) before it waits for its predecessor's results.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+// ---- mbarrier + bulk-copy primitives
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Test for completion of the phase with `parity`; a thread whose phase is
+// still open is suspended (it issues nothing) until the phase completes or
+// about 1 ms passes, so waiting warps leave the issue slots to working ones.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: gives up after ~2 s (or when another thread of the CTA gave
+// up), raising the CTA's abort flag; callers then stop and report an error.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > 4000000000ll) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+// global -> shared bulk copy completing on an mbarrier (16-byte aligned, size % 16 == 0)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void consumer_sync(int nthreads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+}
+__device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ float ld_relaxed(const float* p) {
+  float v;
+  asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// d += A B for one m16n8k32 s8 tile (A row-major 16 x 32, B column-major 32 x 8)
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 2^n as an exact float, |n| <= 126
+__device__ __forceinline__ float exp2i(int n) { return __int_as_float((n + 127) << 23); }
+
+constexpr int MMV_NW = 8;                              // consumer warps
+constexpr int MMV_NE = 1;                              // epilogue warps
+constexpr int MMV_UB = 4;                              // pieces per epilogue batch
+constexpr int MMV_NB = MMV_NE * MMV_UB;                // partial-sum buffers
+constexpr int MMV_THREADS = (MMV_NW + MMV_NE + 1) * 32;  // + one producer warp
+constexpr int MMV_MAX_STAGES = 12;
+constexpr int MMV_MAX_SMEM = 200 * 1024;
+constexpr int MMV_CE = 8192;                           // activation elements (x tokens) per K chunk
+constexpr int kMagic = 0x4B400000;                     // bits of 1.5 * 2^23
+constexpr float kMagicF = 12582912.0f;
+// most block pairs per sub-chunk (one ring stage)
+__host__ __device__ constexpr int mmv_sc(int kind) { return kind == MK_Q4 ? 32 : 16; }
+
+struct MmvArgs {
+  const uint8_t* data;
+  int rows, tiles, pairs, cols, T;
+  const float* x;
+  int ldx;
+  float* y;
+  int ldy, mode;
+  int ks, ckp, nsc, scp, stages;
+  uint32_t stage_bytes;
+  int* err;
+  int* cnt;
+  float* ws;
+  MvFuse f;
+};
+
+// final value v of (row, token tt); partner = value of row ^ 1 of the same token
+__device__ __forceinline__ void mmv_store(const MmvArgs& a, int row, int tt, float v, float partner) {
+  if (a.mode == EPI_STORE) {
+    a.y[(size_t)tt * a.ldy + row] = v;
+  } else if (a.mode == EPI_RESID) {
+    float* py = a.y + (size_t)tt * a.ldy + row;
+    *py = *py + v;
+  } else if (a.mode == EPI_SWIGLU) {
+    // rows (2i, 2i + 1) = (gate_i, up_i), web/inference-worker.js:567-577
+    if (!(row & 1)) a.y[(size_t)tt * a.ldy + (row >> 1)] = (v / (1.0f + expf(-v))) * partner;
+  } else {  // EPI_QKV_ROPE (web/inference-worker.js:528-540 and the KV push of :554)
+    const MvFuse& f = a.f;
+    const RowInfo ri = f.rinfo[tt];
+    if (row < f.q_dim + f.kv_dim) {
+      if (row & 1) return;  // handled with its even partner
+      const bool isq = row < f.q_dim;
+      const int rr = isq ? row : row - f.q_dim, head = rr / f.hd, i = (rr % f.hd) >> 1, half = f.hd >> 1;
+      const double2 c = f.cs[(size_t)tt * half + i];
+      const double av = v, bv = partner;
+      const float o0 = (float)__dsub_rn(__dmul_rn(av, c.x), __dmul_rn(bv, c.y));
+      const float o1 = (float)__dadd_rn(__dmul_rn(av, c.y), __dmul_rn(bv, c.x));
+      float* dst = isq ? f.q_out + (size_t)tt * f.q_dim + head * f.hd
+                       : f.kc + ri.slot * f.slot_stride + head * f.kvh_stride + (size_t)ri.kv_idx * f.hd;
+      dst[i] = o0;
+      dst[half + i] = o1;
+    } else {
+      const int dv = row - f.q_dim - f.kv_dim;
+      f.vc[ri.slot * f.slot_stride + (dv / f.hd) * f.kvh_stride + (size_t)ri.kv_idx * f.hd + dv % f.hd] = v;
+    }
+  }
+}
+
+// position (chunk, tile, sub-chunk) of a unit, advanced without divisions
+struct UnitPos {
+  int kc, t, sc;
+  __device__ __forceinline__ UnitPos(int u, int per_chunk, int nsc) {
+    kc = u / per_chunk;
+    const int r = u - kc * per_chunk;
+    t = r / nsc;
+    sc = r - t * nsc;
+  }
+  __device__ __forceinline__ void next(int nsc, int tiles) {
+    if (++sc == nsc) {
+      sc = 0;
+      if (++t == tiles) {
+        t = 0;
+        ++kc;
+      }
+    }
+  }
+};
+
+// Units are (tile t, K chunk kc, sub-chunk sc), chunk major then tile major,
+// u = (kc * tiles + t) * nsc + sc, in contiguous runs per CTA; a run holds at
+// least nsc units, so the sub-chunks of one (tile, chunk) fall into at most
+// two runs ("pieces": part 0 starts at sc = 0, part 1 after a run boundary).
+template <int KIND, int TT>
+__global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
+  constexpr int AB = tile_a_bytes(KIND), REC = tile_rec_bytes(KIND);
+  constexpr int SC = mmv_sc(KIND), PPW = SC / MMV_NW, NV = 16 * TT, NC = MMV_NW * 32;
+  constexpr int CP = MMV_CE / TT / 64;     // most pairs per chunk
+  constexpr int DS = CP * 16 + 8;          // words per digit plane (skewed against bank conflicts)
+  constexpr int NG = MMV_CE / TT / 4 / NC; // 4-element groups per consumer thread and token
+  constexpr int ZERO = TT * 4 * DS;        // two zero words after the planes
+  constexpr unsigned FULL = 0xffffffffu;
+  extern __shared__ __align__(128) uint8_t ring[];
+  // digit planes of the current chunk: word ((tt*4 + digit)*DS + ((p*2 + q)*4 + c)*2 + h)
+  // holds that digit of elements 16h + 4c .. 16h + 4c + 3 of block 2p + q
+  __shared__ __align__(16) uint32_t planes[TT * 4 * DS + 2];
+  __shared__ float red[MMV_NB][MMV_NW][NV];
+  __shared__ __align__(8) uint64_t full[MMV_MAX_STAGES];
+  __shared__ __align__(8) uint64_t empty[MMV_MAX_STAGES];
+  __shared__ __align__(8) uint64_t red_full[MMV_NB];
+  __shared__ __align__(8) uint64_t red_empty[MMV_NB];
+  __shared__ int last_unit[MMV_MAX_STAGES];
+  __shared__ double sred[MMV_NW][TT];
+  __shared__ float mred[MMV_NW][TT];
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int NSU = a.tiles * a.nsc;  // units per chunk
+  const int NU = a.ks * NSU;
+  const int u0 = (int)((int64_t)NU * blockIdx.x / gridDim.x);
+  const int nu = (int)((int64_t)NU * (blockIdx.x + 1) / gridDim.x) - u0;
+
+  if (tid == 0) {
+    abort_flag = 0;
+    planes[ZERO] = 0u;
+    planes[ZERO + 1] = 0u;
+    for (int s = 0; s < a.stages; s++) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], MMV_NW);
+      last_unit[s] = -1;
+    }
+    for (int b = 0; b < MMV_NB; b++) {
+      mbar_init(&red_full[b], MMV_NW);
+      mbar_init(&red_empty[b], 1);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == MMV_NW + MMV_NE) {
+    // ======================= producer: one bulk copy per unit into the ring
+    // (weights do not depend on the previous kernel: no wait for it)
+    if (lane == 0) {
+      UnitPos up(u0, NSU, a.nsc);
+      for (int k = 0; k < nu; k++, up.next(a.nsc, a.tiles)) {
+        const int st = k % a.stages;
+        if (k >= a.stages) {
+          // every consumer warp has read the unit this stage held
+          if (!mbar_wait(&empty[st], ((k / a.stages) - 1) & 1, &abort_flag)) break;
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        }
+        if (abort_flag) break;
+        const int kc = up.kc, t = up.t, first = up.sc * a.scp;
+        const int n = max(0, min(a.scp, min(a.ckp, a.pairs - kc * a.ckp) - first));
+        const uint32_t bytes = (uint32_t)n * REC;
+        last_unit[st] = k;
+        mbar_expect_tx(&full[st], bytes);  // an empty sub-chunk completes on this arrival alone
+        if (bytes)
+          bulk_g2s(ring + (size_t)st * a.stage_bytes,
+                   a.data + ((size_t)t * a.pairs + (size_t)kc * a.ckp + first) * REC, bytes, &full[st]);
+      }
+    }
+  } else if (warp < MMV_NW) {
+    // ======================= consumers
+    const int g = lane >> 2, c = lane & 3;
+    pdl_wait();  // x is produced by the predecessor kernel
+    const float* xrow[TT];
+    bool xvec = true;
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++) {
+      xrow[tt] = a.x + (size_t)(tt < a.T ? (a.f.rowsel ? a.f.rowsel[tt] : tt) : 0) * a.ldx;
+      xvec = xvec && (reinterpret_cast<uintptr_t>(xrow[tt]) & 15) == 0;
+    }
+    const bool wvec = a.f.norm_w == nullptr || (reinterpret_cast<uintptr_t>(a.f.norm_w) & 15) == 0;
+
+    // RMSNorm factor over the whole row (web/inference-worker.js:516-522)
+    double inv[TT];
+#pragma unroll
+    for (int tt = 0; tt < TT; tt++) inv[tt] = 1.0;
+    if (a.f.norm_w) {
+#pragma unroll
+      for (int tt = 0; tt < TT; tt++) {
+        double ss = 0.0;
+        if (tt < a.T) {
+          if (xvec) {
+            for (int i = 4 * tid; i < a.cols; i += 4 * NC) {
+              const float4 v = *reinterpret_cast<const float4*>(xrow[tt] + i);
+              ss = fma((double)v.x, (double)v.x, ss);
+              ss = fma((double)v.y, (double)v.y, ss);
+              ss = fma((double)v.z, (double)v.z, ss);
+              ss = fma((double)v.w, (double)v.w, ss);
+            }
+          } else {
+            for (int i = tid; i < a.cols; i += NC) {
+              const double v = xrow[tt][i];
+              ss = fma(v, v, ss);
+            }
+          }
+        }
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
+        if (lane == 0) sred[warp][tt] = ss;
+      }
+      consumer_sync(NC);
+#pragma unroll
+      for (int tt = 0; tt < TT; tt++) {
+        double tot = 0.0;
+        for (int w = 0; w < MMV_NW; w++) tot += sred[w][tt];
+        inv[tt] = 1.0 / sqrt(tot / a.cols + 1e-5);
+      }
+    }
+
+    float fa[TT], fb[TT];
+    // digits of chunk kc into the planes
+    auto setup = [&](int kc) {
+      const int e0 = kc * a.ckp * 64, ce = min(a.ckp, a.pairs - kc * a.ckp) * 64;
+      float v[TT][NG][4];
+      // all loads first (x, then the norm weights), 16 bytes at a time
+#pragma unroll
+      for (int tt = 0; tt < TT; tt++)
+#pragma unroll
+        for (int i = 0; i < NG; i++) {
+          const int el = 4 * (tid + i * NC), col = e0 + el;
+          float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (tt < a.T && el < ce && col < a.cols) {  // col % 4 == 0 and cols % 32 == 0
+            if (xvec) {
+              xv = *reinterpret_cast<const float4*>(xrow[tt] + col);
+            } else {
+              xv.x = xrow[tt][col];
+              xv.y = xrow[tt][col + 1];
+              xv.z = xrow[tt][col + 2];
+              xv.w = xrow[tt][col + 3];
+            }
+          }
+          v[tt][i][0] = xv.x;
+          v[tt][i][1] = xv.y;
+          v[tt][i][2] = xv.z;
+          v[tt][i][3] = xv.w;
+        }
+      if (a.f.norm_w) {
+#pragma unroll
+        for (int i = 0; i < NG; i++) {
+          const int el = 4 * (tid + i * NC), col = e0 + el;
+          float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (el < ce && col < a.cols) {
+            if (wvec) {
+              wv = *reinterpret_cast<const float4*>(a.f.norm_w + col);
+            } else {
+              wv.x = a.f.norm_w[col];
+              wv.y = a.f.norm_w[col + 1];
+              wv.z = a.f.norm_w[col + 2];
+              wv.w = a.f.norm_w[col + 3];
+            }
+          }
+          const float wn[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int tt = 0; tt < TT; tt++)
+#pragma unroll
+            for (int m = 0; m < 4; m++)
+              v[tt][i][m] = (float)__dmul_rn(__dmul_rn((double)v[tt][i][m], inv[tt]), (double)wn[m]);
+        }
+      }
+      float mx[TT];
+#pragma unroll
+      for (int tt = 0; tt < TT; tt++) {
+        mx[tt] = 0.f;
+#pragma unroll
+        for (int i = 0; i < NG; i++)
+#pragma unroll
+          for (int m = 0; m < 4; m++) {
+            float ax = fabsf(v[tt][i][m]);
+            if (!(ax <= FLT_MAX)) ax = INFINITY;  // NaN counts as non-finite
+            mx[tt] = fmaxf(mx[tt], ax);
+          }
+        for (int o = 16; o > 0; o >>= 1) mx[tt] = fmaxf(mx[tt], __shfl_xor_sync(FULL, mx[tt], o));
+        if (lane == 0) mred[warp][tt] = mx[tt];
+      }
+      consumer_sync(NC);  // (also: every consumer is done reading the previous chunk's planes)
+#pragma unroll
+      for (int tt = 0; tt < TT; tt++) {
+        float M = 0.f;
+        for (int w = 0; w < MMV_NW; w++) M = fmaxf(M, mred[w][tt]);
+        const bool bad = !(M <= FLT_MAX);
+        const int s = (!bad && M > 0.f) ? 26 - ilogbf(M) : 0;
+        const int sa = s >> 1, sb = s - sa;
+        const float pa = exp2i(sa), pb = exp2i(sb);
+        fa[tt] = bad ? __int_as_float(0x7fc00000) : exp2i(-sa) * (KIND == MK_Q4 ? 0.0625f : 1.f);
+        fb[tt] = exp2i(-sb);
+#pragma unroll
+        for (int i = 0; i < NG; i++) {
+          const int el = 4 * (tid + i * NC);
+          const int blk = el >> 5, j = el & 31;
+          const int word = (((blk >> 1) * 2 + (blk & 1)) * 4 + ((j & 15) >> 2)) * 2 + (j >> 4);
+          uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+#pragma unroll
+          for (int m = 0; m < 4; m++) {
+            const int X = __float2int_rn((v[tt][i][m] * pa) * pb);
+            p0 |= (uint32_t)(X & 127) << (8 * m);
+            p1 |= (uint32_t)((X >> 7) & 127) << (8 * m);
+            p2 |= (uint32_t)((X >> 14) & 127) << (8 * m);
+            p3 |= (uint32_t)((X >> 21) & 255) << (8 * m);
+          }
+          planes[(tt * 4 + 0) * DS + word] = p0;
+          planes[(tt * 4 + 1) * DS + word] = p1;
+          planes[(tt * 4 + 2) * DS + word] = p2;
+          planes[(tt * 4 + 3) * DS + word] = p3;
+        }
+      }
+      consumer_sync(NC);
+    };
+
+    // this lane's B columns: one token: g = (block parity sel, digit dg), the
+    // other parity's half of B read from the zero words; two tokens: g =
+    // (token sel, digit dg), one instruction per block parity
+    const int sel = g >> 2, dg = g & 3;
+    int boff[2], binc[2];
+    if (TT == 1) {
+      boff[0] = sel == 0 ? dg * DS + c * 2 : ZERO;
+      binc[0] = sel == 0 ? 16 : 0;
+      boff[1] = sel == 1 ? dg * DS + 8 + c * 2 : ZERO;
+      binc[1] = sel == 1 ? 16 : 0;
+    } else {
+      boff[0] = (sel * 4 + dg) * DS + c * 2;
+      boff[1] = boff[0] + 8;
+      binc[0] = binc[1] = 16;
+    }
+    // weights of the digit columns this lane accumulates: 2^(7 digit)
+    const float wlo = (c & 1) ? 16384.f : 1.f, whi = (c & 1) ? 2097152.f : 128.f;
+    int cur_kc = -1, pi = 0;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    // Every consumer runs every iteration even after an abort (then it only
+    // skips the math), so the arrival counts of the mbarriers stay consistent.
+    UnitPos up(u0, NSU, a.nsc);
+    for (int k = 0; k < nu; k++, up.next(a.nsc, a.tiles)) {
+      const int kc = up.kc, sc = up.sc;
+      if (kc != cur_kc) {
+        setup(kc);
+        cur_kc = kc;
+      }
+      const int st = k % a.stages;
+      const bool ready = __all_sync(FULL, mbar_wait(&full[st], (k / a.stages) & 1, &abort_flag));
+      const uint8_t* sbase = ring + (size_t)st * a.stage_bytes;
+      const int first = sc * a.scp, n = max(0, min(a.scp, min(a.ckp, a.pairs - kc * a.ckp) - first));
+      if (ready) {
+        // all pairs' operands first, so their load -> MMA -> FMA chains overlap.
+        // A stage has room for SC pairs, so slot j * NW + warp is always inside
+        // it; slots past the sub-chunk's n pairs hold stale bytes and get scale 0.
+        constexpr int WV = AB / 512;  // 16-byte words per lane per pair
+        uint4 wv[PPW][WV];
+        uint32_t sw[PPW][TT];
+        uint2 bq[PPW][2];
+        const uint8_t* wbase = sbase + (size_t)warp * REC;
+#pragma unroll
+        for (int j = 0; j < PPW; j++) {
+          const uint8_t* rec = wbase + j * MMV_NW * REC;
+          const int pc = min(first + j * MMV_NW + warp, CP - 1);  // chunk-local pair
+#pragma unroll
+          for (int v = 0; v < WV; v++) wv[j][v] = *reinterpret_cast<const uint4*>(rec + lane * 16 * WV + 16 * v);
+          if (TT == 1) {
+            sw[j][0] = *reinterpret_cast<const uint32_t*>(rec + AB + (2 * g + (c >> 1)) * 4);
+          } else {
+            const uint2 s2 = *reinterpret_cast<const uint2*>(rec + AB + 8 * g);
+            sw[j][0] = s2.x;
+            sw[j][TT - 1] = s2.y;
+          }
+#pragma unroll
+          for (int q = 0; q < 2; q++) bq[j][q] = *reinterpret_cast<const uint2*>(&planes[boff[q] + pc * binc[q]]);
+        }
+        // the operands are in registers: hand the stage back to the producer
+        // now, so the ring refills while this warp computes
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+        auto compute = [&](auto all_valid) {
+#pragma unroll
+          for (int j = 0; j < PPW; j++) {
+            const bool valid = decltype(all_valid)::value || j * MMV_NW + warp < n;
+            uint32_t A[2][4];
+            if (KIND == MK_Q4) {
+              const uint32_t M4 = 0xF0F0F0F0u;
+              const uint4 w = wv[j][0];
+              A[0][0] = w.x & M4;
+              A[0][1] = (w.x << 4) & M4;
+              A[0][2] = w.y & M4;
+              A[0][3] = (w.y << 4) & M4;
+              A[1][0] = w.z & M4;
+              A[1][1] = (w.z << 4) & M4;
+              A[1][2] = w.w & M4;
+              A[1][3] = (w.w << 4) & M4;
+            } else {
+              const uint4 w0 = wv[j][0], w1 = wv[j][WV - 1];
+              A[0][0] = w0.x;
+              A[0][1] = w0.y;
+              A[0][2] = w0.z;
+              A[0][3] = w0.w;
+              A[1][0] = w1.x;
+              A[1][1] = w1.y;
+              A[1][2] = w1.z;
+              A[1][3] = w1.w;
+            }
+#pragma unroll
+            for (int q = 0; q < TT; q++) {
+              int D[4] = {kMagic, kMagic, kMagic, kMagic};
+              if (TT == 1) {
+                mma_s8(D, A[0], bq[j][0].x, bq[j][1].x);
+                mma_s8(D, A[1], bq[j][0].y, bq[j][1].y);
+              } else {
+                mma_s8(D, A[0], q == 0 ? bq[j][0].x : 0u, q == 1 ? bq[j][1].x : 0u);
+                mma_s8(D, A[1], q == 0 ? bq[j][0].y : 0u, q == 1 ? bq[j][1].y : 0u);
+              }
+              const uint32_t s32 = sw[j][q];
+              float2 d = __half22float2(*reinterpret_cast<const __half2*>(&s32));  // (row g, row g + 8)
+              if (!decltype(all_valid)::value && !valid) d = make_float2(0.f, 0.f);
+              acc[0] = fmaf(d.x, __int_as_float(D[0]) - kMagicF, acc[0]);
+              acc[1] = fmaf(d.x, __int_as_float(D[1]) - kMagicF, acc[1]);
+              acc[2] = fmaf(d.y, __int_as_float(D[2]) - kMagicF, acc[2]);
+              acc[3] = fmaf(d.y, __int_as_float(D[3]) - kMagicF, acc[3]);
+            }
+          }
+        };
+        if (n == SC) compute(std::true_type{});
+        else compute(std::false_type{});
+      } else {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
+      }
+      if (sc != a.nsc - 1 && k != nu - 1) continue;  // the piece goes on
+      // end of a piece: recombine the digit columns, sum the lanes of a row,
+      // undo the 2^s scaling, hand the 16 (x TT) row sums to the epilogue
+      float vg = fmaf(acc[1], whi, acc[0] * wlo), vh = fmaf(acc[3], whi, acc[2] * wlo);
+      vg += __shfl_xor_sync(FULL, vg, 1);
+      vh += __shfl_xor_sync(FULL, vh, 1);
+      if (TT == 1) {
+        vg += __shfl_xor_sync(FULL, vg, 2);
+        vh += __shfl_xor_sync(FULL, vh, 2);
+      }
+      const int tt = TT == 1 ? 0 : (c >> 1);
+      const float sa = (TT == 1 || tt == 0) ? fa[0] : fa[TT - 1], sb = (TT == 1 || tt == 0) ? fb[0] : fb[TT - 1];
+      vg = (vg * sa) * sb;
+      vh = (vh * sa) * sb;
+      const int b = pi % MMV_NB;
+      if (pi >= MMV_NB) mbar_wait(&red_empty[b], ((pi / MMV_NB) - 1) & 1, &abort_flag);
+      if ((c & (TT == 1 ? 3 : 1)) == 0) {
+        red[b][warp][tt * 16 + g] = vg;
+        red[b][warp][tt * 16 + g + 8] = vh;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_full[b]);
+      pi++;
+      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+  } else {
+    // ======================= epilogue warps
+    // Pieces are numbered in unit order; warp e takes batches of MMV_UB
+    // consecutive pieces (e * UB, then every NE * UB).  A whole (tile, chunk)
+    // with one chunk is final at once; other pieces go to the workspace, and
+    // their arrivals (counted in units) are published with one release-atomic
+    // per piece issued from UB lanes at once.
+    pdl_wait();  // y, the KV cache and the step's row table belong to earlier kernels
+    const int e = warp - MMV_NW, target = a.ks * a.nsc;
+    auto finish = [&](int t, float v) {
+      const int rr = lane & 15, tt = lane >> 4, row = t * 16 + rr;
+      const float partner = __shfl_xor_sync(FULL, v, 1);
+      if (lane < NV && tt < a.T && row < a.rows) mmv_store(a, row, tt, v, partner);
+    };
+    float vb[MMV_UB] = {};
+    int tb[MMV_UB] = {}, ub[MMV_UB] = {};
+    bool fb_[MMV_UB] = {};
+    int nbat = 0;
+    bool bad = false;
+    auto flush = [&]() {
+      if (!bad) {
+        // final at once: a whole (tile, chunk) of a one-chunk matrix
+#pragma unroll
+        for (int i = 0; i < MMV_UB; i++)
+          if (i < nbat && fb_[i] && a.ks == 1) finish(tb[i], vb[i]);
+        __syncwarp();  // the workspace writes before the lanes' release atomics
+        int mt = tb[0], mu = ub[0];
+        bool mine = nbat > 0 && !(fb_[0] && a.ks == 1);
+#pragma unroll
+        for (int i = 1; i < MMV_UB; i++)
+          if (lane == i) {
+            mt = tb[i];
+            mu = ub[i];
+            mine = i < nbat && !(fb_[i] && a.ks == 1);
+          }
+        int old = 0;
+        if (lane < nbat && mine) old = atom_add_acq_rel(a.cnt + mt, mu);
+        const unsigned fin = __ballot_sync(FULL, lane < nbat && mine && old + mu == target);
+        __syncwarp();  // loads below come after the acquiring atomics
+#pragma unroll
+        for (int i = 0; i < MMV_UB; i++) {
+          if (!((fin >> i) & 1u)) continue;
+          const int t = tb[i];
+          float v = 0.f;
+          if (lane < NV) {
+            // the tile's partials in (chunk, part) order; eight loads in flight at a time
+            for (int q0 = 0; q0 < 2 * a.ks; q0 += 8) {
+              float pv[8];
+#pragma unroll
+              for (int j = 0; j < 8; j++) {
+                const int q = q0 + j;
+                pv[j] = q < 2 * a.ks ? ld_relaxed(a.ws + (((size_t)(q >> 1) * a.tiles + t) * 2 + (q & 1)) * 32 + lane)
+                                     : 0.f;
+              }
+#pragma unroll
+              for (int j = 0; j < 8; j++) v += pv[j];
+            }
+          }
+          if (lane == i) a.cnt[t] = 0;  // ready for the next launch
+          finish(t, v);
+        }
+      }
+      nbat = 0;
+      bad = false;
+    };
+    int pi = 0, pstart = 0;
+    UnitPos up(u0, NSU, a.nsc);
+    for (int k = 0; k < nu; k++, up.next(a.nsc, a.tiles)) {
+      const int kc = up.kc, t = up.t, sc = up.sc;
+      if (sc != a.nsc - 1 && k != nu - 1) continue;
+      // piece pi: units pstart .. k, sub-chunks sc0 .. sc of (t, kc)
+      const int cnt_u = k - pstart + 1, sc0 = sc - (k - pstart);
+      if ((pi / MMV_UB) % MMV_NE == e) {
+        const int b = pi % MMV_NB;
+        const bool ok = mbar_wait(&red_full[b], (pi / MMV_NB) & 1, &abort_flag);
+        float v = 0.f;
+        if (lane < NV) {
+#pragma unroll
+          for (int w = 0; w < MMV_NW; w++) v += red[b][w][lane];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&red_empty[b]);
+        bad = bad || __any_sync(FULL, !ok || abort_flag);
+        const bool whole = sc0 == 0 && sc == a.nsc - 1;
+        if (!(whole && a.ks == 1) && lane < NV) {
+          float* w0 = a.ws + (((size_t)kc * a.tiles + t) * 2 + (sc0 == 0 ? 0 : 1)) * 32 + lane;
+          *w0 = v;
+          if (whole) w0[32] = 0.f;  // no second part
+        }
+        vb[nbat] = v;
+        tb[nbat] = t;
+        ub[nbat] = cnt_u;
+        fb_[nbat] = whole;
+        if (++nbat == MMV_UB) flush();
+      }
+      pi++;
+      pstart = k + 1;
+    }
+    if (nbat) flush();
+  }
+
+  __syncthreads();
+  if (tid == 0 && abort_flag) {
+    // no copy may still be landing when the CTA exits
+    for (int s = 0; s < a.stages; s++) {
+      const int j = last_unit[s];
+      if (j < 0) continue;
+      abort_flag = 0;
+      if (!mbar_wait(&full[s], (j / a.stages) & 1, &abort_flag)) break;
+    }
+    atomicExch(a.err, 1);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+// dynamic shared memory a CTA may take next to the kernel's static arrays
+template <int KIND, int TT>
+static int mmv_max_dyn() {
+  int dev = 0, optin = 0;
+  cudaGetDevice(&dev);
+  cudaFuncAttributes fa{};
+  if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+      cudaFuncGetAttributes(&fa, k_mmv<KIND, TT>) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return std::min(MMV_MAX_SMEM, optin - (int)fa.sharedSizeBytes);
+}
+
+template <int KIND, int TT>
+static int mmv_occ(int smem) {
+  int o = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_mmv<KIND, TT>, MMV_THREADS, smem) != cudaSuccess) {
+    cudaGetLastError();
+    o = 0;
+  }
+  return o;
+}
+
+// Two CTAs per SM when they fit (more warps to overlap the MMA work), with
+// the deepest ring that keeps that occupancy; a stage is free again as soon
+// as its operands are in registers, so every stage is in flight.
+template <int KIND, int TT>
+static void mmv_pick(MmShape* sh) {
+  const int stage = (int)sh->stage_bytes, max_dyn = mmv_max_dyn<KIND, TT>();
+  if (cudaFuncSetAttribute(k_mmv<KIND, TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn) != cudaSuccess)
+    cudaGetLastError();
+  int best_s = 2, best_o = 0;
+  for (int s = std::min(MMV_MAX_STAGES, max_dyn / stage); s >= 2; s--) {
+    // (s goes down: the first depth that reaches an occupancy is the deepest one)
+    const int o = std::min(mmv_occ<KIND, TT>(s * stage), 2);
+    if (o > best_o) {
+      best_o = o;
+      best_s = s;
+    }
+    if (o == 2) break;
+  }
+  if (best_o == 0) best_o = 1;
+  sh->stages = best_s;
+  sh->smem = best_s * stage;
+  sh->ctas = best_o;
+}
+
+int mm_prepare(Matrix* m) {
+  TN_REQUIRE(m->kind == MK_Q4 || m->kind == MK_Q8, TN_EINVAL, "mm_prepare: kind %d", m->kind);
+  int ks_max = 1;
+  for (int tt = 1; tt <= 2; tt++) {
+    MmShape& sh = m->mm[tt - 1];
+    const int cp = MMV_CE / tt / 64, scmax = mmv_sc(m->kind);
+    sh.ks = (m->pairs + cp - 1) / cp;
+    sh.ckp = (m->pairs + sh.ks - 1) / sh.ks;
+    sh.nsc = (sh.ckp + scmax - 1) / scmax;
+    sh.scp = (sh.ckp + sh.nsc - 1) / sh.nsc;
+    sh.stage_bytes = (uint32_t)scmax * tile_rec_bytes(m->kind);  // room for a full sub-chunk
+    ks_max = std::max(ks_max, sh.ks);
+    // (set once per matrix, outside any stream capture)
+    if (m->kind == MK_Q4) {
+      if (tt == 1) mmv_pick<MK_Q4, 1>(&sh);
+      else mmv_pick<MK_Q4, 2>(&sh);
+    } else {
+      if (tt == 1) mmv_pick<MK_Q8, 1>(&sh);
+      else mmv_pick<MK_Q8, 2>(&sh);
+    }
+  }
+  m->ws_floats = (size_t)ks_max * m->tiles * 2 * 32;
+  return TN_OK;
+}
+
+template <int KIND, int TT>
+static int launch_mmv(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
+                      const MvFuse& f, int* err, cudaStream_t s) {
+  const MmShape& sh = m.mm[TT - 1];
+  const int NU = m.tiles * sh.nsc * sh.ks;
+  // at least nsc units per CTA, so a (tile, chunk) spans at most two CTAs
+  const int grid = std::max(1, std::min(NU / sh.nsc, sh.ctas * num_sms()));
+  const MmvArgs a{m.data, m.rows, m.tiles, m.pairs, m.cols, T, x, ldx, y, ldy, mode, sh.ks, sh.ckp, sh.nsc,
+                  sh.scp, sh.stages, sh.stage_bytes, err, m.cnt, m.ws, f};
+  TN_CHECK_CUDA(launch_pdl(k_mmv<KIND, TT>, dim3(grid), dim3(MMV_THREADS), (size_t)sh.smem, s, a));
+  return TN_OK;
+}
+
+bool matvec_dec_ok(const Matrix& m, int T) { return (m.kind == MK_Q4 || m.kind == MK_Q8) && T >= 1 && T <= 2; }
+
+int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
+               int* err, cudaStream_t s) {
+  TN_REQUIRE(m.kind == MK_Q4 || m.kind == MK_Q8, TN_EUNSUPPORTED, "matvec_dec: matrix kind %d", m.kind);
+  TN_REQUIRE(mode != EPI_SWIGLU || (m.rows & 1) == 0, TN_EINVAL, "swiglu needs paired rows");
+  TN_REQUIRE(err, TN_EINVAL, "matvec_dec: error flag required");
+  TN_REQUIRE(m.ws && m.cnt, TN_ESTATE, "matvec_dec: cross-CTA workspace missing");
+  // tokens two at a time; each launch streams the whole matrix
+  for (int t0 = 0; t0 < T; t0 += 2) {
+    const int n = std::min(2, T - t0);
+    MvFuse g = f;
+    const float* xj = x;
+    if (f.rowsel) g.rowsel = f.rowsel + t0;
+    else xj = x + (size_t)t0 * ldx;
+    if (f.rinfo) g.rinfo = f.rinfo + t0;
+    if (f.cs) g.cs = f.cs + (size_t)t0 * (f.hd / 2);
+    if (f.q_out) g.q_out = f.q_out + (size_t)t0 * f.q_dim;
+    float* yj = y + (size_t)t0 * ldy;
+    int rc;
+    if (m.kind == MK_Q4)
+      rc = n == 1 ? launch_mmv<MK_Q4, 1>(m, n, xj, ldx, yj, ldy, mode, g, err, s)
+                  : launch_mmv<MK_Q4, 2>(m, n, xj, ldx, yj, ldy, mode, g, err, s);
+    else
+      rc = n == 1 ? launch_mmv<MK_Q8, 1>(m, n, xj, ldx, yj, ldy, mode, g, err, s)
+                  : launch_mmv<MK_Q8, 2>(m, n, xj, ldx, yj, ldy, mode, g, err, s);
+    if (rc != TN_OK) return rc;
+  }
+  return TN_OK;
+}
+
+}  // namespace tn

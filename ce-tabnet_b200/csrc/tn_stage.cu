@@ -172,14 +172,16 @@ static int dalloc(tn_stage* st, T** p, size_t count) {
 }
 
 // device copy of `bytes` of weights: the pointer itself when already on the
-// device, else the staging buffer after a synchronous upload
+// device, else the staging buffer after an upload ordered on the stage stream.
+// (A plain cudaMemcpy from pageable memory may return before its DMA lands, and
+// the legacy stream does not order the non-blocking stage stream's repack after it.)
 static int stage_src(const tn_stage_spec* sp, const void* src, uint64_t bytes, uint8_t* staging,
-                     const uint8_t** out) {
+                     cudaStream_t s, const uint8_t** out) {
   if (sp->weights_on_device) {
     *out = (const uint8_t*)src;
     return TN_OK;
   }
-  TN_CHECK_CUDA(cudaMemcpy(staging, src, bytes, cudaMemcpyHostToDevice));
+  TN_CHECK_CUDA(cudaMemcpyAsync(staging, src, bytes, cudaMemcpyHostToDevice, s));
   *out = staging;
   return TN_OK;
 }
@@ -192,7 +194,7 @@ static int load_layer(tn_stage* st, const tn_stage_spec* sp, int li, uint8_t* st
   TN_REQUIRE(lw.buf && lw.len >= L.total, TN_EINVAL, "layer %d: buffer of %llu bytes, layout needs %llu",
              lw.idx, (unsigned long long)lw.len, (unsigned long long)L.total);
   const uint8_t* src = nullptr;
-  int rc = stage_src(sp, lw.buf, L.total, staging, &src);
+  int rc = stage_src(sp, lw.buf, L.total, staging, st->stream, &src);
   if (rc) return rc;
   LayerW& W = st->layers[li];
   const int q = lw.quant;
@@ -298,7 +300,7 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
     if ((rc = load_layer(st, sp, i, staging))) return rc;
   const uint8_t* src = nullptr;
   if (st->first) {
-    if ((rc = stage_src(sp, sp->embed, embed_bytes, staging, &src))) return rc;
+    if ((rc = stage_src(sp, sp->embed, embed_bytes, staging, st->stream, &src))) return rc;
     if ((rc = matrix_alloc(&st->embed, sp->embed_quant, st->V, st->H, st->stream))) return rc;
     if ((rc = matrix_repack(&st->embed, src, sp->embed_quant, st->V, 0, 1, st->stream))) return rc;
     TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
@@ -306,11 +308,11 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
     st->packed_bytes += embed_bytes;
   }
   if (st->last) {
-    if ((rc = stage_src(sp, sp->lm_head, head_bytes, staging, &src))) return rc;
+    if ((rc = stage_src(sp, sp->lm_head, head_bytes, staging, st->stream, &src))) return rc;
     if ((rc = matrix_alloc(&st->lm_head, sp->lm_head_quant, st->V, st->H, st->stream))) return rc;
     if ((rc = matrix_repack(&st->lm_head, src, sp->lm_head_quant, st->V, 0, 1, st->stream))) return rc;
     TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
-    if ((rc = stage_src(sp, sp->norm, (uint64_t)st->H * 2, staging, &src))) return rc;
+    if ((rc = stage_src(sp, sp->norm, (uint64_t)st->H * 2, staging, st->stream, &src))) return rc;
     TN_CHECK_CUDA(cudaMalloc(&st->final_norm, align256(st->H * sizeof(float))));
     if ((rc = hop_decode((const uint16_t*)src, st->H, st->final_norm, st->stream))) return rc;
     TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
@@ -466,7 +468,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec_dec(L.qkv, T, st->h, H, st->qkv, ldqkv, EPI_QKV_ROPE, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, st->kerr, s));
       TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1,
                      rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->slot_stride, st->kvh_stride, st->nH,
                              st->nKV, st->hd, T, s));
@@ -477,19 +479,19 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
     if (fuse && matvec_dec_ok(L.o, T))
       TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, st->kerr, s));
     if (fuse && matvec_dec_ok(L.gu, T)) {
       MvFuse f;
       f.norm_w = L.ffn_norm;
       TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec_dec(L.gu, T, st->h, H, st->act, st->F, EPI_SWIGLU, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.ffn_norm, st->xn, H, H, T, s));
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, st->kerr, s));
     }
     if (fuse && matvec_dec_ok(L.down, T))
       TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec_dec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, st->kerr, s));
   }
   if (st->last) {
     if (!(st->flags & TN_FLAG_NO_FUSED_DECODE) && matvec_dec_ok(st->lm_head, n_out)) {
@@ -501,7 +503,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, outrows, st->final_norm, st->xn, H, H, n_out, s));
       TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1,
-                     matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, s));
+                     matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, st->kerr, s));
     }
     TN_STEP_LAUNCH(TN_PROF_OTHER, 1, sample_rows(st->logits, n_out, st->V, params, st->tok_out, s));
   } else {
@@ -726,6 +728,15 @@ static int forward_impl(tn_stage* st, const tn_fwd_req* reqs, int n, tn_fwd_out*
     TN_CHECK_CUDA(cudaMemcpy(&kerr, st->kerr, sizeof(int), cudaMemcpyDeviceToHost));
     if (kerr) {
       TN_CHECK_CUDA(cudaMemset(st->kerr, 0, sizeof(int)));
+      // a launch that gave up may have left split-K arrival counts behind
+      for (LayerW& L : st->layers) {
+        matrix_reset_counters(L.qkv, s);
+        matrix_reset_counters(L.o, s);
+        matrix_reset_counters(L.gu, s);
+        matrix_reset_counters(L.down, s);
+      }
+      matrix_reset_counters(st->lm_head, s);
+      TN_CHECK_CUDA(cudaStreamSynchronize(s));
       set_error("a kernel's bounded wait on its copy pipeline gave up; the step's outputs are invalid");
       return TN_ETIMEOUT;
     }
