@@ -113,9 +113,30 @@ extern "C" void tn_matrix_free(tn_matrix* m) {
   delete m;
 }
 
+// caller scratch: [row table][arrival counters][split partials], 256-byte aligned pieces
+static size_t attn_rows_bytes(int n_rows) { return ((size_t)n_rows * sizeof(RowInfo) + 255) & ~(size_t)255; }
+static size_t attn_cnt_bytes(int n_rows, int n_kv_heads) {
+  return ((size_t)n_rows * n_kv_heads * sizeof(int) + 255) & ~(size_t)255;
+}
 static size_t attn_total_scratch(int n_rows, int n_heads, int n_kv_heads, int head_dim, int max_ctx) {
-  return ((size_t)n_rows * sizeof(RowInfo) + 255 & ~(size_t)255) +
+  return attn_rows_bytes(n_rows) + attn_cnt_bytes(n_rows, n_kv_heads) +
          attn_scratch_bytes(n_rows, n_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx));
+}
+
+// row table + zeroed counters, then the one-kernel attention
+static int attn_run(int n_rows, int n_slots, int n_heads, int n_kv_heads, int head_dim, int max_ctx, const float* d_q,
+                    const float* d_k, const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
+                    void* scratch, cudaStream_t s) {
+  RowInfo* rows = (RowInfo*)scratch;
+  int* cnt = (int*)((char*)scratch + attn_rows_bytes(n_rows));
+  void* part = (char*)cnt + attn_cnt_bytes(n_rows, n_kv_heads);
+  k_rows_from_slots<<<(n_rows + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows);
+  TN_CHECK_LAUNCH();
+  TN_CHECK_CUDA(cudaMemsetAsync(cnt, 0, (size_t)n_rows * n_kv_heads * sizeof(int), s));
+  const size_t kvh_stride = (size_t)max_ctx * head_dim;
+  return attention(d_q, n_heads * head_dim, d_k, d_v, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows, n_heads,
+                   n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out, n_heads * head_dim, part,
+                   cnt, s);
 }
 
 extern "C" uint64_t tn_attention_scratch_bytes(int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,
@@ -141,15 +162,8 @@ extern "C" int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, in
   const size_t need = attn_total_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx);
   TN_REQUIRE(scratch_bytes >= need, TN_EINVAL, "tn_attention: scratch of %llu bytes, %zu needed",
              (unsigned long long)scratch_bytes, need);
-  cudaStream_t s = (cudaStream_t)stream;
-  RowInfo* rows = (RowInfo*)d_scratch;
-  void* part = (char*)d_scratch + (((size_t)n_rows * sizeof(RowInfo) + 255) & ~(size_t)255);
-  k_rows_from_slots<<<(n_rows + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows);
-  TN_CHECK_LAUNCH();
-  const size_t kvh_stride = (size_t)max_ctx * head_dim;
-  return attention(d_q, n_heads * head_dim, d_k, d_v, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows,
-                   n_heads, n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out,
-                   n_heads * head_dim, part, s);
+  return attn_run(n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v, d_slot, d_len, d_out,
+                  d_scratch, (cudaStream_t)stream);
 }
 
 // ---- tn_attention_static: attention with its scratch in a fixed device array,
@@ -198,15 +212,8 @@ extern "C" int tn_attention_static(int32_t n_rows, int32_t n_slots, int32_t n_he
   void* scratch = nullptr;
   const int rc = attn_static_scratch(&scratch);
   if (rc) return rc;
-  cudaStream_t s = (cudaStream_t)stream;
-  RowInfo* rows = (RowInfo*)scratch;
-  void* part = (char*)scratch + (((size_t)n_rows * sizeof(RowInfo) + 255) & ~(size_t)255);
-  k_rows_from_slots<<<(n_rows + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows);
-  TN_CHECK_LAUNCH();
-  const size_t kvh_stride = (size_t)max_ctx * head_dim;
-  return attention(d_q, n_heads * head_dim, d_k, d_v, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows, n_heads,
-                   n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out, n_heads * head_dim, part,
-                   s);
+  return attn_run(n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v, d_slot, d_len, d_out,
+                  scratch, (cudaStream_t)stream);
 }
 
 extern "C" int tn_hop_encode(const float* d_in, uint16_t* d_out, uint64_t n, void* stream) {

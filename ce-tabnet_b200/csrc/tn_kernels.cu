@@ -635,198 +635,243 @@ int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs,
 }
 
 // ================================================================ attention
-// One-query GQA attention (web/inference-worker.js:556-564) as split-K
-// flash-decoding: CTA (split, kv head, row) walks its slice of the row's
-// cached positions in tiles of 32, serving all G query heads of the KV head
-// from one copy of each K/V tile in shared memory; (max, sum, unnormalised
-// output) partials are merged by k_attn_combine.
-constexpr int ATT_TILE = 32;
-constexpr int ATT_THREADS = 128;
+// One-query GQA attention (web/inference-worker.js:556-564) for T rows in one
+// kernel.  CTA (split, KV head, row) takes its share of the row's cached
+// positions, and each of its 8 warps a contiguous part of that share.  A lane
+// holds HD/32 dimensions of q for the G query heads of the KV head; a warp
+// step covers PS = 32/G positions: the PS x G partial dot products of a lane
+// are reduce-scattered over the warp so that lane l ends with the full score
+// of (position l / G, head l % G) -- every exp is computed once -- and an
+// online softmax per head rescales the lane's G x HD/32 output accumulators.
+// The warps merge in shared memory; with several splits, the CTA writes its
+// (max, sum, unnormalised output) partial and the last CTA of the (row, KV
+// head) merges the splits in split order (deterministic) and resets the
+// arrival counter.
+constexpr int ATT_WARPS = 8;
 
 template <int HD, int G>
-__global__ void __launch_bounds__(ATT_THREADS)
-    k_attn_split(const float* __restrict__ q, int ldq, const float* __restrict__ kc,
-                 const float* __restrict__ vc, size_t slot_stride, size_t kvh_stride,
-                 const RowInfo* __restrict__ rows, int nH, int n_splits, float scale,
-                 float* __restrict__ part_o, float2* __restrict__ part_ml) {
-  constexpr int HD4 = HD / 4;
-  __shared__ __align__(16) float Ks[ATT_TILE][HD];
-  __shared__ __align__(16) float Vs[ATT_TILE][HD];
-  __shared__ __align__(16) float Qs[G][HD];
-  __shared__ float Ps[G][ATT_TILE];
-  __shared__ float alpha_s[G];
-  const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
+__global__ void __launch_bounds__(ATT_WARPS * 32)
+    k_attn(const float* __restrict__ q, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
+           size_t slot_stride, size_t kvh_stride, const RowInfo* __restrict__ rows, int S, float scale,
+           float* __restrict__ out, int ldo, float* __restrict__ part, int* __restrict__ cnt) {
+  constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD, PW = GH + 2 * G;  // partial: o[G][HD], m[G], l[G]
+  constexpr unsigned FULL = 0xffffffffu;
+  __shared__ float s_m[ATT_WARPS][G], s_l[ATT_WARPS][G];
+  __shared__ __align__(16) float s_o[ATT_WARPS][GH];
+  __shared__ float s_w[64][G];  // merge weights exp(m - M) (warps, or splits <= 64)
+  __shared__ float s_M[G], s_L[G];
+  __shared__ int s_last;
+  const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z, nKV = gridDim.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();
+  pdl_wait();  // q and the cache rows of this step come from the previous kernels
   const RowInfo ri = rows[t];
   const int L = ri.len;
-  const int lo = (int)((int64_t)L * split / n_splits), hi = (int)((int64_t)L * (split + 1) / n_splits);
-  const float* kbase = kc + ri.slot * slot_stride + kvh * kvh_stride;
-  const float* vbase = vc + ri.slot * slot_stride + kvh * kvh_stride;
+  const int lo = (int)((int64_t)L * split / S), hi = (int)((int64_t)L * (split + 1) / S);
+  const int wlo = lo + (int)((int64_t)(hi - lo) * warp / ATT_WARPS);
+  const int whi = lo + (int)((int64_t)(hi - lo) * (warp + 1) / ATT_WARPS);
+  const float* kb = kc + ri.slot * slot_stride + kvh * kvh_stride + lane * DPL;
+  const float* vb = vc + ri.slot * slot_stride + kvh * kvh_stride + lane * DPL;
 
-  for (int k = tid; k < G * HD; k += ATT_THREADS)
-    Qs[k / HD][k % HD] = q[(size_t)t * ldq + (kvh * G + k / HD) * HD + k % HD];
-
-  // per-head running max / sum live in every lane of the warp owning the head
-  float m_run[(G + 3) / 4], l_run[(G + 3) / 4];
+  float qr[G][DPL], acc[G][DPL];
 #pragma unroll
-  for (int i = 0; i < (G + 3) / 4; i++) {
-    m_run[i] = -INFINITY;
-    l_run[i] = 0.f;
-  }
-  constexpr int DPT = (G * HD + ATT_THREADS - 1) / ATT_THREADS;  // (head, dim) outputs per thread
-  float acc[DPT];
+  for (int h = 0; h < G; h++)
 #pragma unroll
-  for (int i = 0; i < DPT; i++) acc[i] = 0.f;
-
-  for (int p0 = lo; p0 < hi; p0 += ATT_TILE) {
-    const int n = min(ATT_TILE, hi - p0);
-    __syncthreads();
-    for (int k = tid; k < ATT_TILE * HD4; k += ATT_THREADS) {
-      const int p = k / HD4, j = k % HD4;
-      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-      if (p < n) {
-        kv = *reinterpret_cast<const float4*>(kbase + (size_t)(p0 + p) * HD + 4 * j);
-        vv = *reinterpret_cast<const float4*>(vbase + (size_t)(p0 + p) * HD + 4 * j);
+    for (int d = 0; d < DPL; d++) {
+      qr[h][d] = q[(size_t)t * ldq + (kvh * G + h) * HD + lane * DPL + d];
+      acc[h][d] = 0.f;
+    }
+  auto load_row = [&](const float* base, int p, float (&r)[DPL]) {
+    if (DPL == 4) {
+      const float4 v = *reinterpret_cast<const float4*>(base + (size_t)p * HD);
+      r[0] = v.x;
+      r[DPL > 1 ? 1 : 0] = v.y;
+      r[DPL > 2 ? 2 : 0] = v.z;
+      r[DPL > 3 ? 3 : 0] = v.w;
+    } else if (DPL == 2) {
+      const float2 v = *reinterpret_cast<const float2*>(base + (size_t)p * HD);
+      r[0] = v.x;
+      r[DPL > 1 ? 1 : 0] = v.y;
+    } else {
+      r[0] = base[(size_t)p * HD];
+    }
+  };
+  // this lane's (head, position) after the reduce-scatter; its head's running
+  // max / sum live in every lane of that head
+  const int my_h = lane % G, my_p = lane / G;
+  float m_run = -INFINITY, l_run = 0.f;
+  for (int p0 = wlo; p0 < whi; p0 += PS) {
+    float kr[PS][DPL], vr[PS][DPL];
+#pragma unroll
+    for (int i = 0; i < PS; i++) {
+      const int p = min(p0 + i, whi - 1);  // past the end: a valid row, masked below
+      load_row(kb, p, kr[i]);
+      load_row(vb, p, vr[i]);
+    }
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < PS; i++)
+#pragma unroll
+      for (int h = 0; h < G; h++) {
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) s = fmaf(qr[h][d], kr[i][d], s);
+        v[i * G + h] = s;
       }
-      *reinterpret_cast<float4*>(&Ks[p][4 * j]) = kv;
-      *reinterpret_cast<float4*>(&Vs[p][4 * j]) = vv;
-    }
-    __syncthreads();
-    // scores: thread (p = lane, heads warp, warp+4, ...)
-    for (int g = warp; g < G; g += ATT_THREADS / 32) {
-      float dot = 0.f;
-      const int p = lane;
-#pragma unroll 8
-      for (int j0 = 0; j0 < HD4; j0++) {
-        const int j = (j0 + p) % HD4;  // rotate to keep the 8 lanes of a phase on distinct banks
-        const float4 kk = *reinterpret_cast<const float4*>(&Ks[p][4 * j]);
-        const float4 qq = *reinterpret_cast<const float4*>(&Qs[g][4 * j]);
-        dot = fmaf(qq.x, kk.x, dot);
-        dot = fmaf(qq.y, kk.y, dot);
-        dot = fmaf(qq.z, kk.z, dot);
-        dot = fmaf(qq.w, kk.w, dot);
-      }
-      const float sc = p < n ? dot * scale : -INFINITY;
-      float mx = sc;
-      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      const int gi = g / (ATT_THREADS / 32);
-      const float m_new = fmaxf(m_run[gi], mx);
-      const float e = p < n ? expf(sc - m_new) : 0.f;
-      float se = e;
-      for (int o = 16; o > 0; o >>= 1) se += __shfl_xor_sync(0xffffffffu, se, o);
-      const float al = expf(m_run[gi] - m_new);  // m_run = -inf on the first tile -> 0
-      l_run[gi] = l_run[gi] * al + se;
-      m_run[gi] = m_new;
-      Ps[g][p] = e;
-      if (lane == 0) alpha_s[g] = al;
-    }
-    __syncthreads();
+    const float sc = warp_reduce_scatter<32>(v, lane) * scale;
+    const float s = p0 + my_p < whi ? sc : -INFINITY;
+    float mx = s;
 #pragma unroll
-    for (int i = 0; i < DPT; i++) {
-      const int k = tid + i * ATT_THREADS;
-      if (k < G * HD) {
-        const int g = k / HD, d = k % HD;
-        float a = acc[i] * alpha_s[g];
-#pragma unroll 8
-        for (int p = 0; p < ATT_TILE; p++) a = fmaf(Ps[g][p], Vs[p][d], a);
-        acc[i] = a;
-      }
-    }
-  }
-  // partials: [(t * nH + head) * n_splits + split]
+    for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    const float m_new = fmaxf(m_run, mx);  // finite: position p0 is always valid
+    const float p = s == -INFINITY ? 0.f : expf(s - m_new);
+    const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+    float ps = p;
 #pragma unroll
-  for (int i = 0; i < DPT; i++) {
-    const int k = tid + i * ATT_THREADS;
-    if (k < G * HD) {
-      const int g = k / HD, d = k % HD, head = kvh * G + g;
-      part_o[(((size_t)t * nH + head) * n_splits + split) * HD + d] = acc[i];
+    for (int o = G; o < 32; o <<= 1) ps += __shfl_xor_sync(FULL, ps, o);
+    l_run = l_run * alpha + ps;
+    m_run = m_new;
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+      const float a = __shfl_sync(FULL, alpha, h);
+#pragma unroll
+      for (int d = 0; d < DPL; d++) acc[h][d] *= a;
     }
+#pragma unroll
+    for (int i = 0; i < PS; i++)
+#pragma unroll
+      for (int h = 0; h < G; h++) {
+        const float w = __shfl_sync(FULL, p, i * G + h);
+#pragma unroll
+        for (int d = 0; d < DPL; d++) acc[h][d] = fmaf(w, vr[i][d], acc[h][d]);
+      }
   }
-  for (int g = warp; g < G; g += ATT_THREADS / 32) {
-    const int gi = g / (ATT_THREADS / 32), head = kvh * G + g;
-    if (lane == 0) part_ml[((size_t)t * nH + head) * n_splits + split] = make_float2(m_run[gi], l_run[gi]);
+  // merge the warps
+  if (lane < G) {
+    s_m[warp][lane] = m_run;
+    s_l[warp][lane] = l_run;
   }
-}
-
-__global__ void k_attn_combine(const float* __restrict__ part_o, const float2* __restrict__ part_ml,
-                               int nH, int hd, int n_splits, float* __restrict__ out, int ldo) {
-  const int head = blockIdx.x, t = blockIdx.y;
-  const size_t base = ((size_t)t * nH + head) * n_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < n_splits; s++) M = fmaxf(M, part_ml[base + s].x);
-  float Lsum = 0.f;
-  for (int s = 0; s < n_splits; s++) {
-    const float2 ml = part_ml[base + s];
-    if (ml.y > 0.f) Lsum += ml.y * expf(ml.x - M);
+#pragma unroll
+  for (int h = 0; h < G; h++)
+#pragma unroll
+    for (int d = 0; d < DPL; d++) s_o[warp][h * HD + lane * DPL + d] = acc[h][d];
+  __syncthreads();
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, s_m[w][tid]);
+    float Lsum = 0.f;
+    for (int w = 0; w < ATT_WARPS; w++) {
+      const float f = s_m[w][tid] == -INFINITY ? 0.f : expf(s_m[w][tid] - M);
+      s_w[w][tid] = f;
+      Lsum += s_l[w][tid] * f;
+    }
+    s_M[tid] = M;
+    s_L[tid] = Lsum;
   }
-  const float inv = Lsum > 0.f ? 1.0f / Lsum : 0.f;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+  __syncthreads();
+  float* my_part = part + (((size_t)t * nKV + kvh) * S + split) * PW;
+  for (int e = tid; e < GH; e += ATT_WARPS * 32) {
+    const int h = e / HD;
     float o = 0.f;
-    for (int s = 0; s < n_splits; s++) {
-      const float2 ml = part_ml[base + s];
-      if (ml.y > 0.f) o = fmaf(part_o[(base + s) * hd + d], expf(ml.x - M), o);
-    }
-    out[(size_t)t * ldo + head * hd + d] = o * inv;
+    for (int w = 0; w < ATT_WARPS; w++) o = fmaf(s_o[w][e], s_w[w][h], o);
+    if (S == 1) out[(size_t)t * ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
+    else my_part[e] = o;
   }
+  if (S == 1) return;
+  if (tid < G) {
+    my_part[GH + tid] = s_M[tid];
+    my_part[GH + G + tid] = s_L[tid];
+  }
+  // publish the partial; the last CTA of the (row, KV head) merges
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    s_last = atomicAdd(&cnt[t * nKV + kvh], 1) == S - 1;
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* pbase = part + ((size_t)t * nKV + kvh) * S * PW;
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < S; sp++) M = fmaxf(M, __ldcg(pbase + (size_t)sp * PW + GH + tid));
+    float Lsum = 0.f;
+    for (int sp = 0; sp < S; sp++) {
+      const float ms = __ldcg(pbase + (size_t)sp * PW + GH + tid);
+      const float f = ms == -INFINITY ? 0.f : expf(ms - M);
+      s_w[sp][tid] = f;
+      Lsum += __ldcg(pbase + (size_t)sp * PW + GH + G + tid) * f;
+    }
+    s_L[tid] = Lsum;
+  }
+  __syncthreads();
+  for (int e = tid; e < GH; e += ATT_WARPS * 32) {
+    const int h = e / HD;
+    float o = 0.f;
+    for (int sp = 0; sp < S; sp++) o = fmaf(__ldcg(pbase + (size_t)sp * PW + e), s_w[sp][h], o);
+    out[(size_t)t * ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
+  }
+  if (tid == 0) cnt[t * nKV + kvh] = 0;  // ready for the next call
 }
 
 int attn_splits(int T, int nKV, int max_ctx) {
-  const int want = (2 * num_sms() + T * nKV - 1) / (T * nKV);
-  const int cap = std::max(1, (max_ctx + 127) / 128);
+  // about one CTA per SM, at least 128 positions of the longest row per split, at most 64 splits
+  const int want = (num_sms() + T * nKV - 1) / (T * nKV);
+  const int cap = std::max(1, std::min(64, (max_ctx + 127) / 128));
   return std::max(1, std::min(want, cap));
 }
 
 size_t attn_scratch_bytes(int T, int nH, int hd, int n_splits) {
-  const size_t n = (size_t)T * nH * n_splits;
-  return ((n * hd * sizeof(float) + 255) & ~(size_t)255) + n * sizeof(float2);
+  return (((size_t)T * nH * n_splits * (hd + 2) * sizeof(float)) + 255) & ~(size_t)255;
 }
 
 template <int HD>
 static int launch_attn_hd(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
-                          size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int G,
-                          int n_splits, float* part_o, float2* part_ml, cudaStream_t s) {
+                          size_t kvh_stride, const RowInfo* rows, int T, int nKV, int G, int n_splits, float* out,
+                          int ldo, float* part, int* cnt, cudaStream_t s) {
   const dim3 grid(n_splits, nKV, T);
   const float scale = (float)(1.0 / sqrt((double)HD));
+  cudaError_t e;
   switch (G) {
-#define TN_ATT_CASE(g)                                                                             \
-  case g:                                                                                          \
-    k_attn_split<HD, g><<<grid, ATT_THREADS, 0, s>>>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, nH, \
-                                                     n_splits, scale, part_o, part_ml);            \
+#define TN_ATT_CASE(g)                                                                                          \
+  case g:                                                                                                       \
+    e = launch_pdl(k_attn<HD, g>, grid, dim3(ATT_WARPS * 32), 0, s, q, ldq, kc, vc, slot_stride, kvh_stride, \
+                   rows, n_splits, scale, out, ldo, part, cnt);                                                  \
     break;
     TN_ATT_CASE(1)
     TN_ATT_CASE(2)
     TN_ATT_CASE(4)
     TN_ATT_CASE(8)
-    TN_ATT_CASE(16)
 #undef TN_ATT_CASE
+    case 16:
+      if (HD <= 64) {
+        e = launch_pdl(k_attn<HD <= 64 ? HD : 64, 16>, grid, dim3(ATT_WARPS * 32), 0, s, q, ldq, kc, vc, slot_stride,
+                       kvh_stride, rows, n_splits, scale, out, ldo, part, cnt);
+        break;
+      }
+      [[fallthrough]];
     default:
-      set_error("attention: %d query heads per KV head unsupported", G);
+      set_error("attention: %d query heads per KV head with head_dim %d unsupported", G, HD);
       return TN_EUNSUPPORTED;
   }
-  TN_CHECK_LAUNCH();
+  TN_CHECK_CUDA(e);
   return TN_OK;
 }
 
 int attention(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
               size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, int n_splits,
-              float* out, int ldo, void* scratch, cudaStream_t s) {
+              float* out, int ldo, void* scratch, int* cnt, cudaStream_t s) {
   if (T <= 0) return TN_OK;
   TN_REQUIRE(nH % nKV == 0, TN_EUNSUPPORTED, "attention: n_heads %% n_kv_heads != 0");
+  TN_REQUIRE(n_splits >= 1 && n_splits <= 64, TN_EINVAL, "attention: %d splits", n_splits);
   const int G = nH / nKV;
-  const size_t n = (size_t)T * nH * n_splits;
-  float* part_o = (float*)scratch;
-  float2* part_ml = (float2*)((char*)scratch + ((n * hd * sizeof(float) + 255) & ~(size_t)255));
-  int rc;
+  float* part = (float*)scratch;
   switch (hd) {
-    case 32: rc = launch_attn_hd<32>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nH, nKV, G, n_splits, part_o, part_ml, s); break;
-    case 64: rc = launch_attn_hd<64>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nH, nKV, G, n_splits, part_o, part_ml, s); break;
-    case 128: rc = launch_attn_hd<128>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nH, nKV, G, n_splits, part_o, part_ml, s); break;
+    case 32: return launch_attn_hd<32>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, part, cnt, s);
+    case 64: return launch_attn_hd<64>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, part, cnt, s);
+    case 128: return launch_attn_hd<128>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, part, cnt, s);
     default: set_error("attention: head_dim %d unsupported", hd); return TN_EUNSUPPORTED;
   }
-  if (rc) return rc;
-  k_attn_combine<<<dim3(nH, T), std::min(hd, 128), 0, s>>>(part_o, part_ml, nH, hd, n_splits, out, ldo);
-  TN_CHECK_LAUNCH();
-  return TN_OK;
 }
 
 // ================================================================ hop codec

@@ -30,6 +30,28 @@ enum MatKind { MK_Q4 = 0, MK_Q8 = 1, MK_F16 = 2, MK_F32 = 3 };
 __host__ __device__ constexpr int tile_a_bytes(int k) { return k == MK_Q4 ? 512 : 1024; }
 __host__ __device__ constexpr int tile_rec_bytes(int k) { return tile_a_bytes(k) + 64; }
 
+// Programmatic dependent launch: a kernel lets its successor start as soon as
+// every CTA of it is running, and the successor streams weights (which no
+// kernel writes) before it waits for its predecessor's results.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // Launch shape of the tensor-core matvec for one token count (1 or 2): K is
 // cut into ks chunks of ckp block pairs (a chunk's activation digits fill one
 // shared-memory table), a chunk into nsc sub-chunks of scp pairs (one
@@ -111,11 +133,6 @@ int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ld
                int* err, cudaStream_t s);
 // zero the split-K arrival counters (after a launch gave up part way)
 void matrix_reset_counters(const Matrix& m, cudaStream_t s);
-// split-K decode attention with the split merge done by the last CTA of each
-// (row, KV head); counters: T * nKV ints, zero between calls
-int attention_dec(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
-                  size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, int n_splits,
-                  float* out, int ldo, void* scratch, int* counters, cudaStream_t s);
 int embed_rows(const Matrix& emb, const int* ids, int T, float* out, int ldo, int* d_err,
                cudaStream_t s);
 int rope_table(const RowInfo* rows, const double* freq, int half, int T, double2* cs, cudaStream_t s);
@@ -123,11 +140,17 @@ int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs,
             float* kc, float* vc, size_t slot_stride, size_t kvh_stride, int nH, int nKV, int hd, int T,
             cudaStream_t s);
 
+// One-query GQA attention (web/inference-worker.js:556-564) for T rows, one
+// kernel: CTA (split, KV head, row) over its share of the row's positions;
+// the last CTA of a (row, KV head) merges the splits in split order.
+// scratch (attn_scratch_bytes) holds the split partials; counters holds
+// T * nKV arrival counters that must be zero before the first call (every
+// call leaves them zero).
 int attn_splits(int T, int nKV, int max_ctx);
 size_t attn_scratch_bytes(int T, int nH, int hd, int n_splits);
 int attention(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
               size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, int n_splits,
-              float* out, int ldo, void* scratch, cudaStream_t s);
+              float* out, int ldo, void* scratch, int* counters, cudaStream_t s);
 
 int hop_encode_rows(const float* h, int ldh, const int* rowsel, int T, int H, uint16_t* out,
                     cudaStream_t s);
