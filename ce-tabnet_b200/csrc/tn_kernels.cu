@@ -698,7 +698,7 @@ __global__ void __launch_bounds__(ATT_WARPS * 32)
   };
   // this lane's (head, position) after the reduce-scatter; its head's running
   // max / sum live in every lane of that head
-  const int my_h = lane % G, my_p = lane / G;
+  const int my_p = lane / G;
   float m_run = -INFINITY, l_run = 0.f;
   for (int p0 = wlo; p0 < whi; p0 += PS) {
     float kr[PS][DPL], vr[PS][DPL];
