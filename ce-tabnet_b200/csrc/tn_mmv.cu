@@ -92,9 +92,6 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                "l"(src), "r"(bytes), "r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void consumer_sync(int nthreads) {
-  asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
-}
 __device__ __forceinline__ int atom_add_acq_rel(int* p, int v) {
   int old;
   asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
@@ -206,7 +203,6 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
   constexpr int SC = mmv_sc(KIND), PPW = SC / MMV_NW, NV = 16 * TT, NC = MMV_NW * 32;
   constexpr int CP = MMV_CE / TT / 64;     // most pairs per chunk
   constexpr int DS = CP * 16 + 8;          // words per digit plane (skewed against bank conflicts)
-  constexpr int NG = MMV_CE / TT / 4 / NC; // 4-element groups per consumer thread and token
   constexpr int ZERO = TT * 4 * DS;        // two zero words after the planes
   constexpr unsigned FULL = 0xffffffffu;
   extern __shared__ __align__(128) uint8_t ring[];
@@ -218,9 +214,9 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
   __shared__ __align__(8) uint64_t empty[MMV_MAX_STAGES];
   __shared__ __align__(8) uint64_t red_full[MMV_NB];
   __shared__ __align__(8) uint64_t red_empty[MMV_NB];
+  __shared__ __align__(8) uint64_t ss_bar;  // the consumers' sums of squares are in sred
   __shared__ int last_unit[MMV_MAX_STAGES];
   __shared__ double sred[MMV_NW][TT];
-  __shared__ float mred[MMV_NW][TT];
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -242,6 +238,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
       mbar_init(&red_full[b], MMV_NW);
       mbar_init(&red_empty[b], 1);
     }
+    mbar_init(&ss_bar, MMV_NW);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
@@ -283,55 +280,56 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     }
     const bool wvec = a.f.norm_w == nullptr || (reinterpret_cast<uintptr_t>(a.f.norm_w) & 15) == 0;
 
-    // RMSNorm factor over the whole row (web/inference-worker.js:516-522)
-    double inv[TT];
-#pragma unroll
-    for (int tt = 0; tt < TT; tt++) inv[tt] = 1.0;
-    if (a.f.norm_w) {
+    // RMSNorm (web/inference-worker.js:516-522) is applied to the row sums:
+    // y = inv * W (x o w), inv = 1 / sqrt(mean(x^2) + 1e-5), computed by the
+    // epilogue warp from the consumers' sums of squares.  With one chunk the
+    // warps' digit passes below cover the row and provide those sums; with
+    // several, a first pass over the row does.
+    const bool ss_in_setup = a.f.norm_w != nullptr && a.ks == 1;
+    if (a.f.norm_w != nullptr && a.ks > 1) {
 #pragma unroll
       for (int tt = 0; tt < TT; tt++) {
         double ss = 0.0;
-        if (tt < a.T) {
-          if (xvec) {
-            for (int i = 4 * tid; i < a.cols; i += 4 * NC) {
-              const float4 v = *reinterpret_cast<const float4*>(xrow[tt] + i);
-              ss = fma((double)v.x, (double)v.x, ss);
-              ss = fma((double)v.y, (double)v.y, ss);
-              ss = fma((double)v.z, (double)v.z, ss);
-              ss = fma((double)v.w, (double)v.w, ss);
-            }
-          } else {
-            for (int i = tid; i < a.cols; i += NC) {
-              const double v = xrow[tt][i];
-              ss = fma(v, v, ss);
-            }
+        if (tt < a.T)
+          for (int i = tid; i < a.cols; i += NC) {
+            const double v = xrow[tt][i];
+            ss = fma(v, v, ss);
           }
-        }
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
         if (lane == 0) sred[warp][tt] = ss;
       }
-      consumer_sync(NC);
-#pragma unroll
-      for (int tt = 0; tt < TT; tt++) {
-        double tot = 0.0;
-        for (int w = 0; w < MMV_NW; w++) tot += sred[w][tt];
-        inv[tt] = 1.0 / sqrt(tot / a.cols + 1e-5);
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ss_bar);
     }
 
+    // Activation digits are built by each warp for exactly the block pairs it
+    // multiplies -- pairs sc * scp + 8 j + warp of the chunk -- with its own
+    // power-of-two scale, so no CTA-wide step stands between the predecessor
+    // kernel's output and the first MMA.
+    constexpr int WP = CP / MMV_NW;  // most pairs of a chunk per warp
+    constexpr int IT = WP / 2;       // a lane covers one float4 of a pair, two pairs per step
     float fa[TT], fb[TT];
-    // digits of chunk kc into the planes
     auto setup = [&](int kc) {
-      const int e0 = kc * a.ckp * 64, ce = min(a.ckp, a.pairs - kc * a.ckp) * 64;
-      float v[TT][NG][4];
+      const int e0 = kc * a.ckp * 64, np = min(a.ckp, a.pairs - kc * a.ckp);
+      float v[TT][IT][4];
+      int word[IT];
+      bool ok[IT];
+      double ss[TT];
+#pragma unroll
+      for (int tt = 0; tt < TT; tt++) ss[tt] = 0.0;
       // all loads first (x, then the norm weights), 16 bytes at a time
 #pragma unroll
-      for (int tt = 0; tt < TT; tt++)
+      for (int it = 0; it < IT; it++) {
+        const int i = 2 * it + (lane >> 4), sc = i / PPW, jj = i - sc * PPW;
+        const int pc = sc * a.scp + 8 * jj + warp, el = pc * 64 + (lane & 15) * 4, col = e0 + el;
+        ok[it] = 8 * jj + warp < a.scp && pc < np;
+        const int blk = el >> 5, j = el & 31;
+        word[it] = (blk * 4 + ((j & 15) >> 2)) * 2 + (j >> 4);
+        const bool valid = ok[it] && col < a.cols;  // col % 4 == 0 and cols % 32 == 0
 #pragma unroll
-        for (int i = 0; i < NG; i++) {
-          const int el = 4 * (tid + i * NC), col = e0 + el;
+        for (int tt = 0; tt < TT; tt++) {
           float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (tt < a.T && el < ce && col < a.cols) {  // col % 4 == 0 and cols % 32 == 0
+          if (valid && tt < a.T) {
             if (xvec) {
               xv = *reinterpret_cast<const float4*>(xrow[tt] + col);
             } else {
@@ -341,17 +339,14 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
               xv.w = xrow[tt][col + 3];
             }
           }
-          v[tt][i][0] = xv.x;
-          v[tt][i][1] = xv.y;
-          v[tt][i][2] = xv.z;
-          v[tt][i][3] = xv.w;
+          v[tt][it][0] = xv.x;
+          v[tt][it][1] = xv.y;
+          v[tt][it][2] = xv.z;
+          v[tt][it][3] = xv.w;
         }
-      if (a.f.norm_w) {
-#pragma unroll
-        for (int i = 0; i < NG; i++) {
-          const int el = 4 * (tid + i * NC), col = e0 + el;
+        if (a.f.norm_w) {
           float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (el < ce && col < a.cols) {
+          if (valid) {
             if (wvec) {
               wv = *reinterpret_cast<const float4*>(a.f.norm_w + col);
             } else {
@@ -365,57 +360,58 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
 #pragma unroll
           for (int tt = 0; tt < TT; tt++)
 #pragma unroll
-            for (int m = 0; m < 4; m++)
-              v[tt][i][m] = (float)__dmul_rn(__dmul_rn((double)v[tt][i][m], inv[tt]), (double)wn[m]);
+            for (int m = 0; m < 4; m++) {
+              const float xv = v[tt][it][m];
+              ss[tt] = fma((double)xv, (double)xv, ss[tt]);
+              v[tt][it][m] = xv * wn[m];
+            }
         }
       }
-      float mx[TT];
+      if (ss_in_setup) {
 #pragma unroll
-      for (int tt = 0; tt < TT; tt++) {
-        mx[tt] = 0.f;
-#pragma unroll
-        for (int i = 0; i < NG; i++)
-#pragma unroll
-          for (int m = 0; m < 4; m++) {
-            float ax = fabsf(v[tt][i][m]);
-            if (!(ax <= FLT_MAX)) ax = INFINITY;  // NaN counts as non-finite
-            mx[tt] = fmaxf(mx[tt], ax);
-          }
-        for (int o = 16; o > 0; o >>= 1) mx[tt] = fmaxf(mx[tt], __shfl_xor_sync(FULL, mx[tt], o));
-        if (lane == 0) mred[warp][tt] = mx[tt];
+        for (int tt = 0; tt < TT; tt++) {
+          for (int o = 16; o > 0; o >>= 1) ss[tt] += __shfl_xor_sync(FULL, ss[tt], o);
+          if (lane == 0) sred[warp][tt] = ss[tt];
+        }
       }
-      consumer_sync(NC);  // (also: every consumer is done reading the previous chunk's planes)
 #pragma unroll
       for (int tt = 0; tt < TT; tt++) {
         float M = 0.f;
-        for (int w = 0; w < MMV_NW; w++) M = fmaxf(M, mred[w][tt]);
+#pragma unroll
+        for (int it = 0; it < IT; it++)
+#pragma unroll
+          for (int m = 0; m < 4; m++) {
+            float ax = fabsf(v[tt][it][m]);
+            if (!(ax <= FLT_MAX)) ax = INFINITY;  // NaN counts as non-finite
+            M = fmaxf(M, ax);
+          }
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
         const bool bad = !(M <= FLT_MAX);
-        const int s = (!bad && M > 0.f) ? 26 - ilogbf(M) : 0;
-        const int sa = s >> 1, sb = s - sa;
+        const int sh = (!bad && M > 0.f) ? 26 - ilogbf(M) : 0;
+        const int sa = sh >> 1, sb = sh - sa;
         const float pa = exp2i(sa), pb = exp2i(sb);
         fa[tt] = bad ? __int_as_float(0x7fc00000) : exp2i(-sa) * (KIND == MK_Q4 ? 0.0625f : 1.f);
         fb[tt] = exp2i(-sb);
 #pragma unroll
-        for (int i = 0; i < NG; i++) {
-          const int el = 4 * (tid + i * NC);
-          const int blk = el >> 5, j = el & 31;
-          const int word = (((blk >> 1) * 2 + (blk & 1)) * 4 + ((j & 15) >> 2)) * 2 + (j >> 4);
+        for (int it = 0; it < IT; it++) {
+          if (!ok[it]) continue;
           uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
 #pragma unroll
           for (int m = 0; m < 4; m++) {
-            const int X = __float2int_rn((v[tt][i][m] * pa) * pb);
+            const int X = __float2int_rn((v[tt][it][m] * pa) * pb);
             p0 |= (uint32_t)(X & 127) << (8 * m);
             p1 |= (uint32_t)((X >> 7) & 127) << (8 * m);
             p2 |= (uint32_t)((X >> 14) & 127) << (8 * m);
             p3 |= (uint32_t)((X >> 21) & 255) << (8 * m);
           }
-          planes[(tt * 4 + 0) * DS + word] = p0;
-          planes[(tt * 4 + 1) * DS + word] = p1;
-          planes[(tt * 4 + 2) * DS + word] = p2;
-          planes[(tt * 4 + 3) * DS + word] = p3;
+          planes[(tt * 4 + 0) * DS + word[it]] = p0;
+          planes[(tt * 4 + 1) * DS + word[it]] = p1;
+          planes[(tt * 4 + 2) * DS + word[it]] = p2;
+          planes[(tt * 4 + 3) * DS + word[it]] = p3;
         }
       }
-      consumer_sync(NC);
+      __syncwarp();
+      if (ss_in_setup && kc == 0 && lane == 0) mbar_arrive(&ss_bar);  // the row's sums of squares are out
     };
 
     // this lane's B columns: one token: g = (block parity sel, digit dg), the
@@ -566,8 +562,19 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     // per piece issued from UB lanes at once.
     pdl_wait();  // y, the KV cache and the step's row table belong to earlier kernels
     const int e = warp - MMV_NW, target = a.ks * a.nsc;
+    // RMSNorm factor of this lane's token, from the consumers' sums of squares
+    double inv = 1.0;
+    if (a.f.norm_w) {
+      if (__all_sync(FULL, mbar_wait(&ss_bar, 0, &abort_flag))) {
+        const int tt = min(lane >> 4, TT - 1);
+        double tot = 0.0;
+        for (int w = 0; w < MMV_NW; w++) tot += sred[w][tt];
+        inv = 1.0 / sqrt(tot / a.cols + 1e-5);
+      }
+    }
     auto finish = [&](int t, float v) {
       const int rr = lane & 15, tt = lane >> 4, row = t * 16 + rr;
+      v = (float)((double)v * inv);
       const float partner = __shfl_xor_sync(FULL, v, 1);
       if (lane < NV && tt < a.T && row < a.rows) mmv_store(a, row, tt, v, partner);
     };
