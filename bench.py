@@ -208,13 +208,8 @@ def device_weights(pkg, torch, m, lo, hi, first, last):
 
 
 class Pipeline:
-    """One stage per rank; tick schedule with all P2P ops of a tick batched.
-
-    Rank r runs step j = tau - r at tick tau (micro-batch j % M).  At the start
-    of tick tau it receives the input of step j and sends the output of step
-    j - 1 (so every send meets its receive in the same tick on the peer); the
-    last rank's token of step j reaches rank 0 at tick j + W and feeds step
-    j + M (M >= W)."""
+    """One stage per rank, stepping micro-batches on the tick schedule of
+    planner.pipeline_tick with all P2P ops of a tick batched."""
 
     def __init__(self, pkg, torch, ctx, rank, world, M, H):
         self.pkg, self.torch, self.ctx = pkg, torch, ctx
@@ -224,8 +219,8 @@ class Pipeline:
         self.stream = torch.cuda.ExternalStream(self.stream_ptr)
         dev = torch.device("cuda", torch.cuda.current_device())
         self.tok = torch.zeros((M, 1), dtype=torch.int32, device=dev)          # rank 0 inputs / last outputs
-        self.hin = torch.zeros((M, H), dtype=torch.int16, device=dev)          # hidden inputs
-        self.hout = torch.zeros((M, H), dtype=torch.int16, device=dev)         # hidden outputs
+        self.hin = torch.zeros((M, H), dtype=torch.float16, device=dev)        # hidden inputs (fp16 bits)
+        self.hout = torch.zeros((M, H), dtype=torch.float16, device=dev)       # hidden outputs (fp16 bits)
         self.tok_out = torch.zeros((M, 1), dtype=torch.int32, device=dev)
         self.seq_ids = [(C.c_uint64 * 1)(ctx.seq_key(mb)) for mb in range(M)]
         self.pos = [0] * M
@@ -256,25 +251,17 @@ class Pipeline:
                 return
             import torch.distributed as dist
 
-            for tau in range(n + W):
-                j = tau - r
-                ops = []
-                if r == 0:
-                    jt = tau - W  # token of step jt arrives now, for step jt + M
-                    if 0 <= jt < n and jt + M < n:
-                        ops.append(dist.P2POp(dist.irecv, self.tok[jt % M], W - 1))
-                elif 0 <= j < n:
-                    ops.append(dist.P2POp(dist.irecv, self.hin[j % M], r - 1))
-                if 1 <= j <= n:  # output of step j - 1
-                    if r < W - 1:
-                        ops.append(dist.P2POp(dist.isend, self.hout[(j - 1) % M], r + 1))
-                    elif j - 1 + M < n:
-                        ops.append(dist.P2POp(dist.isend, self.tok_out[(j - 1) % M], 0))
+            bufs = {"recv_token": self.tok, "recv_hidden": self.hin, "send_hidden": self.hout,
+                    "send_token": self.tok_out}
+            for tau in range(self.pkg.planner.pipeline_ticks(W, n)):
+                sched, mb = self.pkg.planner.pipeline_tick(r, W, M, n, tau)
+                ops = [dist.P2POp(dist.irecv if kind.startswith("recv") else dist.isend, bufs[kind][b], peer)
+                       for kind, b, peer in sched]
                 if ops:
                     for w in dist.batch_isend_irecv(ops):
                         w.wait()
-                if 0 <= j < n:
-                    self._step(j % M)
+                if mb is not None:
+                    self._step(mb)
 
 
 def prefill(pkg, torch, ctx, rank, world, prompts, H):
@@ -288,7 +275,7 @@ def prefill(pkg, torch, ctx, rank, world, prompts, H):
     else:
         import torch.distributed as dist
 
-        buf = torch.empty((M, L, H), dtype=torch.int16, device="cuda")
+        buf = torch.empty((M, L, H), dtype=torch.float16, device="cuda")
         dist.recv(buf, rank - 1)
         hid = buf.cpu().numpy().view(np.uint16)
         reqs = [{"seq_id": mb, "token_pos": 0, "hidden": hid[mb], "temperature": 0, "hop_mode": "all"}
@@ -304,7 +291,7 @@ def prefill(pkg, torch, ctx, rank, world, prompts, H):
     import torch.distributed as dist
 
     hs = np.stack([o["hidden"] for o in out]).astype(np.uint16)
-    dist.send(torch.from_numpy(hs.view(np.int16)).cuda(), rank + 1)
+    dist.send(torch.from_numpy(hs.view(np.float16)).cuda(), rank + 1)
     if rank == 0:
         t = torch.empty(M, dtype=torch.int32, device="cuda")
         dist.recv(t, world - 1)
@@ -518,19 +505,19 @@ def pipeline_e2e(pkg, torch, ctx, pipe, args, rank, world, barrier, max_over_ran
         mb = j % M
         if rank == 0:
             out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [toks[mb]]})
-            dist.send(torch.from_numpy(out["hidden"].view(np.int16).copy()).cuda(), 1)
+            dist.send(torch.from_numpy(out["hidden"].view(np.float16).copy()).cuda(), 1)
             t = torch.empty(1, dtype=torch.int32, device="cuda")
             dist.recv(t, W - 1)
             toks[mb] = int(t.item())
         else:
-            buf = torch.empty(H, dtype=torch.int16, device="cuda")
+            buf = torch.empty(H, dtype=torch.float16, device="cuda")
             dist.recv(buf, rank - 1)
             out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb],
                                     "hidden": buf.cpu().numpy().view(np.uint16), "temperature": 0})
             if ctx.is_last:
                 dist.send(torch.tensor([out["token_id"]], dtype=torch.int32, device="cuda"), 0)
             else:
-                dist.send(torch.from_numpy(out["hidden"].view(np.int16).copy()).cuda(), rank + 1)
+                dist.send(torch.from_numpy(out["hidden"].view(np.float16).copy()).cuda(), rank + 1)
         pipe.pos[mb] += 1
     torch.cuda.synchronize()
     s = max_over_ranks(time.perf_counter() - t0)

@@ -115,3 +115,39 @@ def plan_gpus(n_layers: int, n_gpus: int, layer_bytes: int, kv_per_layer: int, e
         raise ValueError(f"{n_layers} layers do not fit {n_gpus} GPUs with budgets {budgets}")
     return [{"stage": i, "layers": r, "is_first": i == 0, "is_last": i == len(ranges) - 1, "device_rank": i}
             for i, r in enumerate(ranges)]
+
+
+def pipeline_tick(rank: int, world: int, n_mb: int, n_steps: int, tick: int) -> tuple[list[tuple], int | None]:
+    """The decode pipeline's schedule at one tick, for one stage (rank).
+
+    Stages run one micro-batch step per tick: rank r runs step j = tick - r
+    (micro-batch j % n_mb).  At the start of the tick it receives the input of
+    step j from rank r - 1 and sends the output of step j - 1 to rank r + 1, so
+    every send meets its receive in the same tick on the peer.  The last rank's
+    sampled token of step j goes back to rank 0, arriving at tick j + world, and
+    feeds step j + n_mb (n_mb >= world keeps that arrival in time).
+
+    Returns (ops, mb): ops are ("recv_hidden" | "recv_token" | "send_hidden" |
+    "send_token", micro-batch, peer) to post together before the step, and mb is
+    the micro-batch this rank steps at this tick, or None.
+    """
+    assert n_mb >= world, "need at least as many micro-batches as stages"
+    j = tick - rank
+    ops: list[tuple] = []
+    if rank == 0:
+        jt = tick - world  # the token of step jt arrives now, for step jt + n_mb
+        if world > 1 and 0 <= jt < n_steps and jt + n_mb < n_steps:
+            ops.append(("recv_token", jt % n_mb, world - 1))
+    elif 0 <= j < n_steps:
+        ops.append(("recv_hidden", j % n_mb, rank - 1))
+    if world > 1 and 1 <= j <= n_steps:  # output of step j - 1
+        if rank < world - 1:
+            ops.append(("send_hidden", (j - 1) % n_mb, rank + 1))
+        elif j - 1 + n_mb < n_steps:
+            ops.append(("send_token", (j - 1) % n_mb, 0))
+    return ops, (j % n_mb if 0 <= j < n_steps else None)
+
+
+def pipeline_ticks(world: int, n_steps: int) -> int:
+    """Ticks for n_steps micro-batch steps per stage, fill and drain included."""
+    return n_steps + world
