@@ -547,20 +547,21 @@ int rmsnorm(const float* h, int ldh, const int* rowsel, const float* w, float* o
 
 // ================================================================ embed
 // embedLookup (web/inference-worker.js:509-515) from the repacked embed table
+// grid (row, column block): one element per thread
 __global__ void k_embed(int kind, const uint8_t* data, int vocab, int H, int nb, int cols_pad,
                         const int* __restrict__ ids, float* __restrict__ out, int ldo, int* err) {
-  const int t = blockIdx.x;
+  const int t = blockIdx.x, c = blockIdx.y * blockDim.x + threadIdx.x;
   const int id = ids[t];
   const bool ok = id >= 0 && id < vocab;
-  if (!ok && threadIdx.x == 0) atomicExch(err, 1);
-  for (int c = threadIdx.x; c < H; c += blockDim.x)
-    out[(size_t)t * ldo + c] = ok ? mat_elem(kind, data, nb, cols_pad, (uint64_t)id, c) : 0.f;
+  if (!ok && c == 0) atomicExch(err, 1);
+  if (c < H) out[(size_t)t * ldo + c] = ok ? mat_elem(kind, data, nb, cols_pad, (uint64_t)id, c) : 0.f;
 }
 
 int embed_rows(const Matrix& emb, const int* ids, int T, float* out, int ldo, int* d_err,
                cudaStream_t s) {
   if (T <= 0) return TN_OK;
-  k_embed<<<T, 256, 0, s>>>(emb.kind, emb.data, emb.rows, emb.cols, emb.nb, emb.cols_pad, ids, out, ldo, d_err);
+  k_embed<<<dim3(T, (emb.cols + 255) / 256), 256, 0, s>>>(emb.kind, emb.data, emb.rows, emb.cols, emb.nb,
+                                                          emb.cols_pad, ids, out, ldo, d_err);
   TN_CHECK_LAUNCH();
   return TN_OK;
 }
@@ -700,13 +701,37 @@ __global__ void __launch_bounds__(ATT_WARPS * 32)
   // max / sum live in every lane of that head
   const int my_p = lane / G;
   float m_run = -INFINITY, l_run = 0.f;
+  // when a step's rows fit in registers twice, the next step's K / V rows are
+  // loaded while the current step computes
+  constexpr bool PF = PS * DPL <= 16;
+  float kn[PF ? PS : 1][DPL], vn[PF ? PS : 1][DPL];
+  auto load_step = [&](int p0, float (&kd)[PF ? PS : 1][DPL], float (&vd)[PF ? PS : 1][DPL]) {
+#pragma unroll
+    for (int i = 0; i < (PF ? PS : 1); i++) {
+      const int p = min(p0 + i, whi - 1);  // past the end: a valid row, masked below
+      load_row(kb, p, kd[i]);
+      load_row(vb, p, vd[i]);
+    }
+  };
+  if (PF && wlo < whi) load_step(wlo, kn, vn);
   for (int p0 = wlo; p0 < whi; p0 += PS) {
     float kr[PS][DPL], vr[PS][DPL];
+    if constexpr (PF) {
 #pragma unroll
-    for (int i = 0; i < PS; i++) {
-      const int p = min(p0 + i, whi - 1);  // past the end: a valid row, masked below
-      load_row(kb, p, kr[i]);
-      load_row(vb, p, vr[i]);
+      for (int i = 0; i < PS; i++)
+#pragma unroll
+        for (int d = 0; d < DPL; d++) {
+          kr[i][d] = kn[i % (PF ? PS : 1)][d];
+          vr[i][d] = vn[i % (PF ? PS : 1)][d];
+        }
+      if (p0 + PS < whi) load_step(p0 + PS, kn, vn);
+    } else {
+#pragma unroll
+      for (int i = 0; i < PS; i++) {
+        const int p = min(p0 + i, whi - 1);
+        load_row(kb, p, kr[i]);
+        load_row(vb, p, vr[i]);
+      }
     }
     float v[32];
 #pragma unroll
@@ -986,10 +1011,27 @@ __global__ void __launch_bounds__(SAMPLE_THREADS) k_sample(float* __restrict__ l
   const double temperature = params[3 * row], top_p = params[3 * row + 1], u = params[3 * row + 2];
   const int tid = threadIdx.x;
 
-  // max (and argmax for greedy)
+  // max (and argmax for greedy): four independent running maxima per thread
+  // over 16-byte loads, so the loads of a thread are in flight together
   float bv = -INFINITY;
   int bi = 0;
-  for (int i = tid; i < vocab; i += blockDim.x) argmax_merge(bv, bi, l[i], i);
+  if ((vocab & 3) == 0) {
+    const float4* l4 = reinterpret_cast<const float4*>(l);
+    const int n4 = vocab >> 2;
+    float v4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    int i4[4] = {0, 0, 0, 0};
+    for (int j = tid; j < n4; j += blockDim.x) {
+      const float4 q = l4[j];
+      argmax_merge(v4[0], i4[0], q.x, 4 * j);
+      argmax_merge(v4[1], i4[1], q.y, 4 * j + 1);
+      argmax_merge(v4[2], i4[2], q.z, 4 * j + 2);
+      argmax_merge(v4[3], i4[3], q.w, 4 * j + 3);
+    }
+#pragma unroll
+    for (int k = 0; k < 4; k++) argmax_merge(bv, bi, v4[k], i4[k]);
+  } else {
+    for (int i = tid; i < vocab; i += blockDim.x) argmax_merge(bv, bi, l[i], i);
+  }
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
     const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
