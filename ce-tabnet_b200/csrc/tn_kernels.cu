@@ -198,9 +198,10 @@ int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
     if (m->ws_floats) {
       const size_t wsb = m->ws_floats * sizeof(float);
       TN_CHECK_CUDA(cudaMalloc(&m->ws, wsb));
-      TN_CHECK_CUDA(cudaMalloc(&m->cnt, (size_t)m->tiles * sizeof(int)));
-      TN_CHECK_CUDA(cudaMemsetAsync(m->cnt, 0, (size_t)m->tiles * sizeof(int), s));
-      m->bytes += wsb + (size_t)m->tiles * sizeof(int);
+      TN_CHECK_CUDA(cudaMemsetAsync(m->ws, 0, wsb, s));
+      TN_CHECK_CUDA(cudaMalloc(&m->cnt, m->cnt_ints * sizeof(int)));
+      TN_CHECK_CUDA(cudaMemsetAsync(m->cnt, 0, m->cnt_ints * sizeof(int), s));
+      m->bytes += wsb + m->cnt_ints * sizeof(int);
     }
   } else {
     mv_prepare(m);
@@ -243,7 +244,8 @@ void matrix_free(Matrix* m) {
 }
 
 void matrix_reset_counters(const Matrix& m, cudaStream_t s) {
-  if (m.cnt) cudaMemsetAsync(m.cnt, 0, (size_t)m.tiles * sizeof(int), s);
+  if (m.cnt) cudaMemsetAsync(m.cnt, 0, m.cnt_ints * sizeof(int), s);
+  if (m.ws) cudaMemsetAsync(m.ws, 0, m.ws_floats * sizeof(float), s);
 }
 
 // value of element (r, c) of a repacked matrix

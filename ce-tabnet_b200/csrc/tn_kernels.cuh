@@ -75,6 +75,7 @@ struct Matrix {
   // counters (zero between launches: the CTA that completes a tile resets it)
   size_t ws_floats = 0;
   float* ws = nullptr;
+  size_t cnt_ints = 0;
   int* cnt = nullptr;
 };
 
@@ -131,7 +132,7 @@ bool matvec_dec_ok(const Matrix& m, int T);
 // err: device int set to 1 if a bounded wait inside the kernel gave up
 int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
                int* err, cudaStream_t s);
-// zero the split-K arrival counters (after a launch gave up part way)
+// zero the split-K counters and workspace (after a launch gave up part way)
 void matrix_reset_counters(const Matrix& m, cudaStream_t s);
 int embed_rows(const Matrix& emb, const int* ids, int T, float* out, int ldo, int* d_err,
                cudaStream_t s);

@@ -26,14 +26,15 @@
 //   x to 27 bits relative to its chunk maximum.
 //
 // Work split: K is cut into chunks of up to 8192 elements (one token; 4096
-// for two) whose activation digits fill a 33 KB shared-memory table built by
-// every CTA when it enters the chunk; a chunk of a 16-row tile into
-// sub-chunks of up to 32 (q4) / 16 (q8) block pairs, one ring stage each.
-// Units (chunk, tile, sub-chunk) are handed out in contiguous runs per CTA,
-// so a tile's chunk is usually summed inside one CTA.  A producer warp
-// streams each unit's records (one contiguous bulk copy) into the ring (full /
-// empty mbarriers; a stage is handed back as soon as the consumers hold its
-// operands in registers); eight consumer warps split every unit's pairs,
+// for two) whose activation digits fill a 33 KB shared-memory table; a chunk
+// of a 16-row tile into sub-chunks of up to 32 (q4) / 16 (q8) block pairs,
+// one ring stage each.  Every CTA works on one chunk (one digit table, built
+// once) and streams a contiguous run of its (tile, sub-chunk) units, so a
+// tile's chunk is usually summed inside one CTA.  A producer warp streams
+// each unit's records (one contiguous bulk copy) into the ring with a decoded
+// descriptor of the unit (full / empty mbarriers; a stage is handed back as
+// soon as the consumers hold its operands in registers); eight consumer warps
+// split every unit's pairs,
 // accumulate a tile's chunk in registers and hand the per-warp row sums to an
 // epilogue warp through mbarrier-guarded buffers.  The epilogue warp sums the
 // eight warps in fixed order; a tile whose chunk is whole in this CTA and the
@@ -173,30 +174,14 @@ __device__ __forceinline__ void mmv_store(const MmvArgs& a, int row, int tt, flo
   }
 }
 
-// position (chunk, tile, sub-chunk) of a unit, advanced without divisions
-struct UnitPos {
-  int kc, t, sc;
-  __device__ __forceinline__ UnitPos(int u, int per_chunk, int nsc) {
-    kc = u / per_chunk;
-    const int r = u - kc * per_chunk;
-    t = r / nsc;
-    sc = r - t * nsc;
-  }
-  __device__ __forceinline__ void next(int nsc, int tiles) {
-    if (++sc == nsc) {
-      sc = 0;
-      if (++t == tiles) {
-        t = 0;
-        ++kc;
-      }
-    }
-  }
-};
+// Work partition.  CTA b works on K chunk b % ks only (one digit table per
+// CTA); the gk CTAs of a chunk split its units u = t * nsc + sc (tile t,
+// sub-chunk sc) into contiguous runs of NSU / gk units (rounded), at least nsc
+// each, so a (tile, chunk) is split into at most two pieces: part 0 from
+// sub-chunk 0, part 1 from a later one.
+__host__ __device__ __forceinline__ int mmv_chunk_ctas(int grid, int ks, int kc) { return (grid - kc + ks - 1) / ks; }
+constexpr int kPieceEnd = 1 << 16;  // unit descriptor flag (with the sub-chunk): the last unit of a piece
 
-// Units are (tile t, K chunk kc, sub-chunk sc), chunk major then tile major,
-// u = (kc * tiles + t) * nsc + sc, in contiguous runs per CTA; a run holds at
-// least nsc units, so the sub-chunks of one (tile, chunk) fall into at most
-// two runs ("pieces": part 0 starts at sc = 0, part 1 after a run boundary).
 template <int KIND, int TT>
 __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
   constexpr int AB = tile_a_bytes(KIND), REC = tile_rec_bytes(KIND);
@@ -216,14 +201,17 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
   __shared__ __align__(8) uint64_t red_empty[MMV_NB];
   __shared__ __align__(8) uint64_t ss_bar;  // the consumers' sums of squares are in sred
   __shared__ int last_unit[MMV_MAX_STAGES];
+  __shared__ int4 udesc[MMV_MAX_STAGES];  // unit in each stage: tile (-1: no more), sub-chunk | kPieceEnd, first pair, pairs
+  __shared__ int rmeta[MMV_NB][3];       // piece in each buffer: tile (-1: no more), first sub-chunk, units
   __shared__ double sred[MMV_NW][TT];
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NSU = a.tiles * a.nsc;  // units per chunk
-  const int NU = a.ks * NSU;
-  const int u0 = (int)((int64_t)NU * blockIdx.x / gridDim.x);
-  const int nu = (int)((int64_t)NU * (blockIdx.x + 1) / gridDim.x) - u0;
+  const int kc0 = blockIdx.x % a.ks, gk = mmv_chunk_ctas(gridDim.x, a.ks, kc0);
+  const int jc = blockIdx.x / a.ks;
+  const int s_begin = (int)((int64_t)NSU * jc / gk), s_end = (int)((int64_t)NSU * (jc + 1) / gk);
+  const int np0 = min(a.ckp, a.pairs - kc0 * a.ckp);  // pairs of the chunk
 
   if (tid == 0) {
     abort_flag = 0;
@@ -246,10 +234,10 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
 
   if (warp == MMV_NW + MMV_NE) {
     // ======================= producer: one bulk copy per unit into the ring
-    // (weights do not depend on the previous kernel: no wait for it)
+    // (weights do not depend on the previous kernel: no wait for it), then a
+    // descriptor without a unit
     if (lane == 0) {
-      UnitPos up(u0, NSU, a.nsc);
-      for (int k = 0; k < nu; k++, up.next(a.nsc, a.tiles)) {
+      for (int u = s_begin, k = 0; u <= s_end; u++, k++) {
         const int st = k % a.stages;
         if (k >= a.stages) {
           // every consumer warp has read the unit this stage held
@@ -257,19 +245,69 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
         if (abort_flag) break;
-        const int kc = up.kc, t = up.t, first = up.sc * a.scp;
-        const int n = max(0, min(a.scp, min(a.ckp, a.pairs - kc * a.ckp) - first));
+        if (u == s_end) {
+          udesc[st] = make_int4(-1, 0, 0, 0);
+          mbar_expect_tx(&full[st], 0);
+          break;
+        }
+        const int t = u / a.nsc, sc = u - t * a.nsc, first = sc * a.scp, n = max(0, min(a.scp, np0 - first));
         const uint32_t bytes = (uint32_t)n * REC;
+        udesc[st] = make_int4(t, sc | (u == s_end - 1 || sc == a.nsc - 1 ? kPieceEnd : 0), first, n);
         last_unit[st] = k;
         mbar_expect_tx(&full[st], bytes);  // an empty sub-chunk completes on this arrival alone
         if (bytes)
           bulk_g2s(ring + (size_t)st * a.stage_bytes,
-                   a.data + ((size_t)t * a.pairs + (size_t)kc * a.ckp + first) * REC, bytes, &full[st]);
+                   a.data + ((size_t)t * a.pairs + (size_t)kc0 * a.ckp + first) * REC, bytes, &full[st]);
       }
     }
   } else if (warp < MMV_NW) {
     // ======================= consumers
     const int g = lane >> 2, c = lane & 3;
+    // Activation digits are built by each warp for exactly the block pairs it
+    // multiplies -- pairs sc * scp + 8 j + warp of the chunk -- with its own
+    // power-of-two scale, so no CTA-wide step stands between the predecessor
+    // kernel's output and the first MMA.  A lane covers one float4 of a pair:
+    // elements 4 l .. 4 l + 3 (l = lane & 15), i.e. block 2p + (l >> 3),
+    // elements 4 (l & 7) .., whose digits go to word 16 p + wl of each plane.
+    constexpr int WP = CP / MMV_NW;  // most pairs of a chunk per warp
+    constexpr int IT = WP / 2;       // two pairs per step
+    const int l16 = lane & 15;
+    const int wl = (l16 >> 3) * 8 + (l16 & 3) * 2 + ((l16 >> 2) & 1);
+    // pair of step it of chunk kc and whether this warp multiplies it
+    auto pair_of = [&](int kc, int it, bool& ok) {
+      const int i = 2 * it + (lane >> 4), sc = i / PPW, jj = i - sc * PPW;
+      const int pc = sc * a.scp + 8 * jj + warp;
+      ok = 8 * jj + warp < a.scp && pc < min(a.ckp, a.pairs - kc * a.ckp);
+      return pc;
+    };
+    // The RMSNorm weights of a chunk (static: no wait for the predecessor) are
+    // parked in the words of digit planes 0..3 that this lane later fills with
+    // its own digits, so only this lane reads them back.
+    auto stage_w = [&](int kc) {
+#pragma unroll
+      for (int it = 0; it < IT; it++) {
+        bool ok;
+        const int pc = pair_of(kc, it, ok), col = kc * a.ckp * 64 + pc * 64 + l16 * 4;
+        if (!ok) continue;
+        float4 w4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (col < a.cols) {
+          if ((reinterpret_cast<uintptr_t>(a.f.norm_w) & 15) == 0) {
+            w4 = *reinterpret_cast<const float4*>(a.f.norm_w + col);
+          } else {
+            w4.x = a.f.norm_w[col];
+            w4.y = a.f.norm_w[col + 1];
+            w4.z = a.f.norm_w[col + 2];
+            w4.w = a.f.norm_w[col + 3];
+          }
+        }
+        float* pw = reinterpret_cast<float*>(planes) + pc * 16 + wl;
+        pw[0] = w4.x;
+        pw[DS] = w4.y;
+        pw[2 * DS] = w4.z;
+        pw[3 * DS] = w4.w;
+      }
+    };
+    if (a.f.norm_w != nullptr) stage_w(kc0);
     pdl_wait();  // x is produced by the predecessor kernel
     const float* xrow[TT];
     bool xvec = true;
@@ -278,7 +316,6 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
       xrow[tt] = a.x + (size_t)(tt < a.T ? (a.f.rowsel ? a.f.rowsel[tt] : tt) : 0) * a.ldx;
       xvec = xvec && (reinterpret_cast<uintptr_t>(xrow[tt]) & 15) == 0;
     }
-    const bool wvec = a.f.norm_w == nullptr || (reinterpret_cast<uintptr_t>(a.f.norm_w) & 15) == 0;
 
     // RMSNorm (web/inference-worker.js:516-522) is applied to the row sums:
     // y = inv * W (x o w), inv = 1 / sqrt(mean(x^2) + 1e-5), computed by the
@@ -302,30 +339,16 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
       if (lane == 0) mbar_arrive(&ss_bar);
     }
 
-    // Activation digits are built by each warp for exactly the block pairs it
-    // multiplies -- pairs sc * scp + 8 j + warp of the chunk -- with its own
-    // power-of-two scale, so no CTA-wide step stands between the predecessor
-    // kernel's output and the first MMA.
-    constexpr int WP = CP / MMV_NW;  // most pairs of a chunk per warp
-    constexpr int IT = WP / 2;       // a lane covers one float4 of a pair, two pairs per step
     float fa[TT], fb[TT];
     auto setup = [&](int kc) {
-      const int e0 = kc * a.ckp * 64, np = min(a.ckp, a.pairs - kc * a.ckp);
+      const int e0 = kc * a.ckp * 64;
       float v[TT][IT][4];
-      int word[IT];
-      bool ok[IT];
-      double ss[TT];
-#pragma unroll
-      for (int tt = 0; tt < TT; tt++) ss[tt] = 0.0;
-      // all loads first (x, then the norm weights), 16 bytes at a time
+      // every x load is issued before any is used, so they are all in flight at once
 #pragma unroll
       for (int it = 0; it < IT; it++) {
-        const int i = 2 * it + (lane >> 4), sc = i / PPW, jj = i - sc * PPW;
-        const int pc = sc * a.scp + 8 * jj + warp, el = pc * 64 + (lane & 15) * 4, col = e0 + el;
-        ok[it] = 8 * jj + warp < a.scp && pc < np;
-        const int blk = el >> 5, j = el & 31;
-        word[it] = (blk * 4 + ((j & 15) >> 2)) * 2 + (j >> 4);
-        const bool valid = ok[it] && col < a.cols;  // col % 4 == 0 and cols % 32 == 0
+        bool ok;
+        const int pc = pair_of(kc, it, ok), col = e0 + pc * 64 + l16 * 4;
+        const bool valid = ok && col < a.cols;  // col % 4 == 0 and cols % 32 == 0
 #pragma unroll
         for (int tt = 0; tt < TT; tt++) {
           float4 xv = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -344,70 +367,75 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
           v[tt][it][2] = xv.z;
           v[tt][it][3] = xv.w;
         }
-        if (a.f.norm_w) {
-          float4 wv = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (valid) {
-            if (wvec) {
-              wv = *reinterpret_cast<const float4*>(a.f.norm_w + col);
-            } else {
-              wv.x = a.f.norm_w[col];
-              wv.y = a.f.norm_w[col + 1];
-              wv.z = a.f.norm_w[col + 2];
-              wv.w = a.f.norm_w[col + 3];
-            }
-          }
-          const float wn[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-          for (int tt = 0; tt < TT; tt++)
-#pragma unroll
-            for (int m = 0; m < 4; m++) {
-              const float xv = v[tt][it][m];
-              ss[tt] = fma((double)xv, (double)xv, ss[tt]);
-              v[tt][it][m] = xv * wn[m];
-            }
-        }
       }
-      if (ss_in_setup) {
+      if (a.f.norm_w) {
+        if (ss_in_setup) {
 #pragma unroll
-        for (int tt = 0; tt < TT; tt++) {
-          for (int o = 16; o > 0; o >>= 1) ss[tt] += __shfl_xor_sync(FULL, ss[tt], o);
-          if (lane == 0) sred[warp][tt] = ss[tt];
+          for (int tt = 0; tt < TT; tt++) {
+            double ss = 0.0;
+#pragma unroll
+            for (int it = 0; it < IT; it++)
+#pragma unroll
+              for (int m = 0; m < 4; m++) ss = fma((double)v[tt][it][m], (double)v[tt][it][m], ss);
+            for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
+            if (lane == 0) sred[warp][tt] = ss;
+          }
+        }
+        // the parked weights, read back before this lane writes any digit
+#pragma unroll
+        for (int it = 0; it < IT; it++) {
+          bool ok;
+          const float* pw = reinterpret_cast<const float*>(planes) + pair_of(kc, it, ok) * 16 + wl;
+          if (!ok) continue;
+#pragma unroll
+          for (int m = 0; m < 4; m++) {
+            const float wv = pw[m * DS];
+#pragma unroll
+            for (int tt = 0; tt < TT; tt++) v[tt][it][m] *= wv;
+          }
         }
       }
 #pragma unroll
       for (int tt = 0; tt < TT; tt++) {
-        float M = 0.f;
+        // largest magnitude: on the bit patterns of |v|, where every NaN and
+        // infinity lies at or above that of +inf
+        uint32_t mb = 0u;
 #pragma unroll
         for (int it = 0; it < IT; it++)
 #pragma unroll
-          for (int m = 0; m < 4; m++) {
-            float ax = fabsf(v[tt][it][m]);
-            if (!(ax <= FLT_MAX)) ax = INFINITY;  // NaN counts as non-finite
-            M = fmaxf(M, ax);
-          }
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(FULL, M, o));
-        const bool bad = !(M <= FLT_MAX);
-        const int sh = (!bad && M > 0.f) ? 26 - ilogbf(M) : 0;
+          for (int m = 0; m < 4; m++) mb = max(mb, __float_as_uint(v[tt][it][m]) & 0x7fffffffu);
+        for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(FULL, mb, o));
+        const bool bad = mb >= 0x7f800000u;
+        const int sh = (!bad && mb != 0u) ? 26 - ilogbf(__uint_as_float(mb)) : 0;
         const int sa = sh >> 1, sb = sh - sa;
         const float pa = exp2i(sa), pb = exp2i(sb);
         fa[tt] = bad ? __int_as_float(0x7fc00000) : exp2i(-sa) * (KIND == MK_Q4 ? 0.0625f : 1.f);
         fb[tt] = exp2i(-sb);
 #pragma unroll
         for (int it = 0; it < IT; it++) {
-          if (!ok[it]) continue;
-          uint32_t p0 = 0, p1 = 0, p2 = 0, p3 = 0;
+          bool ok;
+          const int pc = pair_of(kc, it, ok);
+          if (!ok) continue;
+          // X = d0 + 2^7 d1 + 2^14 d2 + 2^21 d3 -> bytes (d0, d1, d2, d3) of one
+          // word: each step doubles the bits above a digit, opening a zero bit
+          // at 7, 15, 23 (u + (u & ~m) = (u & m) + 2 (u - (u & m)), modulo 2^32)
+          uint32_t dw[4];
 #pragma unroll
           for (int m = 0; m < 4; m++) {
-            const int X = __float2int_rn((v[tt][it][m] * pa) * pb);
-            p0 |= (uint32_t)(X & 127) << (8 * m);
-            p1 |= (uint32_t)((X >> 7) & 127) << (8 * m);
-            p2 |= (uint32_t)((X >> 14) & 127) << (8 * m);
-            p3 |= (uint32_t)((X >> 21) & 255) << (8 * m);
+            uint32_t u = (uint32_t)__float2int_rn((v[tt][it][m] * pa) * pb);
+            u += u & ~0x7fu;
+            u += u & ~0x7fffu;
+            u += u & ~0x7fffffu;
+            dw[m] = u;
           }
-          planes[(tt * 4 + 0) * DS + word[it]] = p0;
-          planes[(tt * 4 + 1) * DS + word[it]] = p1;
-          planes[(tt * 4 + 2) * DS + word[it]] = p2;
-          planes[(tt * 4 + 3) * DS + word[it]] = p3;
+          // 4 x 4 byte transpose: plane d gets byte d of the four elements
+          const uint32_t t0 = __byte_perm(dw[0], dw[1], 0x5140), t1 = __byte_perm(dw[0], dw[1], 0x7362);
+          const uint32_t t2 = __byte_perm(dw[2], dw[3], 0x5140), t3 = __byte_perm(dw[2], dw[3], 0x7362);
+          uint32_t* pw = planes + tt * 4 * DS + pc * 16 + wl;
+          pw[0] = __byte_perm(t0, t2, 0x5410);
+          pw[DS] = __byte_perm(t0, t2, 0x7632);
+          pw[2 * DS] = __byte_perm(t1, t3, 0x5410);
+          pw[3 * DS] = __byte_perm(t1, t3, 0x7632);
         }
       }
       __syncwarp();
@@ -431,22 +459,18 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     }
     // weights of the digit columns this lane accumulates: 2^(7 digit)
     const float wlo = (c & 1) ? 16384.f : 1.f, whi = (c & 1) ? 2097152.f : 128.f;
-    int cur_kc = -1, pi = 0;
+    setup(kc0);  // the only chunk this CTA works on
+    int pi = 0, sc0 = -1;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    // Every consumer runs every iteration even after an abort (then it only
-    // skips the math), so the arrival counts of the mbarriers stay consistent.
-    UnitPos up(u0, NSU, a.nsc);
-    for (int k = 0; k < nu; k++, up.next(a.nsc, a.tiles)) {
-      const int kc = up.kc, sc = up.sc;
-      if (kc != cur_kc) {
-        setup(kc);
-        cur_kc = kc;
-      }
+    for (int k = 0;; k++) {
       const int st = k % a.stages;
-      const bool ready = __all_sync(FULL, mbar_wait(&full[st], (k / a.stages) & 1, &abort_flag));
+      if (!__all_sync(FULL, mbar_wait(&full[st], (k / a.stages) & 1, &abort_flag))) break;
+      const int4 d = udesc[st];
+      if (d.x < 0) break;
+      const int t = d.x, sc = d.y & (kPieceEnd - 1), first = d.z, n = d.w;
+      if (sc0 < 0) sc0 = sc;
       const uint8_t* sbase = ring + (size_t)st * a.stage_bytes;
-      const int first = sc * a.scp, n = max(0, min(a.scp, min(a.ckp, a.pairs - kc * a.ckp) - first));
-      if (ready) {
+      {
         // all pairs' operands first, so their load -> MMA -> FMA chains overlap.
         // A stage has room for SC pairs, so slot j * NW + warp is always inside
         // it; slots past the sub-chunk's n pairs hold stale bytes and get scale 0.
@@ -524,11 +548,8 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
         };
         if (n == SC) compute(std::true_type{});
         else compute(std::false_type{});
-      } else {
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[st]);
       }
-      if (sc != a.nsc - 1 && k != nu - 1) continue;  // the piece goes on
+      if (!(d.y & kPieceEnd)) continue;  // the piece goes on
       // end of a piece: recombine the digit columns, sum the lanes of a row,
       // undo the 2^s scaling, hand the 16 (x TT) row sums to the epilogue
       float vg = fmaf(acc[1], whi, acc[0] * wlo), vh = fmaf(acc[3], whi, acc[2] * wlo);
@@ -548,20 +569,34 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
         red[b][warp][tt * 16 + g] = vg;
         red[b][warp][tt * 16 + g + 8] = vh;
       }
+      if (warp == 0 && lane == 0) {
+        rmeta[b][0] = t;
+        rmeta[b][1] = sc0;
+        rmeta[b][2] = sc - sc0 + 1;
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_full[b]);
       pi++;
+      sc0 = -1;
       acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+    }
+    // no more pieces
+    {
+      const int b = pi % MMV_NB;
+      if (pi >= MMV_NB) mbar_wait(&red_empty[b], ((pi / MMV_NB) - 1) & 1, &abort_flag);
+      if (warp == 0 && lane == 0) rmeta[b][0] = -1;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_full[b]);
     }
   } else {
     // ======================= epilogue warps
-    // Pieces are numbered in unit order; warp e takes batches of MMV_UB
-    // consecutive pieces (e * UB, then every NE * UB).  A whole (tile, chunk)
-    // with one chunk is final at once; other pieces go to the workspace, and
-    // their arrivals (counted in units) are published with one release-atomic
-    // per piece issued from UB lanes at once.
+    // Pieces come in the consumers' order.  A whole (tile, chunk) with one
+    // chunk is final at once; other pieces go to the workspace, and their
+    // arrivals (counted in units) are published in batches of MMV_UB, one
+    // release-atomic per piece issued from UB lanes at once.
+    static_assert(MMV_NE == 1, "one epilogue warp");
     pdl_wait();  // y, the KV cache and the step's row table belong to earlier kernels
-    const int e = warp - MMV_NW, target = a.ks * a.nsc;
+    const int target = a.ks * a.nsc;
     // RMSNorm factor of this lane's token, from the consumers' sums of squares
     double inv = 1.0;
     if (a.f.norm_w) {
@@ -629,38 +664,33 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
       nbat = 0;
       bad = false;
     };
-    int pi = 0, pstart = 0;
-    UnitPos up(u0, NSU, a.nsc);
-    for (int k = 0; k < nu; k++, up.next(a.nsc, a.tiles)) {
-      const int kc = up.kc, t = up.t, sc = up.sc;
-      if (sc != a.nsc - 1 && k != nu - 1) continue;
-      // piece pi: units pstart .. k, sub-chunks sc0 .. sc of (t, kc)
-      const int cnt_u = k - pstart + 1, sc0 = sc - (k - pstart);
-      if ((pi / MMV_UB) % MMV_NE == e) {
-        const int b = pi % MMV_NB;
-        const bool ok = mbar_wait(&red_full[b], (pi / MMV_NB) & 1, &abort_flag);
-        float v = 0.f;
-        if (lane < NV) {
-#pragma unroll
-          for (int w = 0; w < MMV_NW; w++) v += red[b][w][lane];
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&red_empty[b]);
-        bad = bad || __any_sync(FULL, !ok || abort_flag);
-        const bool whole = sc0 == 0 && sc == a.nsc - 1;
-        if (!(whole && a.ks == 1) && lane < NV) {
-          float* w0 = a.ws + (((size_t)kc * a.tiles + t) * 2 + (sc0 == 0 ? 0 : 1)) * 32 + lane;
-          *w0 = v;
-          if (whole) w0[32] = 0.f;  // no second part
-        }
-        vb[nbat] = v;
-        tb[nbat] = t;
-        ub[nbat] = cnt_u;
-        fb_[nbat] = whole;
-        if (++nbat == MMV_UB) flush();
+    for (int pi = 0;; pi++) {
+      const int b = pi % MMV_NB;
+      const bool ok = __all_sync(FULL, mbar_wait(&red_full[b], (pi / MMV_NB) & 1, &abort_flag));
+      const int t = rmeta[b][0], sc0 = rmeta[b][1], cnt_u = rmeta[b][2];
+      if (!ok || abort_flag) {
+        bad = true;
+        break;
       }
-      pi++;
-      pstart = k + 1;
+      if (t < 0) break;
+      float v = 0.f;
+      if (lane < NV) {
+#pragma unroll
+        for (int w = 0; w < MMV_NW; w++) v += red[b][w][lane];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&red_empty[b]);
+      const bool whole = sc0 == 0 && cnt_u == a.nsc;
+      if (!(whole && a.ks == 1) && lane < NV) {
+        float* w0 = a.ws + (((size_t)kc0 * a.tiles + t) * 2 + (sc0 == 0 ? 0 : 1)) * 32 + lane;
+        *w0 = v;
+        if (whole) w0[32] = 0.f;  // no second part
+      }
+      vb[nbat] = v;
+      tb[nbat] = t;
+      ub[nbat] = cnt_u;
+      fb_[nbat] = whole;
+      if (++nbat == MMV_UB) flush();
     }
     if (nbat) flush();
   }
@@ -729,7 +759,7 @@ static void mmv_pick(MmShape* sh) {
 
 int mm_prepare(Matrix* m) {
   TN_REQUIRE(m->kind == MK_Q4 || m->kind == MK_Q8, TN_EINVAL, "mm_prepare: kind %d", m->kind);
-  int ks_max = 1;
+  size_t ws = 0;
   for (int tt = 1; tt <= 2; tt++) {
     MmShape& sh = m->mm[tt - 1];
     const int cp = MMV_CE / tt / 64, scmax = mmv_sc(m->kind);
@@ -738,7 +768,7 @@ int mm_prepare(Matrix* m) {
     sh.nsc = (sh.ckp + scmax - 1) / scmax;
     sh.scp = (sh.ckp + sh.nsc - 1) / sh.nsc;
     sh.stage_bytes = (uint32_t)scmax * tile_rec_bytes(m->kind);  // room for a full sub-chunk
-    ks_max = std::max(ks_max, sh.ks);
+    ws = std::max(ws, (size_t)sh.ks * m->tiles * 2 * 32);
     // (set once per matrix, outside any stream capture)
     if (m->kind == MK_Q4) {
       if (tt == 1) mmv_pick<MK_Q4, 1>(&sh);
@@ -748,7 +778,8 @@ int mm_prepare(Matrix* m) {
       else mmv_pick<MK_Q8, 2>(&sh);
     }
   }
-  m->ws_floats = (size_t)ks_max * m->tiles * 2 * 32;
+  m->ws_floats = ws;                          // two 32-float parts per (chunk, tile)
+  m->cnt_ints = (size_t)m->tiles;  // per-tile arrival counters
   return TN_OK;
 }
 
@@ -756,9 +787,8 @@ template <int KIND, int TT>
 static int launch_mmv(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
                       const MvFuse& f, int* err, cudaStream_t s) {
   const MmShape& sh = m.mm[TT - 1];
-  const int NU = m.tiles * sh.nsc * sh.ks;
-  // at least nsc units per CTA, so a (tile, chunk) spans at most two CTAs
-  const int grid = std::max(1, std::min(NU / sh.nsc, sh.ctas * num_sms()));
+  // at most one CTA per (tile, chunk), at least one per chunk
+  const int grid = std::max(sh.ks, std::min(m.tiles * sh.ks, sh.ctas * num_sms()));
   const MmvArgs a{m.data, m.rows, m.tiles, m.pairs, m.cols, T, x, ldx, y, ldy, mode, sh.ks, sh.ckp, sh.nsc,
                   sh.scp, sh.stages, sh.stage_bytes, err, m.cnt, m.ws, f};
   TN_CHECK_CUDA(launch_pdl(k_mmv<KIND, TT>, dim3(grid), dim3(MMV_THREADS), (size_t)sh.smem, s, a));
