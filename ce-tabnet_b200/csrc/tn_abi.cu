@@ -113,36 +113,25 @@ extern "C" void tn_matrix_free(tn_matrix* m) {
   delete m;
 }
 
-// caller scratch: [row table][arrival counters][split partials], 256-byte aligned pieces
-static size_t attn_rows_bytes(int n_rows) { return ((size_t)n_rows * sizeof(RowInfo) + 255) & ~(size_t)255; }
-static size_t attn_cnt_bytes(int n_rows, int n_kv_heads) {
-  return ((size_t)n_rows * n_kv_heads * sizeof(int) + 255) & ~(size_t)255;
-}
-static size_t attn_total_scratch(int n_rows, int n_heads, int n_kv_heads, int head_dim, int max_ctx) {
-  return attn_rows_bytes(n_rows) + attn_cnt_bytes(n_rows, n_kv_heads) +
-         attn_scratch_bytes(n_rows, n_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx));
-}
+// caller scratch: the row table (the splits merge on chip)
+static size_t attn_total_scratch(int n_rows) { return ((size_t)n_rows * sizeof(RowInfo) + 255) & ~(size_t)255; }
 
-// row table + zeroed counters, then the one-kernel attention
+// row table, then the one-kernel attention
 static int attn_run(int n_rows, int n_slots, int n_heads, int n_kv_heads, int head_dim, int max_ctx, const float* d_q,
                     const float* d_k, const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
                     void* scratch, cudaStream_t s) {
   RowInfo* rows = (RowInfo*)scratch;
-  int* cnt = (int*)((char*)scratch + attn_rows_bytes(n_rows));
-  void* part = (char*)cnt + attn_cnt_bytes(n_rows, n_kv_heads);
   k_rows_from_slots<<<(n_rows + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows);
   TN_CHECK_LAUNCH();
-  TN_CHECK_CUDA(cudaMemsetAsync(cnt, 0, (size_t)n_rows * n_kv_heads * sizeof(int), s));
   const size_t kvh_stride = (size_t)max_ctx * head_dim;
   return attention(d_q, n_heads * head_dim, d_k, d_v, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows, n_heads,
-                   n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out, n_heads * head_dim, part,
-                   cnt, s);
+                   n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out, n_heads * head_dim, s);
 }
 
 extern "C" uint64_t tn_attention_scratch_bytes(int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,
                                                int32_t head_dim, int32_t max_ctx) {
   if (n_rows <= 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || max_ctx <= 0) return 0;
-  return attn_total_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx);
+  return attn_total_scratch(n_rows);
 }
 
 extern "C" int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
@@ -159,7 +148,7 @@ extern "C" int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, in
   TN_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128, TN_EUNSUPPORTED,
              "tn_attention: head_dim %d unsupported", head_dim);
   if (n_rows == 0) return TN_OK;
-  const size_t need = attn_total_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx);
+  const size_t need = attn_total_scratch(n_rows);
   TN_REQUIRE(scratch_bytes >= need, TN_EINVAL, "tn_attention: scratch of %llu bytes, %zu needed",
              (unsigned long long)scratch_bytes, need);
   return attn_run(n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v, d_slot, d_len, d_out,
@@ -204,11 +193,11 @@ extern "C" int tn_attention_static(int32_t n_rows, int32_t n_slots, int32_t n_he
   TN_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128, TN_EUNSUPPORTED,
              "tn_attention_static: head_dim %d unsupported", head_dim);
   if (n_rows == 0) return TN_OK;
-  const size_t need = attn_total_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx);
+  const size_t need = attn_total_scratch(n_rows);
   TN_REQUIRE(need <= TN_ATTENTION_STATIC_SCRATCH_BYTES, TN_ECAPACITY,
-             "tn_attention_static: %d rows x %d heads need %zu bytes of scratch, above the fixed %u; "
+             "tn_attention_static: %d rows need %zu bytes of scratch, above the fixed %u; "
              "use tn_attention with caller scratch",
-             n_rows, n_heads, need, (unsigned)TN_ATTENTION_STATIC_SCRATCH_BYTES);
+             n_rows, need, (unsigned)TN_ATTENTION_STATIC_SCRATCH_BYTES);
   void* scratch = nullptr;
   const int rc = attn_static_scratch(&scratch);
   if (rc) return rc;

@@ -7,7 +7,11 @@
 // rotation, softmax normaliser of the sampler) are evaluated in double here too.
 #include <cfloat>
 
+#include <cooperative_groups.h>
+
 #include "tn_kernels.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tn {
 
@@ -646,25 +650,23 @@ int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs,
 // are reduce-scattered over the warp so that lane l ends with the full score
 // of (position l / G, head l % G) -- every exp is computed once -- and an
 // online softmax per head rescales the lane's G x HD/32 output accumulators.
-// The warps merge in shared memory; with several splits, the CTA writes its
-// (max, sum, unnormalised output) partial and the last CTA of the (row, KV
-// head) merges the splits in split order (deterministic) and resets the
-// arrival counter.
+// The warps merge in shared memory; with several splits, the splits of a
+// (row, KV head) run as one thread-block cluster and merge through
+// distributed shared memory, in split order (deterministic).
 constexpr int ATT_WARPS = 8;
 
 template <int HD, int G>
 __global__ void __launch_bounds__(ATT_WARPS * 32)
     k_attn(const float* __restrict__ q, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
            size_t slot_stride, size_t kvh_stride, const RowInfo* __restrict__ rows, int S, float scale,
-           float* __restrict__ out, int ldo, float* __restrict__ part, int* __restrict__ cnt) {
-  constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD, PW = GH + 2 * G;  // partial: o[G][HD], m[G], l[G]
+           float* __restrict__ out, int ldo) {
+  constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD;
   constexpr unsigned FULL = 0xffffffffu;
   __shared__ float s_m[ATT_WARPS][G], s_l[ATT_WARPS][G];
   __shared__ __align__(16) float s_o[ATT_WARPS][GH];
-  __shared__ float s_w[64][G];  // merge weights exp(m - M) (warps, or splits <= 64)
+  __shared__ float s_w[ATT_WARPS][G];  // merge weights exp(m - M) of the warps
   __shared__ float s_M[G], s_L[G];
-  __shared__ int s_last;
-  const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z, nKV = gridDim.y;
+  const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_launch_dependents();
   pdl_wait();  // q and the cache rows of this step come from the previous kernels
@@ -773,7 +775,8 @@ __global__ void __launch_bounds__(ATT_WARPS * 32)
         for (int d = 0; d < DPL; d++) acc[h][d] = fmaf(w, vr[i][d], acc[h][d]);
       }
   }
-  // merge the warps
+  // merge the warps; the CTA's partial (unnormalised output relative to its
+  // per-head max, the max, the sum) stays in shared memory
   if (lane < G) {
     s_m[warp][lane] = m_run;
     s_l[warp][lane] = l_run;
@@ -796,74 +799,56 @@ __global__ void __launch_bounds__(ATT_WARPS * 32)
     s_L[tid] = Lsum;
   }
   __syncthreads();
-  float* my_part = part + (((size_t)t * nKV + kvh) * S + split) * PW;
+  float* const c_o = s_o[0];  // element e is read and rewritten by one thread only
   for (int e = tid; e < GH; e += ATT_WARPS * 32) {
     const int h = e / HD;
     float o = 0.f;
     for (int w = 0; w < ATT_WARPS; w++) o = fmaf(s_o[w][e], s_w[w][h], o);
     if (S == 1) out[(size_t)t * ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
-    else my_part[e] = o;
+    else c_o[e] = o;
   }
   if (S == 1) return;
-  if (tid < G) {
-    my_part[GH + tid] = s_M[tid];
-    my_part[GH + G + tid] = s_L[tid];
-  }
-  // publish the partial; the last CTA of the (row, KV head) merges
-  __syncthreads();
-  if (tid == 0) {
-    __threadfence();
-    s_last = atomicAdd(&cnt[t * nKV + kvh], 1) == S - 1;
-  }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  const float* pbase = part + ((size_t)t * nKV + kvh) * S * PW;
-  if (tid < G) {
-    float M = -INFINITY;
-    for (int sp = 0; sp < S; sp++) M = fmaxf(M, __ldcg(pbase + (size_t)sp * PW + GH + tid));
-    float Lsum = 0.f;
-    for (int sp = 0; sp < S; sp++) {
-      const float ms = __ldcg(pbase + (size_t)sp * PW + GH + tid);
-      const float f = ms == -INFINITY ? 0.f : expf(ms - M);
-      s_w[sp][tid] = f;
-      Lsum += __ldcg(pbase + (size_t)sp * PW + GH + G + tid) * f;
-    }
-    s_L[tid] = Lsum;
-  }
-  __syncthreads();
-  for (int e = tid; e < GH; e += ATT_WARPS * 32) {
+  // The splits of this (row, KV head) are one thread-block cluster: after the
+  // barrier, split r finalises outputs [r GH / S, (r + 1) GH / S) from every
+  // split's partial, read from the others' shared memory in split order.
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  for (int e = GH * split / S + tid; e < GH * (split + 1) / S; e += ATT_WARPS * 32) {
     const int h = e / HD;
-    float o = 0.f;
-    for (int sp = 0; sp < S; sp++) o = fmaf(__ldcg(pbase + (size_t)sp * PW + e), s_w[sp][h], o);
-    out[(size_t)t * ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
+    float M = -INFINITY;
+    for (int c = 0; c < S; c++) M = fmaxf(M, *cluster.map_shared_rank(&s_M[h], c));
+    float Lsum = 0.f, o = 0.f;
+    for (int c = 0; c < S; c++) {
+      const float mc = *cluster.map_shared_rank(&s_M[h], c);
+      const float f = mc == -INFINITY ? 0.f : expf(mc - M);
+      Lsum += *cluster.map_shared_rank(&s_L[h], c) * f;
+      o = fmaf(*cluster.map_shared_rank(&c_o[e], c), f, o);
+    }
+    out[(size_t)t * ldo + (kvh * G + h) * HD + e % HD] = Lsum > 0.f ? o / Lsum : 0.f;
   }
-  if (tid == 0) cnt[t * nKV + kvh] = 0;  // ready for the next call
+  cluster.sync();  // no CTA leaves while another still reads its shared memory
 }
 
 int attn_splits(int T, int nKV, int max_ctx) {
-  // about one CTA per SM, at least 128 positions of the longest row per split, at most 64 splits
+  // about one CTA per SM, at least 128 positions of the longest row per split,
+  // at most a portable cluster (8) of splits
   const int want = (num_sms() + T * nKV - 1) / (T * nKV);
-  const int cap = std::max(1, std::min(64, (max_ctx + 127) / 128));
+  const int cap = std::max(1, std::min(8, (max_ctx + 127) / 128));
   return std::max(1, std::min(want, cap));
-}
-
-size_t attn_scratch_bytes(int T, int nH, int hd, int n_splits) {
-  return (((size_t)T * nH * n_splits * (hd + 2) * sizeof(float)) + 255) & ~(size_t)255;
 }
 
 template <int HD>
 static int launch_attn_hd(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
                           size_t kvh_stride, const RowInfo* rows, int T, int nKV, int G, int n_splits, float* out,
-                          int ldo, float* part, int* cnt, cudaStream_t s) {
+                          int ldo, cudaStream_t s) {
   const dim3 grid(n_splits, nKV, T);
   const float scale = (float)(1.0 / sqrt((double)HD));
   cudaError_t e;
   switch (G) {
 #define TN_ATT_CASE(g)                                                                                          \
   case g:                                                                                                       \
-    e = launch_pdl(k_attn<HD, g>, grid, dim3(ATT_WARPS * 32), 0, s, q, ldq, kc, vc, slot_stride, kvh_stride, \
-                   rows, n_splits, scale, out, ldo, part, cnt);                                                  \
+    e = launch_pdl_cluster(k_attn<HD, g>, grid, dim3(ATT_WARPS * 32), 0, n_splits, s, q, ldq, kc, vc,       \
+                           slot_stride, kvh_stride, rows, n_splits, scale, out, ldo);                            \
     break;
     TN_ATT_CASE(1)
     TN_ATT_CASE(2)
@@ -872,8 +857,8 @@ static int launch_attn_hd(const float* q, int ldq, const float* kc, const float*
 #undef TN_ATT_CASE
     case 16:
       if (HD <= 64) {
-        e = launch_pdl(k_attn<HD <= 64 ? HD : 64, 16>, grid, dim3(ATT_WARPS * 32), 0, s, q, ldq, kc, vc, slot_stride,
-                       kvh_stride, rows, n_splits, scale, out, ldo, part, cnt);
+        e = launch_pdl_cluster(k_attn<HD <= 64 ? HD : 64, 16>, grid, dim3(ATT_WARPS * 32), 0, n_splits, s, q, ldq,
+                               kc, vc, slot_stride, kvh_stride, rows, n_splits, scale, out, ldo);
         break;
       }
       [[fallthrough]];
@@ -887,16 +872,15 @@ static int launch_attn_hd(const float* q, int ldq, const float* kc, const float*
 
 int attention(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
               size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, int n_splits,
-              float* out, int ldo, void* scratch, int* cnt, cudaStream_t s) {
+              float* out, int ldo, cudaStream_t s) {
   if (T <= 0) return TN_OK;
   TN_REQUIRE(nH % nKV == 0, TN_EUNSUPPORTED, "attention: n_heads %% n_kv_heads != 0");
-  TN_REQUIRE(n_splits >= 1 && n_splits <= 64, TN_EINVAL, "attention: %d splits", n_splits);
+  TN_REQUIRE(n_splits >= 1 && n_splits <= 8, TN_EINVAL, "attention: %d splits", n_splits);
   const int G = nH / nKV;
-  float* part = (float*)scratch;
   switch (hd) {
-    case 32: return launch_attn_hd<32>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, part, cnt, s);
-    case 64: return launch_attn_hd<64>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, part, cnt, s);
-    case 128: return launch_attn_hd<128>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, part, cnt, s);
+    case 32: return launch_attn_hd<32>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, s);
+    case 64: return launch_attn_hd<64>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, s);
+    case 128: return launch_attn_hd<128>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, s);
     default: set_error("attention: head_dim %d unsupported", hd); return TN_EUNSUPPORTED;
   }
 }

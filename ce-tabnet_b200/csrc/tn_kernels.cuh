@@ -51,6 +51,26 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
+// launch_pdl with thread-block clusters of cluster_x CTAs along x
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, int cluster_x,
+                                      cudaStream_t s, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 
 // Launch shape of the tensor-core matvec for one token count (1 or 2): K is
 // cut into ks chunks of ckp block pairs (a chunk's activation digits fill one
@@ -143,15 +163,12 @@ int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs,
 
 // One-query GQA attention (web/inference-worker.js:556-564) for T rows, one
 // kernel: CTA (split, KV head, row) over its share of the row's positions;
-// the last CTA of a (row, KV head) merges the splits in split order.
-// scratch (attn_scratch_bytes) holds the split partials; counters holds
-// T * nKV arrival counters that must be zero before the first call (every
-// call leaves them zero).
+// the splits of a (row, KV head) form a thread-block cluster and merge in
+// split order through distributed shared memory (n_splits <= 8).
 int attn_splits(int T, int nKV, int max_ctx);
-size_t attn_scratch_bytes(int T, int nH, int hd, int n_splits);
 int attention(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
               size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, int n_splits,
-              float* out, int ldo, void* scratch, int* counters, cudaStream_t s);
+              float* out, int ldo, cudaStream_t s);
 
 int hop_encode_rows(const float* h, int ldh, const int* rowsel, int T, int H, uint16_t* out,
                     cudaStream_t s);

@@ -34,9 +34,8 @@
 // each unit's records (one contiguous bulk copy) into the ring with a decoded
 // descriptor of the unit (full / empty mbarriers; a stage is handed back as
 // soon as the consumers hold its operands in registers); eight consumer warps
-// split every unit's pairs,
-// accumulate a tile's chunk in registers and hand the per-warp row sums to an
-// epilogue warp through mbarrier-guarded buffers.  The epilogue warp sums the
+// split every unit's pairs, accumulate a tile's chunk in registers and hand
+// the per-warp row sums to an epilogue warp through mbarrier-guarded buffers.  The epilogue warp sums the
 // eight warps in fixed order; a tile whose chunk is whole in this CTA and the
 // only chunk is final at once (fused epilogue: store / residual add / SwiGLU /
 // RoPE + KV append); other pieces go to a workspace, arrivals are counted per

@@ -95,8 +95,6 @@ struct tn_stage {
   int* kerr = nullptr;  // set by a kernel whose bounded wait gave up
   double2* cs = nullptr;
   double* freq = nullptr;
-  void* attn_scratch = nullptr;
-  int* attn_cnt = nullptr;
   // control block: rows | outrows | sampler params, uploaded once per step
   char* d_ctl = nullptr;
   size_t ctl_outrows_off = 0, ctl_params_off = 0, ctl_bytes = 0;
@@ -352,16 +350,6 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   if ((rc = dalloc(st, &st->kerr, 1))) return rc;
   if ((rc = dalloc(st, &st->cs, (size_t)T * (st->hd / 2)))) return rc;
   if ((rc = dalloc(st, &st->freq, (size_t)(st->hd / 2)))) return rc;
-  size_t att_bytes = 0;
-  for (int t = 1; t <= T; t++)
-    att_bytes = std::max(att_bytes, attn_scratch_bytes(t, st->nH, st->hd, attn_splits(t, st->nKV, st->max_ctx)));
-  {
-    char* p = nullptr;
-    if ((rc = dalloc(st, &p, att_bytes))) return rc;
-    st->attn_scratch = p;
-  }
-  // split arrival counters of the attention kernel (zeroed here, left zero by every call)
-  if ((rc = dalloc(st, &st->attn_cnt, (size_t)T * st->nKV))) return rc;
   // RoPE frequencies theta^(-2i/hd) in double (web/inference-worker.js:533)
   std::vector<double> freq(st->hd / 2);
   for (int i = 0; i < st->hd / 2; i++) freq[i] = std::pow(st->theta, (double)(-2 * i) / st->hd);
@@ -478,7 +466,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
     }
     TN_STEP_LAUNCH(TN_PROF_ATTENTION, 2,
                    attention(st->q, st->qDim, kc, vc, st->slot_stride, st->kvh_stride, rows, T, st->nH, st->nKV,
-                             st->hd, ns, st->att, st->qDim, st->attn_scratch, st->attn_cnt, s));
+                             st->hd, ns, st->att, st->qDim, s));
     if (fuse && matvec_dec_ok(L.o, T))
       TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else

@@ -221,11 +221,12 @@ int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_
  * from JavaScript), a C binding layer that has no allocator of its own, or a
  * serving loop that must never pay the device-wide synchronisation that
  * cudaMalloc/cudaFree can imply.  This variant takes the same inputs and
- * output as tn_attention but keeps its row table and split partials in a
+ * output as tn_attention but keeps its row table (16 bytes a row) in a
  * fixed array compiled into the library: TN_ATTENTION_STATIC_SCRATCH_BYTES
- * (8 MiB) of device memory, held on every GPU that loads the library until the
- * process exits.  Calls whose tn_attention_scratch_bytes() exceeds that size
- * fail with TN_ECAPACITY and launch nothing; nothing here allocates.
+ * (1 MiB, 65536 rows) of device memory, held on every GPU that loads the
+ * library until the process exits.  Calls whose tn_attention_scratch_bytes()
+ * exceeds that size fail with TN_ECAPACITY and launch nothing; nothing here
+ * allocates.
  *
  * It runs on the calling thread's current device.  Its first call on a device
  * looks up that device's address of the array (once per device), so make that
@@ -233,7 +234,7 @@ int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_
  * leave their contents in it; every call writes all it reads, so nothing needs
  * clearing, but calls whose work overlaps on the GPU (other streams, other
  * threads) race on the array and must be serialised by the caller. */
-#define TN_ATTENTION_STATIC_SCRATCH_BYTES (8u << 20)
+#define TN_ATTENTION_STATIC_SCRATCH_BYTES (1u << 20)
 int tn_attention_static(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
                         int32_t head_dim, int32_t max_ctx, const float* d_q, const float* d_k,
                         const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,

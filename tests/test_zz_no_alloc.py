@@ -71,8 +71,8 @@ def test_static_scratch_attention_matches_caller_scratch(pkg, torch_cuda):
 def test_static_scratch_rejects_oversized_calls(pkg, torch_cuda):
     torch = torch_cuda
     lib = pkg._lib.load()
-    n, nH, nKV, hd, max_ctx = 256, 64, 8, 128, 4096
-    assert lib.tn_attention_scratch_bytes(n, nH, nKV, hd, max_ctx) > (8 << 20)
+    n, nH, nKV, hd, max_ctx = 70000, 64, 8, 128, 4096  # the fixed array holds 65536 rows
+    assert lib.tn_attention_scratch_bytes(n, nH, nKV, hd, max_ctx) > (1 << 20)
     dummy = torch.zeros(16, dtype=torch.float32, device="cuda")
     idx = torch.zeros(n, dtype=torch.int32, device="cuda")
     rc = lib.tn_attention_static(n, 1, nH, nKV, hd, max_ctx, dummy.data_ptr(), dummy.data_ptr(),
