@@ -373,9 +373,12 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
           for (int tt = 0; tt < TT; tt++) {
             double ss = 0.0;
 #pragma unroll
-            for (int it = 0; it < IT; it++)
+            for (int it = 0; it < IT; it++) {
+              float s4 = 0.f;  // four squares in f32, then one double add
 #pragma unroll
-              for (int m = 0; m < 4; m++) ss = fma((double)v[tt][it][m], (double)v[tt][it][m], ss);
+              for (int m = 0; m < 4; m++) s4 = fmaf(v[tt][it][m], v[tt][it][m], s4);
+              ss += (double)s4;
+            }
             for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(FULL, ss, o);
             if (lane == 0) sred[warp][tt] = ss;
           }
@@ -471,8 +474,8 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
       const uint8_t* sbase = ring + (size_t)st * a.stage_bytes;
       {
         // all pairs' operands first, so their load -> MMA -> FMA chains overlap.
-        // A stage has room for SC pairs, so slot j * NW + warp is always inside
-        // it; slots past the sub-chunk's n pairs hold stale bytes and get scale 0.
+        // This warp's pairs are slots j * NW + warp of the stage; slots past the
+        // sub-chunk's n pairs are skipped (n is the same for the whole warp).
         constexpr int WV = AB / 512;  // 16-byte words per lane per pair
         uint4 wv[PPW][WV];
         uint32_t sw[PPW][TT];
@@ -480,6 +483,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
         const uint8_t* wbase = sbase + (size_t)warp * REC;
 #pragma unroll
         for (int j = 0; j < PPW; j++) {
+          if (n < SC && j * MMV_NW + warp >= n) break;
           const uint8_t* rec = wbase + j * MMV_NW * REC;
           const int pc = min(first + j * MMV_NW + warp, CP - 1);  // chunk-local pair
 #pragma unroll
@@ -501,7 +505,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
         auto compute = [&](auto all_valid) {
 #pragma unroll
           for (int j = 0; j < PPW; j++) {
-            const bool valid = decltype(all_valid)::value || j * MMV_NW + warp < n;
+            if (!decltype(all_valid)::value && j * MMV_NW + warp >= n) break;
             uint32_t A[2][4];
             if (KIND == MK_Q4) {
               const uint32_t M4 = 0xF0F0F0F0u;
@@ -536,8 +540,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
                 mma_s8(D, A[1], q == 0 ? bq[j][0].y : 0u, q == 1 ? bq[j][1].y : 0u);
               }
               const uint32_t s32 = sw[j][q];
-              float2 d = __half22float2(*reinterpret_cast<const __half2*>(&s32));  // (row g, row g + 8)
-              if (!decltype(all_valid)::value && !valid) d = make_float2(0.f, 0.f);
+              const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&s32));  // (row g, row g + 8)
               acc[0] = fmaf(d.x, __int_as_float(D[0]) - kMagicF, acc[0]);
               acc[1] = fmaf(d.x, __int_as_float(D[1]) - kMagicF, acc[1]);
               acc[2] = fmaf(d.y, __int_as_float(D[2]) - kMagicF, acc[2]);
