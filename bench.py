@@ -492,37 +492,46 @@ def run_ours(args):
 
 
 def pipeline_e2e(pkg, torch, ctx, pipe, args, rank, world, barrier, max_over_ranks):
-    """e2e for N>1: each stage step goes through the host-buffer API; the
-    returned fp16 frames cross to the next rank over NCCL."""
+    """e2e for N>1: every stage step goes through the host-buffer API
+    (tn_stage_forward), on the tick schedule of the timed rounds: a step's
+    input frame comes to the host from the NCCL receive buffer and its output
+    frame goes back to the device for the send, so the stages work on
+    different micro-batches at once."""
     import torch.distributed as dist
 
     M, H, W = pipe.M, pipe.H, world
     n = args.steps * M
-    toks = pipe.tok.cpu().view(-1).tolist() if rank == 0 else None
+    dev = pipe.tok.device
+    hin = torch.zeros((M, H), dtype=torch.float16, device=dev)
+    hout = torch.zeros((M, H), dtype=torch.float16, device=dev)
+    tok_out = torch.zeros((M, 1), dtype=torch.int32, device=dev)
+    bufs = {"recv_token": pipe.tok, "recv_hidden": hin, "send_hidden": hout, "send_token": tok_out}
     barrier()
     t0 = time.perf_counter()
-    for j in range(n):  # sequential hop through the stages, micro-batch by micro-batch
-        mb = j % M
+    for tau in range(pkg.planner.pipeline_ticks(W, n)):
+        sched, mb = pkg.planner.pipeline_tick(rank, W, M, n, tau)
+        ops = [dist.P2POp(dist.irecv if kind.startswith("recv") else dist.isend, bufs[kind][b], peer)
+               for kind, b, peer in sched]
+        if ops:
+            for w in dist.batch_isend_irecv(ops):
+                w.wait()
+        if mb is None:
+            continue
         if rank == 0:
-            out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [toks[mb]]})
-            dist.send(torch.from_numpy(out["hidden"].view(np.float16).copy()).cuda(), 1)
-            t = torch.empty(1, dtype=torch.int32, device="cuda")
-            dist.recv(t, W - 1)
-            toks[mb] = int(t.item())
+            out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [int(pipe.tok[mb, 0].item())]})
+            hout[mb].copy_(torch.from_numpy(out["hidden"].view(np.float16)))
         else:
-            buf = torch.empty(H, dtype=torch.float16, device="cuda")
-            dist.recv(buf, rank - 1)
             out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb],
-                                    "hidden": buf.cpu().numpy().view(np.uint16), "temperature": 0})
+                                    "hidden": hin[mb].cpu().numpy().view(np.uint16), "temperature": 0})
             if ctx.is_last:
-                dist.send(torch.tensor([out["token_id"]], dtype=torch.int32, device="cuda"), 0)
+                tok_out[mb, 0] = out["token_id"]
             else:
-                dist.send(torch.from_numpy(out["hidden"].view(np.float16).copy()).cuda(), rank + 1)
+                hout[mb].copy_(torch.from_numpy(out["hidden"].view(np.float16)))
         pipe.pos[mb] += 1
     torch.cuda.synchronize()
     s = max_over_ranks(time.perf_counter() - t0)
-    if rank == 0:
-        pipe.tok.copy_(torch.tensor(toks, dtype=torch.int32).view(M, 1))
+    # per round: token ids in (rank 0) and out (last rank), one fp16 frame into
+    # and one out of the host API at each of the W - 1 stage boundaries
     return n / s, 4 * M + 2 * H * M * (W - 1), 4 * M + 2 * H * M * (W - 1)
 
 
