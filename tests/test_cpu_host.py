@@ -40,7 +40,7 @@ def test_layout_matches_oracle_and_library(pkg, ref):
             L = pkg.pack.layer_layout(m, q)
             d = m.c_dims()
             assert L["total"] == lib.tn_layer_bytes(C.byref(d), pkg._lib.QUANT[q])
-    # survey figures: packed layer bytes of each workload
+    # packed layer bytes of each workload (web/inference-worker.js:142-159 layout with each model's dims)
     assert pkg.pack.layer_layout(pkg.pack.MODELS["tiny"])["total"] == 736_512
     assert pkg.pack.layer_layout(pkg.pack.MODELS["llama8b"])["total"] == 122_699_776
     assert pkg.pack.layer_layout(pkg.pack.MODELS["llama70b"])["total"] == 481_329_152
