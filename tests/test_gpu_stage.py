@@ -186,6 +186,59 @@ def test_device_step_matches_forward(pkg, ref, tiny, torch_cuda):
     pkg.freeStage(b)
 
 
+def test_device_step_three_stages(pkg, tiny, torch_cuda):
+    """The device-buffer step API (what the multi-GPU pipeline drives) on a
+    first, a middle and a last stage: fp16 frames and tokens identical to the
+    host API on a twin chain of stages."""
+    torch = torch_cuda
+    m, w = tiny
+    lib = pkg._lib.load()
+    import ctypes as C
+
+    cuts = [(0, 1, True, False), (1, 3, False, False), (3, m.n_layers, False, True)]
+    host = [_stage(pkg, m, w, *c)[0] for c in cuts]
+    dev = [_stage(pkg, m, w, *c)[0] for c in cuts]
+    prompt = pkg.pack.synth_prompt(m, 9, seed=31)
+    pos = len(prompt) - 1
+    for chain in (host, dev):  # prefill: stage 0 hops its last position (web/tabnet-node.js:167-169)
+        h = pkg.forward(chain[0], {"seq_id": 5, "token_pos": 0, "token_ids": prompt})["hidden"]
+        h = pkg.forward(chain[1], {"seq_id": 5, "token_pos": pos, "hidden": h})["hidden"]
+        tok = pkg.forward(chain[2], {"seq_id": 5, "token_pos": pos, "hidden": h, "temperature": 0})["token_id"]
+    H = m.hidden_dim
+    d_tok = torch.tensor([tok], dtype=torch.int32, device="cuda")
+    d_h1 = torch.zeros(H, dtype=torch.float16, device="cuda")
+    d_h2 = torch.zeros(H, dtype=torch.float16, device="cuda")
+    d_out = torch.zeros(1, dtype=torch.int32, device="cuda")
+    chain_stream = torch.cuda.Stream()  # not the legacy default stream, whose handle 0 means "the stage's own"
+    stream = chain_stream.cuda_stream
+    torch.cuda.synchronize()  # the buffers above were filled on the default stream
+    for step in range(6):
+        pos += 1
+        h1 = pkg.forward(host[0], {"seq_id": 5, "token_pos": pos, "token_ids": [tok]})["hidden"]
+        h2 = pkg.forward(host[1], {"seq_id": 5, "token_pos": pos, "hidden": h1})["hidden"]
+        tok = pkg.forward(host[2], {"seq_id": 5, "token_pos": pos, "hidden": h2, "temperature": 0})["token_id"]
+        p = (C.c_int32 * 1)(pos)
+        for i, ctx in enumerate(dev):
+            ids = (C.c_uint64 * 1)(ctx.seq_key(5))
+            d = pkg._lib.StepDesc(n_seqs=1, seq_ids=ids, token_pos=p, temperature=0.0, top_p=0.95, rng_seed=0)
+            if i == 0:
+                d.d_token_ids, d.d_hidden_out = d_tok.data_ptr(), d_h1.data_ptr()
+            elif i == 1:
+                d.d_hidden_in, d.d_hidden_out = d_h1.data_ptr(), d_h2.data_ptr()
+            else:
+                d.d_hidden_in, d.d_token_out = d_h2.data_ptr(), d_out.data_ptr()
+            # one stream for the chain, so each stage reads the frame the previous one wrote
+            pkg._lib.check(lib.tn_stage_step_async(ctx.handle, C.byref(d), C.c_void_p(stream)))
+        torch.cuda.synchronize()
+        assert np.array_equal(d_h1.cpu().numpy().view(np.uint16), h1), step
+        assert np.array_equal(d_h2.cpu().numpy().view(np.uint16), h2), step
+        assert int(d_out.item()) == tok, step
+        with torch.cuda.stream(chain_stream):
+            d_tok.copy_(d_out)
+    for c in host + dev:
+        pkg.freeStage(c)
+
+
 def test_errors(pkg, tiny):
     m, w = tiny
     ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, max_ctx=16, max_seqs=2)
