@@ -94,6 +94,31 @@ def test_matvec_vs_oracle(pkg, ref, torch_cuda, quant, rows, cols, T):
         assert _maxrel(got[t], want) < MATVEC_TOL, (t, _maxrel(got[t], want))
 
 
+@pytest.mark.parametrize("quant,rows,cols,T", [
+    ("q4_0", 4096, 4096, 4), ("q4_0", 4096, 4096, 16), ("q4_0", 4096, 4096, 64), ("q4_0", 4096, 4096, 512),
+    ("q4_0", 14336, 4096, 16), ("q4_0", 14336, 4096, 64), ("q8_0", 4096, 14336, 16), ("q8_0", 4096, 4096, 64),
+    ("q4_0", 128256, 4096, 4),  # the 8B lm_head
+])
+def test_matvec_token_sweep(pkg, ref, torch_cuda, quant, rows, cols, T):
+    """The matvec microbench's token counts (4 .. 512) on its weight shapes:
+    every token's row against the oracle."""
+    torch = torch_cuda
+    buf = _synth_matrix(pkg, rows, cols, quant, seed=rows ^ cols ^ T)
+    mat = Mat(pkg, quant, rows, cols, buf)
+    rng = np.random.default_rng(1000 + T)
+    x = rng.standard_normal((T, cols)).astype(np.float32)
+    dx = torch.from_numpy(x).cuda()
+    dy = torch.full((T, rows), float("nan"), dtype=torch.float32, device="cuda")
+    pkg._lib.check(mat.lib.tn_matrix_matvec(mat.h, T, dx.data_ptr(), dy.data_ptr(), None))
+    torch.cuda.synchronize()
+    got = dy.cpu().numpy()
+    assert np.isfinite(got).all()
+    step = max(1, T // 16)  # past 16 tokens the oracle checks every step-th one and the last
+    for t in sorted(set(range(0, T, step)) | {T - 1}):
+        want = ref.matvec(buf, quant, rows, cols, x[t])
+        assert _maxrel(got[t], want) < MATVEC_TOL, (t, _maxrel(got[t], want))
+
+
 @pytest.mark.parametrize("hd,nH,nKV", [(128, 32, 8), (128, 64, 8), (32, 8, 2)])
 def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV):
     torch = torch_cuda
@@ -122,6 +147,41 @@ def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV):
         Vr = V[s, :, :L, :].transpose(1, 0, 2).reshape(L, nKV * hd)
         want = ref.attention(q[r], Kr, Vr, nH, nKV, hd)
         assert _maxrel(got[r], want) < ATTN_TOL, (r, L, _maxrel(got[r], want))
+
+
+@pytest.mark.parametrize("L,n_rows,n_slots", [(512, 1, 1), (2048, 8, 8), (2048, 64, 16), (8192, 8, 4),
+                                              (32768, 1, 1), (32768, 8, 2)])
+def test_attention_context_sweep(pkg, ref, torch_cuda, L, n_rows, n_slots):
+    """The GQA decode-attention sweep (32 query / 8 KV heads x 128, contexts
+    512 .. 32768, 1 .. 64 concurrent rows) against the oracle."""
+    torch = torch_cuda
+    lib = pkg._lib.load()
+    hd, nH, nKV = 128, 32, 8
+    rng = np.random.default_rng(L + n_rows)
+    K = rng.standard_normal((n_slots, nKV, L, hd), dtype=np.float32)
+    V = rng.standard_normal((n_slots, nKV, L, hd), dtype=np.float32)
+    lens = [L - (r % 3) for r in range(n_rows)]
+    slots = [r % n_slots for r in range(n_rows)]
+    q = rng.standard_normal((n_rows, nH * hd), dtype=np.float32)
+    dK, dV, dq = (torch.from_numpy(a).cuda() for a in (K, V, q))
+    dslot = torch.tensor(slots, dtype=torch.int32, device="cuda")
+    dlen = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = torch.zeros((n_rows, nH * hd), dtype=torch.float32, device="cuda")
+    nbytes = lib.tn_attention_scratch_bytes(n_rows, nH, nKV, hd, L)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    pkg._lib.check(lib.tn_attention(n_rows, n_slots, nH, nKV, hd, L, dq.data_ptr(), dK.data_ptr(), dV.data_ptr(),
+                                    dslot.data_ptr(), dlen.data_ptr(), out.data_ptr(), scratch.data_ptr(), nbytes,
+                                    None))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    step = max(1, n_rows // 4) if L >= 8192 else 1  # long contexts: the oracle checks a spread of rows
+    for r in sorted(set(range(0, n_rows, step)) | {n_rows - 1}):
+        s, n = slots[r], lens[r]
+        Kr = K[s, :, :n, :].transpose(1, 0, 2).reshape(n, nKV * hd)
+        Vr = V[s, :, :n, :].transpose(1, 0, 2).reshape(n, nKV * hd)
+        want = ref.attention(q[r], Kr, Vr, nH, nKV, hd)
+        assert _maxrel(got[r], want) < ATTN_TOL, (r, n, _maxrel(got[r], want))
 
 
 def test_hop_encode_exhaustive(pkg, ref, torch_cuda):
