@@ -101,7 +101,7 @@ def test_matvec_vs_oracle(pkg, ref, torch_cuda, quant, rows, cols, T):
 ])
 def test_matvec_token_sweep(pkg, ref, torch_cuda, quant, rows, cols, T):
     """The matvec microbench's token counts (4 .. 512) on its weight shapes:
-    every token's row against the oracle."""
+    token rows against the oracle (all up to 16 tokens, a spread past that)."""
     torch = torch_cuda
     buf = _synth_matrix(pkg, rows, cols, quant, seed=rows ^ cols ^ T)
     mat = Mat(pkg, quant, rows, cols, buf)
