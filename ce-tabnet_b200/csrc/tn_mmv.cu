@@ -175,10 +175,20 @@ __device__ __forceinline__ void mmv_store(const MmvArgs& a, int row, int tt, flo
 
 // Work partition.  CTA b works on K chunk b % ks only (one digit table per
 // CTA); the gk CTAs of a chunk split its units u = t * nsc + sc (tile t,
-// sub-chunk sc) into contiguous runs of NSU / gk units (rounded), at least nsc
-// each, so a (tile, chunk) is split into at most two pieces: part 0 from
-// sub-chunk 0, part 1 from a later one.
+// sub-chunk sc): units [0, pool0) in contiguous runs of pool0 / gk units
+// (rounded, at least nsc each, so a (tile, chunk) is split into at most two
+// pieces: part 0 from sub-chunk 0, part 1 from a later one), and on chunks of
+// at least 8 tiles per CTA the last quarter of the tiles, [pool0, NSU), as a
+// pool of whole tiles the chunk's CTAs take in ticket order after their runs
+// -- whole tiles, so the pool adds no cross-CTA pieces -- so that CTAs that
+// got their SM slot late (and start with an empty ring) take fewer of them.
 __host__ __device__ __forceinline__ int mmv_chunk_ctas(int grid, int ks, int kc) { return (grid - kc + ks - 1) / ks; }
+__host__ __device__ __forceinline__ int mmv_pool0(int nsu, int gk, int nsc) {
+  const int q = nsu / gk;
+  if (q < 8 * nsc) return nsu;
+  const int p = (gk * (q - q / 4) + nsc - 1) / nsc * nsc;  // a tile boundary
+  return p < nsu ? p : nsu;
+}
 constexpr int kPieceEnd = 1 << 16;  // unit descriptor flag (with the sub-chunk): the last unit of a piece
 
 template <int KIND, int TT>
@@ -208,8 +218,8 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int NSU = a.tiles * a.nsc;  // units per chunk
   const int kc0 = blockIdx.x % a.ks, gk = mmv_chunk_ctas(gridDim.x, a.ks, kc0);
-  const int jc = blockIdx.x / a.ks;
-  const int s_begin = (int)((int64_t)NSU * jc / gk), s_end = (int)((int64_t)NSU * (jc + 1) / gk);
+  const int jc = blockIdx.x / a.ks, pool0 = mmv_pool0(NSU, gk, a.nsc);
+  const int s_begin = (int)((int64_t)pool0 * jc / gk), s_end = (int)((int64_t)pool0 * (jc + 1) / gk);
   const int np0 = min(a.ckp, a.pairs - kc0 * a.ckp);  // pairs of the chunk
 
   if (tid == 0) {
@@ -233,30 +243,71 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
 
   if (warp == MMV_NW + MMV_NE) {
     // ======================= producer: one bulk copy per unit into the ring
-    // (weights do not depend on the previous kernel: no wait for it), then a
-    // descriptor without a unit
+    // (weights do not depend on the previous kernel: the static run goes out
+    // before any wait for it), then a descriptor without a unit
     if (lane == 0) {
-      for (int u = s_begin, k = 0; u <= s_end; u++, k++) {
+      int k = 0;
+      // the ring stage for unit k, once every consumer warp has read its last unit
+      auto take = [&]() -> int {
         const int st = k % a.stages;
         if (k >= a.stages) {
-          // every consumer warp has read the unit this stage held
-          if (!mbar_wait(&empty[st], ((k / a.stages) - 1) & 1, &abort_flag)) break;
+          if (!mbar_wait(&empty[st], ((k / a.stages) - 1) & 1, &abort_flag)) return -1;
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
-        if (abort_flag) break;
-        if (u == s_end) {
-          udesc[st] = make_int4(-1, 0, 0, 0);
-          mbar_expect_tx(&full[st], 0);
-          break;
-        }
+        return abort_flag ? -1 : st;
+      };
+      auto put = [&](int st, int u, bool piece_end) {
         const int t = u / a.nsc, sc = u - t * a.nsc, first = sc * a.scp, n = max(0, min(a.scp, np0 - first));
         const uint32_t bytes = (uint32_t)n * REC;
-        udesc[st] = make_int4(t, sc | (u == s_end - 1 || sc == a.nsc - 1 ? kPieceEnd : 0), first, n);
+        udesc[st] = make_int4(t, sc | (piece_end || sc == a.nsc - 1 ? kPieceEnd : 0), first, n);
         last_unit[st] = k;
         mbar_expect_tx(&full[st], bytes);  // an empty sub-chunk completes on this arrival alone
         if (bytes)
           bulk_g2s(ring + (size_t)st * a.stage_bytes,
                    a.data + ((size_t)t * a.pairs + (size_t)kc0 * a.ckp + first) * REC, bytes, &full[st]);
+        k++;
+      };
+      auto no_more = [&](int st) {
+        udesc[st] = make_int4(-1, 0, 0, 0);
+        mbar_expect_tx(&full[st], 0);
+      };
+      bool live = true;
+      for (int u = s_begin; u < s_end && live; u++) {
+        const int st = take();
+        if (st < 0) live = false;
+        else put(st, u, u == s_end - 1);
+      }
+      if (pool0 < NSU) {
+        // the tickets were reset by the previous launch on this matrix, which
+        // may be the predecessor
+        pdl_wait();
+        const int ntiles = (NSU - pool0) / a.nsc;
+        while (live) {
+          const int r = atomicAdd(a.cnt + a.tiles + kc0, 1);  // in flight while a stage frees up
+          int st = take();
+          if (st < 0) break;
+          if (r >= ntiles) {
+            no_more(st);
+            break;
+          }
+          for (int u = pool0 + r * a.nsc, ue = u + a.nsc; u < ue; u++) {
+            if (u > pool0 + r * a.nsc && (st = take()) < 0) {
+              live = false;
+              break;
+            }
+            put(st, u, u == ue - 1);
+          }
+        }
+        // the last CTA of the chunk past its last ticket makes the tickets
+        // ready for the next launch
+        __threadfence();
+        if (atomicAdd(a.cnt + a.tiles + a.ks + kc0, 1) == gk - 1) {
+          a.cnt[a.tiles + kc0] = 0;
+          a.cnt[a.tiles + a.ks + kc0] = 0;
+        }
+      } else if (live) {
+        const int st = take();
+        if (st >= 0) no_more(st);
       }
     }
   } else if (warp < MMV_NW) {
@@ -761,6 +812,7 @@ static void mmv_pick(MmShape* sh) {
 
 int mm_prepare(Matrix* m) {
   TN_REQUIRE(m->kind == MK_Q4 || m->kind == MK_Q8, TN_EINVAL, "mm_prepare: kind %d", m->kind);
+  int ks_max = 1;
   size_t ws = 0;
   for (int tt = 1; tt <= 2; tt++) {
     MmShape& sh = m->mm[tt - 1];
@@ -771,6 +823,7 @@ int mm_prepare(Matrix* m) {
     sh.scp = (sh.ckp + sh.nsc - 1) / sh.nsc;
     sh.stage_bytes = (uint32_t)scmax * tile_rec_bytes(m->kind);  // room for a full sub-chunk
     ws = std::max(ws, (size_t)sh.ks * m->tiles * 2 * 32);
+    ks_max = std::max(ks_max, sh.ks);
     // (set once per matrix, outside any stream capture)
     if (m->kind == MK_Q4) {
       if (tt == 1) mmv_pick<MK_Q4, 1>(&sh);
@@ -781,7 +834,7 @@ int mm_prepare(Matrix* m) {
     }
   }
   m->ws_floats = ws;                          // two 32-float parts per (chunk, tile)
-  m->cnt_ints = (size_t)m->tiles;  // per-tile arrival counters
+  m->cnt_ints = (size_t)m->tiles + 2 * ks_max;  // per-tile arrivals, per-chunk tickets and done counts
   return TN_OK;
 }
 
