@@ -12,6 +12,18 @@ the host-buffer API (tn_stage_forward), host<->device copies included.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
   (N>1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N)
+
+Kernel sweeps (one GPU, one JSON line with a point per configuration):
+
+  python bench.py --micro matvec [--shape 4096x4096,...] [--quant q4_0,q8_0] [--tokens 1,4,16,64,512]
+  python bench.py --micro attn [--ctx 512,...] [--seqs 1,8,64]
+
+The matvec sweep covers the dequant-matvec / dequant-GEMM weight shapes
+(4096x4096, 14336x4096, 4096x14336, 128256x4096; q4_0 and q8_0; 1 .. 512
+tokens), the attention sweep the GQA decode attention (32 query / 8 KV heads x
+128, f32 KV; 512 .. 32768 cached positions; 1, 8, 64 rows).  Every launch reads
+another copy of its inputs, and the copies together exceed the 126 MB L2, so
+each launch streams from HBM.
 """
 from __future__ import annotations
 
@@ -45,6 +57,13 @@ def parse_args(argv=None):
     p.add_argument("--microbatches", type=int, default=8)
     p.add_argument("--prompt", type=int, default=1024)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--micro", choices=["matvec", "attn"], default=None, help="kernel sweep instead of decode")
+    p.add_argument("--shape", default=None, help="matvec sweep: rows x cols list, e.g. 57344x8192,4096x4096")
+    p.add_argument("--quant", default="q4_0,q8_0", help="matvec sweep: weight formats")
+    p.add_argument("--tokens", default="1,4,16,64,512", help="matvec sweep: token counts")
+    p.add_argument("--ctx", default="512,2048,8192,32768", help="attention sweep: cached positions")
+    p.add_argument("--seqs", default="1,8,64", help="attention sweep: concurrent rows")
+    p.add_argument("--reps", type=int, default=20, help="kernel sweeps: timed launches per point")
     return p.parse_args(argv)
 
 
@@ -122,6 +141,156 @@ def measured_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+def measured_tensor_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s: the burst figure (kernels timed alone)."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+L2_BYTES = 126e6
+
+
+def _ints(text: str) -> list[int]:
+    return [int(v) for v in text.split(",") if v.strip()]
+
+
+def micro_matvec(args):
+    """The dequant-matvec sweep: each (shape, format, tokens) point timed over
+    args.reps launches with CUDA events, rotating over enough copies of the
+    matrix that each launch reads its weights from HBM."""
+    import torch
+
+    import __graft_entry__ as g
+
+    pkg = g.load_package()
+    lib, P = pkg._lib.load(), pkg._lib
+    torch.cuda.set_device(0)
+    shapes = ([tuple(int(v) for v in sh.split("x")) for sh in args.shape.split(",")] if args.shape
+              else [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
+    hbm, hbm_kind = measured_peaks()
+    tc, tc_kind = measured_tensor_peak()
+    ridge = tc * 1e12 / (hbm * 1e9)  # FLOP per byte where the two roofs meet
+    clocks = ClockSampler(physical_gpu(0))
+    clocks.start()
+    points = []
+    for rows, cols in shapes:
+        for quant in args.quant.split(","):
+            nbytes = pkg.pack.quant_bytes(rows * cols, quant)
+            copies = max(1, int(2 * L2_BYTES // nbytes) + 1) if nbytes < 2 * L2_BYTES else 1
+            m = pkg.pack.ModelDims(cols, 1, 1, 1, rows, 0, 1e4, quant, quant, quant, 5)
+            src = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+            d = m.c_dims()
+            P.check(lib.tn_synth_tensor(5, P.TN_TAG_EMBED, C.byref(d), P.QUANT[quant], src.data_ptr(), 1, None))
+            torch.cuda.synchronize()
+            mats = []
+            for _ in range(copies):
+                h = C.c_void_p()
+                P.check(lib.tn_matrix_create(0, P.QUANT[quant], rows, cols, src.data_ptr(), nbytes, 1, C.byref(h)))
+                mats.append(h)
+            del src
+            for T in _ints(args.tokens):
+                x = torch.randn(T, cols, device="cuda")
+                y = torch.empty(T, rows, device="cuda")
+                for i in range(max(3, args.warmup)):
+                    P.check(lib.tn_matrix_matvec(mats[i % copies], T, x.data_ptr(), y.data_ptr(), None))
+                torch.cuda.synchronize()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for i in range(args.reps):
+                    P.check(lib.tn_matrix_matvec(mats[i % copies], T, x.data_ptr(), y.data_ptr(), None))
+                e1.record()
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) / args.reps * 1e3
+                byts = nbytes + 4 * T * (rows + cols)
+                flops = 2 * T * rows * cols
+                gbs, tfs = byts / us / 1e3, flops / us / 1e6
+                tensor = flops / byts >= ridge
+                roof = ({"bound": "tensor", "achieved": round(tfs, 2), "peak": tc, "unit": "TFLOP/s",
+                         "frac": round(tfs / tc, 4), "peak_source": tc_kind}
+                        if tensor else
+                        {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "peak_source": hbm_kind})
+                points.append({"shape": f"{rows}x{cols}", "quant": quant, "tokens": T, "us": round(us, 2),
+                               "GB_s": round(gbs, 1), "TFLOP_s": round(tfs, 3), "roofline": roof,
+                               "copies": copies})
+                print(f"# {rows}x{cols} {quant} T={T}: {us:.1f} us, {gbs:.0f} GB/s, {tfs:.2f} TFLOP/s",
+                      file=sys.stderr, flush=True)
+            for h in mats:
+                lib.tn_matrix_free(h)
+    clk = clocks.stop()
+    print(json.dumps({"micro": "matvec", "metric": "dequant-matvec HBM GB/s (TFLOP/s past the ridge)",
+                      "unit": "GB/s", "points": points, "clocks": clk, "reps": args.reps,
+                      "config": {"l2": "launches rotate over copies of the matrix totalling > 2 x L2",
+                                 "x": "f32 N(0,1)", "weights": "seeded Irwin-Hall(4) approximation of N(0, 0.02), "
+                                 "quantised per block"}}), flush=True)
+    return 0
+
+
+def micro_attn(args):
+    """The GQA decode-attention sweep: tn_attention over seqs rows of ctx
+    cached positions, each launch on other sequence slots of an arena larger
+    than twice the L2."""
+    import torch
+
+    import __graft_entry__ as g
+
+    pkg = g.load_package()
+    lib, P = pkg._lib.load(), pkg._lib
+    torch.cuda.set_device(0)
+    nH, nKV, hd = 32, 8, 128
+    hbm, hbm_kind = measured_peaks()
+    clocks = ClockSampler(physical_gpu(0))
+    clocks.start()
+    points = []
+    for ctx in _ints(args.ctx):
+        for seqs in _ints(args.seqs):
+            slot_bytes = 2 * nKV * ctx * hd * 4
+            groups = max(1, int(2 * L2_BYTES // (slot_bytes * seqs)) + 1)
+            n_slots = groups * seqs
+            gen = torch.Generator(device="cuda").manual_seed(ctx + seqs)
+            K = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen)
+            V = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen)
+            q = torch.randn((seqs, nH * hd), device="cuda", generator=gen)
+            out = torch.empty_like(q)
+            lens = torch.full((seqs,), ctx, dtype=torch.int32, device="cuda")
+            slots = [torch.arange(g0 * seqs, (g0 + 1) * seqs, dtype=torch.int32, device="cuda") for g0 in range(groups)]
+            nbytes = lib.tn_attention_scratch_bytes(seqs, nH, nKV, hd, ctx)
+            scratch = torch.empty(max(nbytes, 256), dtype=torch.uint8, device="cuda")
+
+            def call(i):
+                P.check(lib.tn_attention(seqs, n_slots, nH, nKV, hd, ctx, q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                                         slots[i % groups].data_ptr(), lens.data_ptr(), out.data_ptr(),
+                                         scratch.data_ptr(), nbytes, None))
+
+            for i in range(max(3, args.warmup)):
+                call(i)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(args.reps):
+                call(i)
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) / args.reps * 1e3
+            byts = seqs * ctx * 2 * nKV * hd * 4 + 2 * seqs * nH * hd * 4
+            gbs = byts / us / 1e3
+            points.append({"ctx": ctx, "seqs": seqs, "us": round(us, 2), "GB_s": round(gbs, 1),
+                           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                        "frac": round(gbs / hbm, 4), "peak_source": hbm_kind},
+                           "arena_MB": round(n_slots * slot_bytes / 1e6, 1)})
+            print(f"# attn ctx={ctx} seqs={seqs}: {us:.1f} us, {gbs:.0f} GB/s", file=sys.stderr, flush=True)
+            del K, V
+            torch.cuda.empty_cache()
+    clk = clocks.stop()
+    print(json.dumps({"micro": "attn", "metric": "GQA decode attention HBM GB/s (32/8 heads x 128, f32 KV)",
+                      "unit": "GB/s", "points": points, "clocks": clk, "reps": args.reps,
+                      "config": {"l2": "launches rotate over sequence slots of an arena > 2 x L2",
+                                 "values": "q, K, V f32 N(0,1)"}}), flush=True)
+    return 0
+
+
 # ------------------------------------------------------------------ oracle CPU timing
 def oracle_token_time(pkg, m, n_threads: int, layer_reps: int) -> dict:
     """The reference CPU path (oracle) on one decode token: `layer_reps`
@@ -149,8 +318,9 @@ def oracle_token_time(pkg, m, n_threads: int, layer_reps: int) -> dict:
     t_layer = statistics.mean(times)
     s_tok = m.n_layers * t_layer + t_head
     return {"tok_s": 1.0 / s_tok, "t_layer_s": t_layer, "t_head_s": t_head, "layer_times": times,
-            "sample": f"{layer_reps} single-token steps through one {m.name} layer + one lm_head matvec, "
-                      f"extrapolated to {m.n_layers} layers"}
+            "sample": f"EXTRAPOLATED: {layer_reps} single-token steps through one {m.name} layer (positions "
+                      f"0..{layer_reps - 1}) + one lm_head matvec, scaled to {m.n_layers} layers; "
+                      f"{n_threads} oracle thread(s)"}
 
 
 def run_reference(args):
@@ -167,6 +337,10 @@ def run_reference(args):
     os.environ["TABNET_ORACLE_THREADS"] = str(n_threads)
     warm = oracle_token_time(pkg, m, n_threads, max(1, args.warmup))
     res = oracle_token_time(pkg, m, n_threads, max(1, args.steps))
+    # the reference engine is single-threaded JavaScript: the same sample on one thread
+    os.environ["TABNET_ORACLE_THREADS"] = "1"
+    one = oracle_token_time(pkg, m, 1, 2)
+    os.environ["TABNET_ORACLE_THREADS"] = str(n_threads)
     # one reference "step" = one round: every micro-batch's sequence +1 token,
     # run one after another as the reference engine does
     s_round = args.microbatches / res["tok_s"]
@@ -176,9 +350,12 @@ def run_reference(args):
             "vs_baseline": None, "dtype": "f64 accumulate, f32 storage (q4_0 weights)", "data": "synthetic",
             "impl": "reference", "config": workload_config(args, world),
             "cpu_baseline": {"value": value, "unit": "tok/s", "cores": n_threads, "kind": "port",
-                             "sample": res["sample"]},
+                             "sample": res["sample"], "extrapolated": True,
+                             "single_thread": {"value": one["tok_s"], "unit": "tok/s", "cores": 1,
+                                               "sample": one["sample"], "extrapolated": True}},
             "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "detail": {"t_layer_s": res["t_layer_s"], "t_head_s": res["t_head_s"], "warm_tok_s": warm["tok_s"]}}
+            "detail": {"t_layer_s": res["t_layer_s"], "t_head_s": res["t_head_s"], "warm_tok_s": warm["tok_s"],
+                       "single_thread_t_layer_s": one["t_layer_s"]}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -467,7 +644,8 @@ def run_ours(args):
         n_threads = os.cpu_count() or 1
         os.environ["TABNET_ORACLE_THREADS"] = str(n_threads)
         o = oracle_token_time(pkg, m, n_threads, 3)
-        cpu = {"value": o["tok_s"], "unit": "tok/s", "cores": n_threads, "kind": "port", "sample": o["sample"]}
+        cpu = {"value": o["tok_s"], "unit": "tok/s", "cores": n_threads, "kind": "port", "sample": o["sample"],
+               "extrapolated": True}
     step_bytes = pkg.pack.model_bytes(m) + M * m.n_layers * 2 * (args.prompt + args.warmup + args.steps) * \
         m.n_kv_heads * hd * 4
     line = {"metric": METRIC, "value": round(value, 3), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -537,6 +715,10 @@ def pipeline_e2e(pkg, torch, ctx, pipe, args, rank, world, barrier, max_over_ran
 
 def main(argv=None):
     args = parse_args(argv)
+    if args.micro == "matvec":
+        return micro_matvec(args)
+    if args.micro == "attn":
+        return micro_attn(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

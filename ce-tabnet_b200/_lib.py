@@ -111,6 +111,7 @@ SIGNATURES = [
     ("tn_matrix_matvec", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("tn_matrix_dequant", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     ("tn_matrix_device_bytes", C.c_uint64, [C.c_void_p]),
+    ("tn_matrix_counter_sum", C.c_int, [C.c_void_p, C.POINTER(C.c_int64)]),
     ("tn_matrix_free", None, [C.c_void_p]),
     ("tn_attention_scratch_bytes", C.c_uint64, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32]),
     ("tn_attention", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,

@@ -105,6 +105,19 @@ extern "C" int tn_matrix_dequant(const tn_matrix* m, float* d_out, void* stream)
 
 extern "C" uint64_t tn_matrix_device_bytes(const tn_matrix* m) { return m ? m->m.bytes : 0; }
 
+extern "C" int tn_matrix_counter_sum(const tn_matrix* m, int64_t* out) {
+  clear_error();
+  TN_REQUIRE(m && out, TN_EINVAL, "tn_matrix_counter_sum: bad argument");
+  DevSwitch g(m->device);
+  *out = 0;
+  if (!m->m.cnt || !m->m.cnt_ints) return TN_OK;
+  std::vector<int> h(m->m.cnt_ints);
+  TN_CHECK_CUDA(cudaDeviceSynchronize());
+  TN_CHECK_CUDA(cudaMemcpy(h.data(), m->m.cnt, h.size() * sizeof(int), cudaMemcpyDeviceToHost));
+  for (int v : h) *out += v;
+  return TN_OK;
+}
+
 extern "C" void tn_matrix_free(tn_matrix* m) {
   if (!m) return;
   DevSwitch g(m->device);

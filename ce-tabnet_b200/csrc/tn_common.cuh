@@ -23,10 +23,14 @@ namespace tn {
 void set_error(const char* fmt, ...);
 void clear_error();
 
+// A failing runtime call also leaves its error in the runtime's last-error
+// slot; it is read back here so that the next TN_CHECK_LAUNCH (which asks
+// cudaGetLastError) does not report this call's error as its own.
 #define TN_CHECK_CUDA(expr)                                                              \
   do {                                                                                   \
     cudaError_t e_ = (expr);                                                             \
     if (e_ != cudaSuccess) {                                                             \
+      (void)cudaGetLastError();                                                          \
       ::tn::set_error("%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
       return TN_ECUDA;                                                                   \
     }                                                                                    \

@@ -658,7 +658,7 @@ constexpr int ATT_WARPS = 8;
 template <int HD, int G>
 __global__ void __launch_bounds__(ATT_WARPS * 32)
     k_attn(const float* __restrict__ q, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
-           size_t slot_stride, size_t kvh_stride, const RowInfo* __restrict__ rows, int S, float scale,
+           size_t slot_stride, size_t kvh_stride, const RowInfo* __restrict__ rows, int S, int nkv, float scale,
            float* __restrict__ out, int ldo) {
   constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD;
   constexpr unsigned FULL = 0xffffffffu;
@@ -666,7 +666,9 @@ __global__ void __launch_bounds__(ATT_WARPS * 32)
   __shared__ __align__(16) float s_o[ATT_WARPS][GH];
   __shared__ float s_w[ATT_WARPS][G];  // merge weights exp(m - M) of the warps
   __shared__ float s_M[G], s_L[G];
-  const int split = blockIdx.x, kvh = blockIdx.y, t = blockIdx.z;
+  // grid.x = (row, KV head, split), splits innermost: the S splits of a
+  // (row, KV head) are one cluster, and rows are not bounded by gridDim.z
+  const int split = (int)(blockIdx.x % S), kvh = (int)((blockIdx.x / S) % nkv), t = (int)(blockIdx.x / (S * nkv));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_launch_dependents();
   pdl_wait();  // q and the cache rows of this step come from the previous kernels
@@ -841,14 +843,14 @@ template <int HD>
 static int launch_attn_hd(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
                           size_t kvh_stride, const RowInfo* rows, int T, int nKV, int G, int n_splits, float* out,
                           int ldo, cudaStream_t s) {
-  const dim3 grid(n_splits, nKV, T);
+  const dim3 grid((unsigned)(n_splits * nKV * T));
   const float scale = (float)(1.0 / sqrt((double)HD));
   cudaError_t e;
   switch (G) {
 #define TN_ATT_CASE(g)                                                                                          \
   case g:                                                                                                       \
     e = launch_pdl_cluster(k_attn<HD, g>, grid, dim3(ATT_WARPS * 32), 0, n_splits, s, q, ldq, kc, vc,       \
-                           slot_stride, kvh_stride, rows, n_splits, scale, out, ldo);                            \
+                           slot_stride, kvh_stride, rows, n_splits, nKV, scale, out, ldo);                       \
     break;
     TN_ATT_CASE(1)
     TN_ATT_CASE(2)
@@ -858,7 +860,7 @@ static int launch_attn_hd(const float* q, int ldq, const float* kc, const float*
     case 16:
       if (HD <= 64) {
         e = launch_pdl_cluster(k_attn<HD <= 64 ? HD : 64, 16>, grid, dim3(ATT_WARPS * 32), 0, n_splits, s, q, ldq,
-                               kc, vc, slot_stride, kvh_stride, rows, n_splits, scale, out, ldo);
+                               kc, vc, slot_stride, kvh_stride, rows, n_splits, nKV, scale, out, ldo);
         break;
       }
       [[fallthrough]];

@@ -195,6 +195,10 @@ int tn_matrix_matvec(const tn_matrix* m, int32_t n_tokens, const float* d_x, flo
 /* the dequantised matrix, [rows][cols] f32 (bit-exact check of repack + decode) */
 int tn_matrix_dequant(const tn_matrix* m, float* d_out, void* stream);
 uint64_t tn_matrix_device_bytes(const tn_matrix* m);
+/* Test hook: the sum of the matrix's cross-CTA arrival and ticket counters,
+ * which every completed matvec leaves at zero for the next launch
+ * (synchronises the matrix's device). */
+int tn_matrix_counter_sum(const tn_matrix* m, int64_t* out);
 void tn_matrix_free(tn_matrix* m);
 
 /* GQA attention for query rows over an f32 KV cache laid out
@@ -204,7 +208,8 @@ void tn_matrix_free(tn_matrix* m);
  * max_ctx are clamped.  Math of
  * web/inference-worker.js:556-564; d_q, d_out: [n_rows][n_heads*head_dim].
  * d_scratch (device, tn_attention_scratch_bytes() bytes, 256-byte aligned)
- * holds the row table and the split-K partials. */
+ * holds only the row table, 16 bytes a row: the split-K partials merge on
+ * chip.  Any row count that fits the caller's buffers is accepted. */
 uint64_t tn_attention_scratch_bytes(int32_t n_rows, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                     int32_t max_ctx);
 int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
@@ -233,7 +238,10 @@ int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_
  * first call before any stream capture.  All calls share the one array and
  * leave their contents in it; every call writes all it reads, so nothing needs
  * clearing, but calls whose work overlaps on the GPU (other streams, other
- * threads) race on the array and must be serialised by the caller. */
+ * threads) race on the array and must be serialised by the caller.  The
+ * address is kept for the life of the process: after cudaDeviceReset (or a
+ * reset of the device's primary context) reload the library before calling
+ * this entry point again. */
 #define TN_ATTENTION_STATIC_SCRATCH_BYTES (1u << 20)
 int tn_attention_static(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
                         int32_t head_dim, int32_t max_ctx, const float* d_q, const float* d_k,

@@ -173,9 +173,32 @@ int ref_matvec_packed(const uint8_t* W, int quant, int rows, int cols, const flo
 #pragma omp for schedule(static)
     for (int r = 0; r < rows; r++) {
       if (!row) continue;
-      ref_dequant_range(W, quant, (int64_t)r * cols, cols, row);
       double a = 0;
-      for (int c = 0; c < cols; c++) a += (double)row[c] * (double)x[c];
+      if ((quant == REF_Q4_0 || quant == REF_Q8_0) && cols % QK == 0) {
+        /* Rows start on a block boundary: the block loop of dequantToF32
+         * (web/inference-worker.js:107-124) takes each block's scale once, and
+         * every weight is formed and accumulated exactly as below in element
+         * order, so the sums are those of the element-wise path. */
+        const int64_t bb = (quant == REF_Q8_0) ? (2 + QK) : (2 + QK / 2);
+        const uint8_t* blk = W + ((int64_t)r * cols / QK) * bb;
+        for (int c0 = 0; c0 < cols; c0 += QK, blk += bb) {
+          const double scale = ref_f16_to_f32(rd_u16(blk));
+          for (int j = 0; j < QK; j++) {
+            float w;
+            if (quant == REF_Q8_0) {
+              w = (float)((double)(int8_t)blk[2 + j] * scale);
+            } else {
+              const uint8_t byte = blk[2 + j / 2];
+              const int nib = (j & 1) ? (byte >> 4) : (byte & 0x0f);
+              w = (float)((double)(nib - 8) * scale);
+            }
+            a += (double)w * (double)x[c0 + j];
+          }
+        }
+      } else {
+        ref_dequant_range(W, quant, (int64_t)r * cols, cols, row);
+        for (int c = 0; c < cols; c++) a += (double)row[c] * (double)x[c];
+      }
       y[r] = (float)a;
     }
     free(row);

@@ -119,6 +119,37 @@ def test_matvec_token_sweep(pkg, ref, torch_cuda, quant, rows, cols, T):
         assert _maxrel(got[t], want) < MATVEC_TOL, (t, _maxrel(got[t], want))
 
 
+def test_matvec_back_to_back_same_matrix(pkg, ref, torch_cuda):
+    """One pool-eligible matrix (the 8B lm_head: whole tiles taken by ticket)
+    launched repeatedly on one stream with no synchronisation in between,
+    alternating one, two and three tokens (three = a two-token and a one-token
+    launch) with fresh x each time: every output row matches the oracle, and
+    the per-tile arrival and per-chunk ticket counters read back as zero."""
+    torch = torch_cuda
+    rows, cols, quant = 128256, 4096, "q4_0"
+    buf = _synth_matrix(pkg, rows, cols, quant, seed=77)
+    mat = Mat(pkg, quant, rows, cols, buf)
+    rng = np.random.default_rng(78)
+    runs = []
+    for T in (1, 2, 1, 3, 2, 1):
+        x = rng.standard_normal((T, cols)).astype(np.float32)
+        dx = torch.from_numpy(x).cuda()
+        dy = torch.full((T, rows), float("nan"), dtype=torch.float32, device="cuda")
+        runs.append((x, dx, dy))
+    torch.cuda.synchronize()
+    for x, dx, dy in runs:  # enqueued back to back
+        pkg._lib.check(mat.lib.tn_matrix_matvec(mat.h, x.shape[0], dx.data_ptr(), dy.data_ptr(), None))
+    torch.cuda.synchronize()
+    for i, (x, _, dy) in enumerate(runs):
+        got = dy.cpu().numpy()
+        for t in range(x.shape[0]):
+            want = ref.matvec(buf, quant, rows, cols, x[t])
+            assert _maxrel(got[t], want) < MATVEC_TOL, (i, t, _maxrel(got[t], want))
+    total = C.c_int64(-1)
+    pkg._lib.check(mat.lib.tn_matrix_counter_sum(mat.h, C.byref(total)))
+    assert total.value == 0
+
+
 @pytest.mark.parametrize("hd,nH,nKV", [(128, 32, 8), (128, 64, 8), (32, 8, 2)])
 def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV):
     torch = torch_cuda

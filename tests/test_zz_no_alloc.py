@@ -68,6 +68,33 @@ def test_static_scratch_attention_matches_caller_scratch(pkg, torch_cuda):
         assert err <= ATTN_TOL, (i, err)
 
 
+def test_static_scratch_row_limit_boundary(pkg, torch_cuda):
+    """65536 rows fill the fixed array exactly and run (rows are not bounded
+    by the grid's y / z limits); the result equals the caller-scratch entry
+    point's.  65537 rows are refused before anything is launched."""
+    torch = torch_cuda
+    lib = pkg._lib.load()
+    rng = np.random.default_rng(65536)
+    n = 1 << 16
+    lens = [1 + (r % 4) for r in range(n)]
+    c = _case(torch, rng, 2, 8, 2, 32, 4, lens, [r % 2 for r in range(n)])
+    assert lib.tn_attention_scratch_bytes(n, 8, 2, 32, 4) == (1 << 20)
+    want = _with_caller_scratch(pkg, torch, c)
+    got = _with_static_scratch(pkg, torch, c)
+    assert np.isfinite(got).all()
+    err = float(np.max(np.abs(got - want)) / max(float(np.max(np.abs(want))), 1e-30))
+    assert err <= ATTN_TOL, err
+    n1 = n + 1
+    dummy = torch.zeros(16, dtype=torch.float32, device="cuda")
+    idx = torch.zeros(n1, dtype=torch.int32, device="cuda")
+    rc = lib.tn_attention_static(n1, 1, 8, 2, 32, 4, dummy.data_ptr(), dummy.data_ptr(), dummy.data_ptr(),
+                                 idx.data_ptr(), idx.data_ptr(), dummy.data_ptr(), None)
+    assert rc == pkg._lib.TN_ECAPACITY
+    # a refused call leaves nothing behind: the next call runs
+    got2 = _with_static_scratch(pkg, torch, c)
+    assert np.array_equal(got2, got)
+
+
 def test_static_scratch_rejects_oversized_calls(pkg, torch_cuda):
     torch = torch_cuda
     lib = pkg._lib.load()
