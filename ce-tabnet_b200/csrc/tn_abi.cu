@@ -40,6 +40,9 @@ struct tn_matrix {
   Matrix m;
   int device = 0;
   int* d_err = nullptr;  // bounded-wait flag of the decode kernel
+  // activation tiles of the dequant-GEMM, grown on first use by a token count
+  void* gemm_scratch = nullptr;
+  size_t gemm_bytes = 0;
 };
 
 extern "C" int tn_matrix_create(int32_t device, int32_t quant, int32_t rows, int32_t cols, const void* packed,
@@ -93,7 +96,21 @@ extern "C" int tn_matrix_matvec(const tn_matrix* m, int32_t n_tokens, const floa
   clear_error();
   TN_REQUIRE(m && d_x && d_y && n_tokens >= 0, TN_EINVAL, "tn_matrix_matvec: bad argument");
   DevSwitch g(m->device);
-  return matvec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, m->d_err, (cudaStream_t)stream);
+  tn_matrix* mm = const_cast<tn_matrix*>(m);
+  if (gemm_ok(m->m, n_tokens)) {
+    const size_t need = gemm_scratch_bytes(n_tokens, m->m.cols);
+    if (need > mm->gemm_bytes) {
+      // (the first call with more tokens than any before allocates; later ones reuse)
+      TN_CHECK_CUDA(cudaStreamSynchronize((cudaStream_t)stream));
+      if (mm->gemm_scratch) cudaFree(mm->gemm_scratch);
+      mm->gemm_scratch = nullptr;
+      mm->gemm_bytes = 0;
+      TN_CHECK_CUDA(cudaMalloc(&mm->gemm_scratch, need));
+      mm->gemm_bytes = need;
+    }
+  }
+  return matvec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, m->d_err, mm->gemm_scratch,
+                mm->gemm_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int tn_matrix_dequant(const tn_matrix* m, float* d_out, void* stream) {
@@ -123,6 +140,7 @@ extern "C" void tn_matrix_free(tn_matrix* m) {
   DevSwitch g(m->device);
   matrix_free(&m->m);
   if (m->d_err) cudaFree(m->d_err);
+  if (m->gemm_scratch) cudaFree(m->gemm_scratch);
   delete m;
 }
 

@@ -1,0 +1,469 @@
+// tn_gemm.cu -- q4_0 / q8_0 dequant-GEMM on the 5th-generation tensor cores
+// (tcgen05, accumulators in tensor memory) for steps of many tokens: prefill
+// positions and fused micro-batches.
+//
+// The matvec of web/inference-worker.js:523-527 for T tokens at once,
+// Y[t][r] = sum_k W[r][k] X[t][k], as D[M = rows][N = tokens] = A B^T with
+// A the weights and B the activations, both K-major fp16 in shared memory and
+// D in f32 TMEM columns.
+//
+// Exactness.  A q4_0 weight is (n - 8) d with d an fp16 scale, a q8_0 weight
+// q d: a multiple of the last place of d with at most 14 (q4) / 18 (q8)
+// significant bits.  It splits into two fp16 values with no error:
+//   w_hi = RN_fp16((n - 8) d)            (one HMUL2)
+//   w_lo = fma_fp16(n - 8, d, -w_hi)      (one HFMA2; the exact residual has
+//                                          at most 3 (q4) / 7 (q8) significant
+//                                          bits on the grid of d, so it is an
+//                                          fp16 value and the FMA returns it)
+// An activation row is scaled by a power of two so its largest magnitude lies
+// in [2^14, 2^15) and split likewise, x_hi = RN_fp16(x 2^e), x_lo =
+// RN_fp16(x 2^e - x_hi) (22 significant bits of x).  Three MMAs per K step
+// accumulate w_hi x_hi + w_hi x_lo + w_lo x_hi in one f32 accumulator; the
+// dropped w_lo x_lo is below 2^-22 of each product.  The result is scaled
+// back by 2^-e per token in the epilogue.
+//
+// CTA = one 128-row M tile (8 record tiles of the matrix's fragment-ordered
+// layout) x one N tile of NT <= 128 tokens, K in slices of 64 (one block pair):
+//   warp 0       raw-weight producer: the 8 records of each slice (one bulk
+//                copy per record tile; weights do not depend on the previous
+//                kernel, so the first slices stream before the dependency wait)
+//   warp 1       TMEM allocator and MMA issuer (one thread): 4 K16 steps x 3
+//                MMAs per slice; tcgen05.commit frees the slice's stage
+//   warps 2..5   dequant: records -> fp16 hi / lo tiles in the 128-byte
+//                swizzled K-major layout the MMA descriptors name; at the end
+//                the epilogue (tcgen05.ld of the accumulator, scale, store /
+//                residual add / SwiGLU)
+//   warp 6       activation producer: the slice's x_hi / x_lo tile, written
+//                pre-swizzled by k_gemm_prep, in one bulk copy
+// Every wait is bounded; a CTA that gives up drains its copies and MMAs,
+// frees its TMEM and raises the error flag.
+#include "tn_kernels.cuh"
+#include "tn_ptx.cuh"
+
+namespace tn {
+
+constexpr int GM_BM = 128;                     // rows per CTA
+constexpr int GM_RT = GM_BM / 16;              // record tiles per CTA
+constexpr int GM_DQ_WARPS = 4;                 // dequant / epilogue warps
+constexpr int GM_THREADS = 7 * 32;
+constexpr int GM_MAX_ST = 4, GM_MAX_RAW = 4;
+constexpr uint32_t GM_A_BYTES = GM_BM * 128;   // one fp16 [128][64] swizzled tile
+
+struct GemmArgs {
+  const uint8_t* data;  // fragment-ordered records of the matrix
+  int rows, tiles, pairs;
+  const uint8_t* xs;    // k_gemm_prep output: [n tile][pair][hi, lo][NT][64] fp16, swizzled
+  const float* xscale;  // [T] 2^-e of each token row
+  int T, NT, ntiles;
+  float* y;
+  int ldy, mode;
+  int stages, raw_stages;
+  uint32_t stage_bytes, tmem_cols, idesc;
+  int* err;
+};
+
+// byte offset of element (n, k) of an fp16 [rows][64] K-major tile in the
+// 128-byte swizzle (8-row atoms of 1024 bytes; the 16-byte chunk index of a
+// row is XORed with the row index mod 8)
+__host__ __device__ __forceinline__ uint32_t sw128_off(int n, int k) {
+  return (uint32_t)((n >> 3) * 1024 + (n & 7) * 128 + ((((k >> 3) ^ n) & 7) << 4) + (k & 7) * 2);
+}
+
+// shared-memory matrix descriptor of a K-major, 128-byte-swizzled tile at
+// `addr` (1024-byte aligned): stride between 8-row atoms 1024 bytes,
+// descriptor version 1 (sm_100), layout type 2 (SWIZZLE_128B)
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ void sts64(uint32_t addr, uint32_t a, uint32_t b) {
+  asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
+}
+
+// Four weights of one row: bytes u0..u3 of `u` hold (value + bias) as
+// unsigned 8-bit integers; 0x64XX is the fp16 1024 + XX, so subtracting
+// (1024 + bias) gives the signed value exactly.  Returns hi pair (0,1), (2,3)
+// and lo pair (0,1), (2,3) for the scale d (fp16, both halves).
+__device__ __forceinline__ void dq4(uint32_t u, uint32_t d2, uint32_t off2, uint32_t (&hi)[2], uint32_t (&lo)[2]) {
+  const uint32_t p0 = __byte_perm(u, 0x64646464u, 0x4140), p1 = __byte_perm(u, 0x64646464u, 0x4342);
+  const uint32_t v0 = hsub2(p0, off2), v1 = hsub2(p1, off2);
+  hi[0] = hmul2(v0, d2);
+  hi[1] = hmul2(v1, d2);
+  lo[0] = hfma2(v0, d2, hi[0] ^ 0x80008000u);
+  lo[1] = hfma2(v1, d2, hi[1] ^ 0x80008000u);
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
+  constexpr int REC = tile_rec_bytes(KIND), AB = tile_a_bytes(KIND);
+  extern __shared__ uint8_t gsm_dyn[];
+  __shared__ __align__(8) uint64_t rfull[GM_MAX_RAW], rempty[GM_MAX_RAW];
+  __shared__ __align__(8) uint64_t afull[GM_MAX_ST], bfull[GM_MAX_ST], sempty[GM_MAX_ST];
+  __shared__ __align__(8) uint64_t accbar;
+  __shared__ uint32_t tmem_base;
+  __shared__ int last_raw[GM_MAX_RAW], last_b[GM_MAX_ST];
+  __shared__ volatile int abort_flag;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // the n tiles of one M tile are neighbours in launch order: they share the raw weights in L2
+  const int nt = (int)(blockIdx.x % a.ntiles), mt = (int)(blockIdx.x / a.ntiles);
+  const int t0 = mt * GM_RT, ntl = min(GM_RT, a.tiles - t0);
+  const int K = a.pairs;  // slices
+  const uint32_t sbase = (smem_u32(gsm_dyn) + 1023u) & ~1023u;
+  uint8_t* const smem = gsm_dyn + (sbase - smem_u32(gsm_dyn));
+  uint8_t* const raw = smem + (size_t)a.stages * a.stage_bytes;
+  const uint32_t raw_stage = GM_RT * REC;
+  const uint32_t bbytes = 2u * (uint32_t)a.NT * 128u;
+
+  if (tid == 0) {
+    abort_flag = 0;
+    for (int r = 0; r < a.raw_stages; r++) {
+      mbar_init(&rfull[r], 1);
+      mbar_init(&rempty[r], GM_DQ_WARPS);
+      last_raw[r] = -1;
+    }
+    for (int s = 0; s < a.stages; s++) {
+      mbar_init(&afull[s], GM_DQ_WARPS);
+      mbar_init(&bfull[s], 1);
+      mbar_init(&sempty[s], 1);
+      last_b[s] = -1;
+    }
+    mbar_init(&accbar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) tmem_alloc(&tmem_base, a.tmem_cols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  pdl_launch_dependents();
+  const uint32_t tmem = tmem_base;
+
+  if (warp == 0) {
+    // ================= raw weights: 8 records per slice, raw_stages slices ahead
+    if (lane == 0) {
+      for (int k = 0; k < K; k++) {
+        const int r = k % a.raw_stages;
+        if (k >= a.raw_stages && !mbar_wait(&rempty[r], ((k / a.raw_stages) - 1) & 1, &abort_flag)) break;
+        mbar_expect_tx(&rfull[r], (uint32_t)ntl * REC);
+        for (int j = 0; j < ntl; j++)
+          bulk_g2s(raw + (size_t)r * raw_stage + (size_t)j * REC,
+                   a.data + ((size_t)(t0 + j) * a.pairs + k) * REC, REC, &rfull[r]);
+        last_raw[r] = k;
+      }
+    }
+  } else if (warp == 6) {
+    // ================= activations: the slice's x_hi | x_lo tile, one bulk copy
+    if (lane == 0) {
+      pdl_wait();  // xs is written by the previous kernel
+      for (int k = 0; k < K; k++) {
+        const int s = k % a.stages;
+        if (k >= a.stages && !mbar_wait(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag)) break;
+        mbar_expect_tx(&bfull[s], bbytes);
+        bulk_g2s(smem + (size_t)s * a.stage_bytes + 2 * GM_A_BYTES,
+                 a.xs + ((size_t)nt * a.pairs + k) * bbytes, bbytes, &bfull[s]);
+        last_b[s] = k;
+      }
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer
+    if (lane == 0) {
+      for (int k = 0; k < K; k++) {
+        const int s = k % a.stages;
+        const uint32_t ph = (k / a.stages) & 1;
+        if (!mbar_wait(&afull[s], ph, &abort_flag) || !mbar_wait(&bfull[s], ph, &abort_flag)) break;
+        tc_fence_after();
+        const uint32_t st = sbase + (uint32_t)s * a.stage_bytes;
+        const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + GM_A_BYTES);
+        const uint64_t bhi = sw128_desc(st + 2 * GM_A_BYTES), blo = sw128_desc(st + 2 * GM_A_BYTES + bbytes / 2);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          // a K16 step is 32 bytes further along the swizzled rows (descriptor units of 16 bytes)
+          const uint64_t dj = (uint64_t)(2 * j);
+          umma_f16(tmem, ahi + dj, bhi + dj, a.idesc, (k | j) != 0);
+          umma_f16(tmem, ahi + dj, blo + dj, a.idesc, 1u);
+          umma_f16(tmem, alo + dj, bhi + dj, a.idesc, 1u);
+        }
+        umma_commit(&sempty[s]);  // the stage is free once these MMAs have read it
+      }
+      // completion of every MMA issued above (also after giving up, so the
+      // TMEM is only freed when nothing writes it any more)
+      umma_commit(&accbar);
+    }
+  } else {
+    // ================= dequant (warps 2..5), then the epilogue
+    const int dw = warp - 2, g = lane >> 2, c = lane & 3;
+    const uint32_t off2 = KIND == MK_Q4 ? 0x64086408u : 0x64806480u;  // fp16 (1024 + bias) twice
+    for (int k = 0; k < K; k++) {
+      const int r = k % a.raw_stages;
+      if (!__all_sync(0xffffffffu, mbar_wait(&rfull[r], (k / a.raw_stages) & 1, &abort_flag))) break;
+      // this lane's slots of record tiles 2 dw and 2 dw + 1
+      constexpr int WPS = AB / 128;  // 32-bit words per lane slot: 4 (q4) / 8 (q8)
+      uint32_t w[2][WPS], sc[2][2];
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const int tt = 2 * dw + j;
+        const uint8_t* rec = raw + (size_t)r * raw_stage + (size_t)tt * REC;
+#pragma unroll
+        for (int v = 0; v < WPS; v++)
+          w[j][v] = tt < ntl ? reinterpret_cast<const uint32_t*>(rec + lane * (AB / 32))[v] : 0u;
+#pragma unroll
+        for (int q = 0; q < 2; q++) sc[j][q] = tt < ntl ? reinterpret_cast<const uint32_t*>(rec + AB)[2 * g + q] : 0u;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&rempty[r]);
+      const int s = k % a.stages;
+      if (k >= a.stages && !__all_sync(0xffffffffu, mbar_wait(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag)))
+        break;
+      const uint32_t st = sbase + (uint32_t)s * a.stage_bytes;
+#pragma unroll
+      for (int j = 0; j < 2; j++) {
+        const int tt = 2 * dw + j;
+#pragma unroll
+        for (int q = 0; q < 2; q++) {
+          // scales of rows g and g + 8 of block 2p + q, each in both fp16 halves
+          const uint32_t dg = __byte_perm(sc[j][q], 0, 0x1010), dg8 = __byte_perm(sc[j][q], 0, 0x3232);
+#pragma unroll
+          for (int h = 0; h < 2; h++) {
+            // elements 16 h + 4 c .. + 3 of block 2p + q = slice columns k0 .. k0 + 3
+            const int k0 = 32 * q + 16 * h + 4 * c;
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+              uint32_t bytes;
+              if (KIND == MK_Q4) {
+                // q4 word 2h + q: byte i = (s(row g) << 4) | s(row g + 8), s = n ^ 8
+                const uint32_t wd = w[j][2 * h + q];
+                bytes = (u == 0 ? (wd >> 4) : wd) & 0x0F0F0F0Fu;
+                bytes ^= 0x08080808u;  // n = s ^ 8, the unsigned nibble
+              } else {
+                // q8 word 4h + 2q + u: byte i = q8 value of row g + 8u; biased by 128
+                bytes = w[j][4 * h + 2 * q + u] ^ 0x80808080u;
+              }
+              uint32_t hi[2], lo[2];
+              dq4(bytes, u == 0 ? dg : dg8, off2, hi, lo);
+              const int row = tt * 16 + g + 8 * u;
+              const uint32_t off = sw128_off(row, k0);
+              sts64(st + off, hi[0], hi[1]);
+              sts64(st + GM_A_BYTES + off, lo[0], lo[1]);
+            }
+          }
+        }
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&afull[s]);
+    }
+    // ---- epilogue: this warp reads TMEM lanes 32 (warp % 4) .. + 31 = rows of the M tile
+    const bool ok = __all_sync(0xffffffffu, mbar_wait(&accbar, 0, &abort_flag)) && !abort_flag;
+    tc_fence_after();
+    if (ok) {
+      pdl_wait();  // y belongs to earlier kernels
+      const int quarter = warp & 3;
+      const int row = mt * GM_BM + quarter * 32 + lane;
+      for (int c0 = 0; c0 < a.NT; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; j++) {
+          const int n = nt * a.NT + c0 + j;
+          const bool tok = n < a.T;
+          const float val = __uint_as_float(v[j]) * (tok ? a.xscale[n] : 0.f);
+          if (a.mode == EPI_SWIGLU) {
+            const float up = __shfl_xor_sync(0xffffffffu, val, 1);
+            if (tok && !(row & 1) && row + 1 < a.rows)
+              a.y[(size_t)n * a.ldy + (row >> 1)] = (val / (1.0f + expf(-val))) * up;
+          } else if (tok && row < a.rows) {
+            float* py = a.y + (size_t)n * a.ldy + row;
+            *py = a.mode == EPI_RESID ? *py + val : val;
+          }
+        }
+      }
+    }
+    tc_fence_before();
+  }
+
+  __syncthreads();
+  if (tid == 0 && abort_flag) {
+    // no copy may still be landing when the CTA exits
+    for (int r = 0; r < a.raw_stages; r++) {
+      const int k = last_raw[r];
+      if (k < 0) continue;
+      abort_flag = 0;
+      if (!mbar_wait(&rfull[r], (k / a.raw_stages) & 1, &abort_flag)) break;
+    }
+    for (int s = 0; s < a.stages; s++) {
+      const int k = last_b[s];
+      if (k < 0) continue;
+      abort_flag = 0;
+      if (!mbar_wait(&bfull[s], (k / a.stages) & 1, &abort_flag)) break;
+    }
+    abort_flag = 0;
+    mbar_wait(&accbar, 0, &abort_flag);  // the MMAs' completion (committed on every path)
+    atomicExch(a.err, 1);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, a.tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------- prep
+// One CTA per token row of the padded N range: the row's largest magnitude
+// picks e (max |x| 2^e in [2^14, 2^15)); every 8-element group becomes a
+// 16-byte chunk of x_hi and one of x_lo at its swizzled place in the
+// (n tile, slice) tile.  Rows past T and columns past K are zero.
+__global__ void __launch_bounds__(256) k_gemm_prep(const float* __restrict__ x, int ldx, const int* __restrict__ rowsel,
+                                                   int T, int K, int pairs, int NT, uint8_t* __restrict__ xs,
+                                                   float* __restrict__ xscale) {
+  __shared__ uint32_t smax[8];
+  const int n = blockIdx.x, tid = threadIdx.x;
+  pdl_launch_dependents();
+  pdl_wait();
+  const bool valid = n < T;
+  const float* row = x + (size_t)(valid ? (rowsel ? rowsel[n] : n) : 0) * ldx;
+  uint32_t mb = 0u;
+  if (valid)
+    for (int i = tid; i < K; i += blockDim.x) mb = max(mb, __float_as_uint(row[i]) & 0x7fffffffu);
+  for (int o = 16; o > 0; o >>= 1) mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, o));
+  if ((tid & 31) == 0) smax[tid >> 5] = mb;
+  __syncthreads();
+  mb = 0u;
+  for (int w = 0; w < (int)(blockDim.x >> 5); w++) mb = max(mb, smax[w]);
+  // non-finite rows pass through unscaled (inf / NaN reach the output)
+  int e = 0;
+  if (mb != 0u && mb < 0x7f800000u) e = min(126, max(-126, 14 - ilogbf(__uint_as_float(mb))));
+  const float sc = __int_as_float((e + 127) << 23);
+  if (tid == 0) xscale[n] = valid ? __int_as_float((127 - e) << 23) : 0.f;
+  const int ntile = n / NT, nn = n % NT;
+  const size_t tile_bytes = (size_t)NT * 128;
+  for (int gi = tid; gi < pairs * 8; gi += blockDim.x) {
+    const int slice = gi >> 3, k = gi * 8;
+    uint32_t hv[4], lv[4];
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      float f[2];
+#pragma unroll
+      for (int m = 0; m < 2; m++) {
+        const int kk = k + 2 * i + m;
+        f[m] = (valid && kk < K) ? row[kk] * sc : 0.f;
+      }
+      const __half2 h2 = __floats2half2_rn(f[0], f[1]);
+      const float2 back = __half22float2(h2);
+      const __half2 l2 = __floats2half2_rn(f[0] - back.x, f[1] - back.y);
+      hv[i] = *reinterpret_cast<const uint32_t*>(&h2);
+      lv[i] = *reinterpret_cast<const uint32_t*>(&l2);
+    }
+    uint8_t* base = xs + ((size_t)ntile * pairs + slice) * 2 * tile_bytes + sw128_off(nn, k & 63);
+    *reinterpret_cast<uint4*>(base) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+    *reinterpret_cast<uint4*>(base + tile_bytes) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+static int gemm_max_dyn() {
+  static int v = -1;
+  if (v < 0) {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaFuncAttributes fa{};
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fa, k_gemm<MK_Q8>) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+    v = optin - (int)fa.sharedSizeBytes;
+    if (cudaFuncSetAttribute(k_gemm<MK_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, v) != cudaSuccess ||
+        cudaFuncSetAttribute(k_gemm<MK_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, v) != cudaSuccess) {
+      cudaGetLastError();
+      v = 0;
+    }
+  }
+  return v;
+}
+
+void gemm_tiling(int T, int* NT, int* ntiles) {
+  const int nt = (T + 127) / 128;
+  *ntiles = nt;
+  *NT = ((((T + nt - 1) / nt) + 15) / 16) * 16;
+}
+
+size_t gemm_scratch_bytes(int T, int cols) {
+  int NT, nt;
+  gemm_tiling(T, &NT, &nt);
+  const size_t pairs = ((size_t)cols + 63) / 64;
+  return (size_t)nt * pairs * 2 * NT * 128 + (size_t)nt * NT * sizeof(float) + 256;
+}
+
+bool gemm_ok(const Matrix& m, int T) { return (m.kind == MK_Q4 || m.kind == MK_Q8) && T >= kGemmMinTokens; }
+
+int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, float* y, int ldy, int mode,
+         void* scratch, size_t scratch_bytes, int* err, cudaStream_t s) {
+  TN_REQUIRE(m.kind == MK_Q4 || m.kind == MK_Q8, TN_EUNSUPPORTED, "gemm: matrix kind %d", m.kind);
+  TN_REQUIRE(mode == EPI_STORE || mode == EPI_RESID || mode == EPI_SWIGLU, TN_EINVAL, "gemm: epilogue %d", mode);
+  TN_REQUIRE(mode != EPI_SWIGLU || (m.rows & 1) == 0, TN_EINVAL, "swiglu needs paired rows");
+  TN_REQUIRE(err, TN_EINVAL, "gemm: error flag required");
+  if (T <= 0) return TN_OK;
+  const size_t need = gemm_scratch_bytes(T, m.cols);
+  TN_REQUIRE(scratch && scratch_bytes >= need, TN_EINVAL, "gemm: scratch of %zu bytes, %zu needed", scratch_bytes,
+             need);
+  TN_REQUIRE((reinterpret_cast<uintptr_t>(scratch) & 255) == 0, TN_EINVAL, "gemm: scratch must be 256-byte aligned");
+  int NT, nt;
+  gemm_tiling(T, &NT, &nt);
+  uint8_t* xs = (uint8_t*)scratch;
+  const size_t xs_bytes = (size_t)nt * m.pairs * 2 * NT * 128;
+  float* xscale = (float*)(xs + ((xs_bytes + 255) & ~(size_t)255));
+  TN_CHECK_CUDA(launch_pdl(k_gemm_prep, dim3(nt * NT), dim3(256), 0, s, x, ldx, rowsel, T, m.cols, m.pairs, NT, xs,
+                           xscale));
+  const int max_dyn = gemm_max_dyn();
+  const int REC = tile_rec_bytes(m.kind);
+  GemmArgs a{};
+  a.data = m.data;
+  a.rows = m.rows;
+  a.tiles = m.tiles;
+  a.pairs = m.pairs;
+  a.xs = xs;
+  a.xscale = xscale;
+  a.T = T;
+  a.NT = NT;
+  a.ntiles = nt;
+  a.y = y;
+  a.ldy = ldy;
+  a.mode = mode;
+  a.stage_bytes = 2 * GM_A_BYTES + 2u * (uint32_t)NT * 128u;
+  a.raw_stages = m.kind == MK_Q4 ? 4 : 3;
+  const int raw_bytes = a.raw_stages * GM_RT * REC;
+  a.stages = std::min(GM_MAX_ST, (max_dyn - 1024 - raw_bytes) / (int)a.stage_bytes);
+  TN_REQUIRE(a.stages >= 2, TN_EUNSUPPORTED, "gemm: %d bytes of shared memory is too little", max_dyn);
+  a.tmem_cols = 32;
+  while ((int)a.tmem_cols < NT) a.tmem_cols <<= 1;
+  // kind::f16 instruction descriptor: f32 accumulator (bit 4), A and B fp16
+  // (formats 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
+  a.idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+  a.err = err;
+  const size_t smem = (size_t)a.stages * a.stage_bytes + raw_bytes + 1024;
+  const int grid = ((m.tiles + GM_RT - 1) / GM_RT) * nt;
+  if (m.kind == MK_Q4)
+    TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q4>, dim3(grid), dim3(GM_THREADS), smem, s, a));
+  else
+    TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q8>, dim3(grid), dim3(GM_THREADS), smem, s, a));
+  return TN_OK;
+}
+
+}  // namespace tn

@@ -504,12 +504,15 @@ static int matvec_kind(const Matrix& m, int T, const float* x, int ldx, float* y
 }
 
 int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, int* err,
-           cudaStream_t s) {
+           void* gemm_scratch, size_t gemm_scratch_bytes, cudaStream_t s) {
   if (T <= 0) return TN_OK;
   if (mode == EPI_SWIGLU) TN_REQUIRE((m.rows & 1) == 0, TN_EINVAL, "swiglu needs paired rows");
   switch (m.kind) {
     case MK_Q4:
-    case MK_Q8: return matvec_dec(m, T, x, ldx, y, ldy, mode, MvFuse(), err, s);
+    case MK_Q8:
+      if (gemm_ok(m, T) && gemm_scratch)
+        return gemm(m, T, x, ldx, nullptr, y, ldy, mode, gemm_scratch, gemm_scratch_bytes, err, s);
+      return matvec_dec(m, T, x, ldx, y, ldy, mode, MvFuse(), err, s);
     case MK_F16: return matvec_kind<MK_F16>(m, T, x, ldx, y, ldy, mode, s);
     default: return matvec_kind<MK_F32>(m, T, x, ldx, y, ldy, mode, s);
   }

@@ -118,8 +118,22 @@ enum EpiMode { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_QKV_ROPE = 3 };
 // y = W x for T tokens.  STORE: y[t*ldy + r] = v.  RESID: y[t*ldy + r] += v.
 // SWIGLU: rows (2i, 2i+1) hold (gate_i, up_i); y[t*ldy + i] = silu(gate) * up.
 // err: device int set to 1 if a bounded wait inside a kernel gave up.
+// q4_0 / q8_0 matrices take the tensor-core dequant-GEMM from kGemmMinTokens
+// tokens on when `gemm_scratch` (gemm_scratch_bytes(T, cols) bytes) is given.
 int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, int* err,
-           cudaStream_t s);
+           void* gemm_scratch, size_t gemm_scratch_bytes, cudaStream_t s);
+
+// ---- tcgen05 dequant-GEMM (tn_gemm.cu) for steps of many tokens
+constexpr int kGemmMinTokens = 3;
+bool gemm_ok(const Matrix& m, int T);
+// N tiling of T tokens: ntiles tiles of NT tokens (NT a multiple of 16, <= 128)
+void gemm_tiling(int T, int* NT, int* ntiles);
+// scratch of a T-token GEMM over `cols` columns: the prepared fp16 hi / lo
+// activation tiles and the per-token scales
+size_t gemm_scratch_bytes(int T, int cols);
+// y = W x (rows of x at rowsel[t] if given) with a STORE / RESID / SWIGLU epilogue
+int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, float* y, int ldy, int mode,
+         void* scratch, size_t scratch_bytes, int* err, cudaStream_t s);
 
 // per-row bookkeeping of a step: KV slot, RoPE position, KV write index, attention length
 struct RowInfo {

@@ -93,6 +93,8 @@ struct tn_stage {
   uint16_t *hid_in = nullptr, *hid_out = nullptr;
   int *ids = nullptr, *tok_out = nullptr, *err = nullptr;
   int* kerr = nullptr;  // set by a kernel whose bounded wait gave up
+  void* gemm_ws = nullptr;  // activation tiles of the dequant-GEMM (steps of many rows)
+  size_t gemm_ws_bytes = 0;
   double2* cs = nullptr;
   double* freq = nullptr;
   // control block: rows | outrows | sampler params, uploaded once per step
@@ -349,6 +351,12 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   if ((rc = dalloc(st, &st->err, 1))) return rc;
   if ((rc = dalloc(st, &st->kerr, 1))) return rc;
   if ((rc = dalloc(st, &st->cs, (size_t)T * (st->hd / 2)))) return rc;
+  if (T >= kGemmMinTokens) {
+    // the widest input of any matrix the GEMM may take: hidden, attention output or FFN activation
+    const int kmax = std::max(st->H, std::max(st->qDim, st->F));
+    st->gemm_ws_bytes = gemm_scratch_bytes(T, kmax);
+    if ((rc = dalloc(st, (char**)&st->gemm_ws, st->gemm_ws_bytes))) return rc;
+  }
   if ((rc = dalloc(st, &st->freq, (size_t)(st->hd / 2)))) return rc;
   // RoPE frequencies theta^(-2i/hd) in double (web/inference-worker.js:533)
   std::vector<double> freq(st->hd / 2);
@@ -459,7 +467,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec_dec(L.qkv, T, st->h, H, st->qkv, ldqkv, EPI_QKV_ROPE, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, st->kerr, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
       TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1,
                      rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->slot_stride, st->kvh_stride, st->nH,
                              st->nKV, st->hd, T, s));
@@ -470,19 +478,19 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
     if (fuse && matvec_dec_ok(L.o, T))
       TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, st->kerr, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
     if (fuse && matvec_dec_ok(L.gu, T)) {
       MvFuse f;
       f.norm_w = L.ffn_norm;
       TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec_dec(L.gu, T, st->h, H, st->act, st->F, EPI_SWIGLU, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.ffn_norm, st->xn, H, H, T, s));
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, st->kerr, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
     }
     if (fuse && matvec_dec_ok(L.down, T))
       TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec_dec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, st->kerr, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
   }
   if (st->last) {
     if (!(st->flags & TN_FLAG_NO_FUSED_DECODE) && matvec_dec_ok(st->lm_head, n_out)) {
@@ -494,7 +502,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, outrows, st->final_norm, st->xn, H, H, n_out, s));
       TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1,
-                     matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, st->kerr, s));
+                     matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
     }
     TN_STEP_LAUNCH(TN_PROF_OTHER, 1, sample_rows(st->logits, n_out, st->V, params, st->tok_out, s));
   } else {

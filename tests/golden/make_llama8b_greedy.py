@@ -3,7 +3,7 @@ Llama-3-8B-shaped q4_0 model (32 layers, one stage: first and last), seeded
 synthetic weights (seed 1), a 32-token uniform prompt, then 64 decode steps.
 
 Two runs, each a separate sequence of the same oracle stage:
-  greedy: every step feeds back the argmax (the north_star's 64-step bar);
+  greedy: every step feeds back the argmax (the 64-step greedy bar);
   forced: every step feeds a predetermined uniform token instead (teacher
           forcing), so each step's argmax depends on a different input and the
           comparison cannot sit at a fixed point of the greedy map.
@@ -13,7 +13,7 @@ that enters the final norm (base64 of little-endian float32).
 
 The oracle is the C restatement of the reference CPU path
 (web/inference-worker.js:471-583, 658-716); this script is test
-infrastructure, run once here:
+infrastructure, run once on a CPU host:
 
     python tests/golden/make_llama8b_greedy.py   (about 15 minutes on 8 cores)
 """
