@@ -159,7 +159,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
     if (lane == 0) {
       for (int k = 0; k < K; k++) {
         const int r = k % a.raw_stages;
-        if (k >= a.raw_stages && !mbar_wait(&rempty[r], ((k / a.raw_stages) - 1) & 1, &abort_flag)) break;
+        if (k >= a.raw_stages) {
+          if (!mbar_wait(&rempty[r], ((k / a.raw_stages) - 1) & 1, &abort_flag)) break;
+          // the dequant warps read this slot with generic loads; the refill is an
+          // async-proxy write: order the two proxies
+          fence_async_smem();
+        }
         mbar_expect_tx(&rfull[r], (uint32_t)ntl * REC);
         for (int j = 0; j < ntl; j++)
           bulk_g2s(raw + (size_t)r * raw_stage + (size_t)j * REC,
@@ -228,8 +233,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&rempty[r]);
       const int s = k % a.stages;
-      if (k >= a.stages && !__all_sync(0xffffffffu, mbar_wait(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag)))
-        break;
+      if (k >= a.stages) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag))) break;
+        // The tensor core read this stage through the async proxy; the stores
+        // below go through the generic proxy.  Without this fence they may land
+        // before the MMAs' reads that the commit reported complete (measured:
+        // the first record tile each warp rewrites, in the last K16 steps).
+        fence_async_smem();
+      }
       const uint32_t st = sbase + (uint32_t)s * a.stage_bytes;
 #pragma unroll
       for (int j = 0; j < 2; j++) {
@@ -319,6 +330,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
   }
   __syncthreads();
   if (warp == 1) {
+    __syncwarp();  // lane 0 rejoins the MMA warp before the warp-wide dealloc
     tc_fence_after();
     tmem_dealloc(tmem, a.tmem_cols);
   }

@@ -181,7 +181,7 @@ def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV):
 
 
 @pytest.mark.parametrize("L,n_rows,n_slots", [(512, 1, 1), (2048, 8, 8), (2048, 64, 16), (8192, 8, 4),
-                                              (32768, 1, 1), (32768, 8, 2)])
+                                              (8192, 64, 8), (32768, 1, 1), (32768, 8, 2), (32768, 64, 8)])
 def test_attention_context_sweep(pkg, ref, torch_cuda, L, n_rows, n_slots):
     """The GQA decode-attention sweep (32 query / 8 KV heads x 128, contexts
     512 .. 32768, 1 .. 64 concurrent rows) against the oracle."""

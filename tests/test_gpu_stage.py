@@ -4,12 +4,17 @@ freeStage), against the oracle on identical seeded weights and prompts.
 Greedy tokens must be identical; hidden states (fp16 hop frames, decoded)
 within max|a-b| / max|b| <= 1e-3.
 """
+import base64
+import json
+from pathlib import Path
+
 import numpy as np
 import pytest
 
 pytestmark = pytest.mark.gpu
 
 HIDDEN_TOL = 1e-3
+LOGIT_TOL = 1e-4  # max |a - b| / max |b| of a logits row (f32 accumulation vs the oracle's f64)
 
 
 def f16(bits):
@@ -45,12 +50,17 @@ def test_tiny_single_stage_greedy_64(pkg, ref, tiny, fused):
     want = oracle.forward(1, 0, token_ids=prompt)
     assert got == want["token_id"]
     toks = [got]
+    assert maxrel(ctx.peek("logits", 1)[0], want["logits"]) <= LOGIT_TOL
     for s in range(64):
         pos = 32 + s
         got = pkg.forward(ctx, {"seq_id": "a", "token_pos": pos, "token_ids": [toks[-1]], "temperature": 0})
         want = oracle.forward(1, pos, token_ids=[toks[-1]])
         lg = np.sort(want["logits"])[::-1]
         assert got["token_id"] == want["token_id"], (s, "top-2 gap", lg[0] - lg[1])
+        # every step's logits, not only their argmax (the greedy map of this
+        # tiny model settles on a fixed point after a dozen steps)
+        err = maxrel(ctx.peek("logits", 1)[0], want["logits"])
+        assert err <= LOGIT_TOL, (s, err)
         toks.append(got["token_id"])
     assert pkg.kv_len(ctx, "a") == 32 + 64 == oracle.kv_len(1)
     pkg.freeStage(ctx)
@@ -308,3 +318,61 @@ def test_large_shape_slices(pkg, ref, name, lo, hi, first, last):
         assert maxrel(f16(got), f16(want)) <= HIDDEN_TOL, ("decode", step)
     pkg.freeStage(ctx)
     oracle.free()
+
+
+def _device_weights(pkg, torch, m):
+    """The seeded packed model written straight into device memory (the same
+    bytes as the host writer, tests/test_gpu_kernels.py checks that)."""
+    w = {"layers": [], "on_device": True, "quant": m.quant, "embedQuant": m.embed_quant,
+         "lmHeadQuant": m.lm_head_quant}
+    for i in range(m.n_layers):
+        t = torch.empty(pkg.pack.tensor_bytes(m, i), dtype=torch.uint8, device="cuda")
+        pkg.pack.synth_device(m, i, t.data_ptr())
+        w["layers"].append({"idx": i, "buf": t, "quant": m.quant})
+    for k in ("embed", "norm", "lm_head"):
+        w[k] = torch.empty(pkg.pack.tensor_bytes(m, k), dtype=torch.uint8, device="cuda")
+        pkg.pack.synth_device(m, k, w[k].data_ptr())
+    torch.cuda.synchronize()
+    return w
+
+
+def test_llama8b_greedy_64_vs_oracle_fixture(pkg, torch_cuda):
+    """The whole Llama-3-8B-shaped q4_0 model as one stage (32 layers, 128256
+    vocab lm_head): a 32-token prompt prefill, then 64 decode steps, against
+    the oracle's run stored in tests/golden/llama8b_greedy.json (made by
+    tests/golden/make_llama8b_greedy.py).  Two sequences: greedy (argmax fed
+    back; the fixture's 65 tokens are all distinct, so the bar is not met at a
+    fixed point) and teacher-forced (fixed inputs).  Every step: identical
+    token, final hidden state (every 32nd element) within HIDDEN_TOL, the
+    oracle's 16 largest logits within HIDDEN_TOL of the largest."""
+    torch = torch_cuda
+    fx = json.loads((Path(__file__).parent / "golden" / "llama8b_greedy.json").read_text())
+    assert fx["greedy_distinct"] >= 16 and fx["forced_distinct"] >= 16
+    m = pkg.pack.MODELS["llama8b"]
+    w = _device_weights(pkg, torch, m)
+    ctx = pkg.initStage({"arch": "llama", "dims": m.dims(), "layers": [0, m.n_layers], "is_first": True,
+                         "is_last": True, "weights": w, "opts": {"max_ctx": 128, "max_seqs": 2, "device": 0}})
+    del w
+    torch.cuda.empty_cache()
+    stride, prompt = fx["hidden_stride"], fx["prompt"]
+
+    def check(rec, got_tok, rows, where):
+        assert got_tok == rec["token"], (where, got_tok, rec["token"], "oracle top-2 gap", rec["gap"])
+        h = ctx.peek("hidden", rows)[rows - 1][::stride]
+        want_h = np.frombuffer(base64.b64decode(rec["hidden_sub"]), dtype="<f4")
+        assert maxrel(h, want_h) <= HIDDEN_TOL, (where, maxrel(h, want_h))
+        lg = ctx.peek("logits", 1)[0]
+        tv = np.asarray(rec["top_val"], dtype=np.float64)
+        err = float(np.max(np.abs(lg[rec["top_idx"]] - tv)) / np.max(np.abs(tv)))
+        assert err <= HIDDEN_TOL, (where, err)
+
+    for run, seq in (("greedy", "g"), ("forced", "f")):
+        steps = fx[run]
+        tok = pkg.forward(ctx, {"seq_id": seq, "token_pos": 0, "token_ids": prompt, "temperature": 0})["token_id"]
+        check(steps[0], tok, len(prompt), (run, "prefill"))
+        for s in range(64):
+            inp = tok if run == "greedy" else fx["forced_inputs"][s]
+            tok = pkg.forward(ctx, {"seq_id": seq, "token_pos": len(prompt) + s, "token_ids": [inp],
+                                    "temperature": 0})["token_id"]
+            check(steps[s + 1], tok, 1, (run, s))
+    pkg.freeStage(ctx)
