@@ -193,7 +193,9 @@ def micro_matvec(args):
             for T in _ints(args.tokens):
                 x = torch.randn(T, cols, device="cuda")
                 y = torch.empty(T, rows, device="cuda")
-                for i in range(max(3, args.warmup)):
+                # every copy once (the first call of a copy with a new token count
+                # sizes its GEMM scratch), then the warm-up launches
+                for i in range(copies + max(3, args.warmup)):
                     P.check(lib.tn_matrix_matvec(mats[i % copies], T, x.data_ptr(), y.data_ptr(), None))
                 torch.cuda.synchronize()
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

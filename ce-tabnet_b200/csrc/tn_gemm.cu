@@ -30,11 +30,18 @@
 //   warp 1       TMEM allocator and MMA issuer (one thread): 4 K16 steps x 3
 //                MMAs per slice; tcgen05.commit frees the slice's stage
 //   warps 2..5   dequant: records -> fp16 hi / lo tiles in the 128-byte
-//                swizzled K-major layout the MMA descriptors name; at the end
-//                the epilogue (tcgen05.ld of the accumulator, scale, store /
-//                residual add / SwiGLU)
+//                swizzled K-major layout the MMA descriptors name
 //   warp 6       activation producer: the slice's x_hi / x_lo tile, written
 //                pre-swizzled by k_gemm_prep, in one bulk copy
+//   warps 7..10  drain + epilogue.  The tensor core's additions into its f32
+//                accumulator do not round to nearest (measured: an error that
+//                grows with the number of accumulating MMAs, ~1e-4 of max |y|
+//                at K = 28672).  So each chunk of GM_CHUNK slices accumulates
+//                into one of two partial TMEM buffers (ping-pong), and these
+//                warps add every finished partial into a running f32 sum in
+//                TMEM with IEEE adds (tcgen05.ld / st), in chunk order; the
+//                last chunk's drain is the epilogue (scale, store / residual
+//                add / SwiGLU).
 // Every wait is bounded; a CTA that gives up drains its copies and MMAs,
 // frees its TMEM and raises the error flag.
 #include "tn_kernels.cuh"
@@ -44,8 +51,10 @@ namespace tn {
 
 constexpr int GM_BM = 128;                     // rows per CTA
 constexpr int GM_RT = GM_BM / 16;              // record tiles per CTA
-constexpr int GM_DQ_WARPS = 4;                 // dequant / epilogue warps
-constexpr int GM_THREADS = 7 * 32;
+constexpr int GM_DQ_WARPS = 4;                 // dequant warps
+constexpr int GM_DR_WARPS = 4;                 // drain / epilogue warps
+constexpr int GM_THREADS = 11 * 32;
+constexpr int GM_CHUNK = 4;                    // K slices accumulated by the tensor core before a drain
 constexpr int GM_MAX_ST = 4, GM_MAX_RAW = 4;
 constexpr uint32_t GM_A_BYTES = GM_BM * 128;   // one fp16 [128][64] swizzled tile
 
@@ -58,7 +67,7 @@ struct GemmArgs {
   float* y;
   int ldy, mode;
   int stages, raw_stages;
-  uint32_t stage_bytes, tmem_cols, idesc;
+  uint32_t stage_bytes, tmem_cols, acc_cols, idesc;
   int* err;
 };
 
@@ -115,6 +124,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
   extern __shared__ uint8_t gsm_dyn[];
   __shared__ __align__(8) uint64_t rfull[GM_MAX_RAW], rempty[GM_MAX_RAW];
   __shared__ __align__(8) uint64_t afull[GM_MAX_ST], bfull[GM_MAX_ST], sempty[GM_MAX_ST];
+  __shared__ __align__(8) uint64_t pfull[2], pempty[2];
   __shared__ __align__(8) uint64_t accbar;
   __shared__ uint32_t tmem_base;
   __shared__ int last_raw[GM_MAX_RAW], last_b[GM_MAX_ST];
@@ -143,6 +153,10 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
       mbar_init(&bfull[s], 1);
       mbar_init(&sempty[s], 1);
       last_b[s] = -1;
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&pfull[b], 1);
+      mbar_init(&pempty[b], GM_DR_WARPS);
     }
     mbar_init(&accbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -189,10 +203,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
     // ================= MMA issuer
     if (lane == 0) {
       for (int k = 0; k < K; k++) {
+        // chunk c accumulates into partial buffer c & 1 (TMEM columns (1 + b) acc_cols ..)
+        const int c = k / GM_CHUNK, b = c & 1;
+        const bool first = k % GM_CHUNK == 0, last = k % GM_CHUNK == GM_CHUNK - 1 || k == K - 1;
+        if (first && c >= 2 && !mbar_wait(&pempty[b], ((c >> 1) - 1) & 1, &abort_flag)) break;
         const int s = k % a.stages;
         const uint32_t ph = (k / a.stages) & 1;
         if (!mbar_wait(&afull[s], ph, &abort_flag) || !mbar_wait(&bfull[s], ph, &abort_flag)) break;
         tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(1 + b) * a.acc_cols;
         const uint32_t st = sbase + (uint32_t)s * a.stage_bytes;
         const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + GM_A_BYTES);
         const uint64_t bhi = sw128_desc(st + 2 * GM_A_BYTES), blo = sw128_desc(st + 2 * GM_A_BYTES + bbytes / 2);
@@ -200,18 +219,74 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
         for (int j = 0; j < 4; j++) {
           // a K16 step is 32 bytes further along the swizzled rows (descriptor units of 16 bytes)
           const uint64_t dj = (uint64_t)(2 * j);
-          umma_f16(tmem, ahi + dj, bhi + dj, a.idesc, (k | j) != 0);
-          umma_f16(tmem, ahi + dj, blo + dj, a.idesc, 1u);
-          umma_f16(tmem, alo + dj, bhi + dj, a.idesc, 1u);
+          umma_f16(d, ahi + dj, bhi + dj, a.idesc, !(first && j == 0));
+          umma_f16(d, ahi + dj, blo + dj, a.idesc, 1u);
+          umma_f16(d, alo + dj, bhi + dj, a.idesc, 1u);
         }
         umma_commit(&sempty[s]);  // the stage is free once these MMAs have read it
+        if (last) umma_commit(&pfull[b]);  // the chunk's partial is complete
       }
       // completion of every MMA issued above (also after giving up, so the
       // TMEM is only freed when nothing writes it any more)
       umma_commit(&accbar);
     }
+  } else if (warp >= 7) {
+    // ================= drain (warps 7..10): TMEM lanes 32 (warp % 4) .. + 31 = rows of the M tile
+    const int quarter = warp & 3;
+    const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    const int NC = (K + GM_CHUNK - 1) / GM_CHUNK;
+    for (int c = 0; c < NC; c++) {
+      const int b = c & 1;
+      if (!__all_sync(0xffffffffu, mbar_wait(&pfull[b], (c >> 1) & 1, &abort_flag))) break;
+      tc_fence_after();
+      const uint32_t pb = tmem + lanes + (uint32_t)(1 + b) * a.acc_cols, sb = tmem + lanes;
+      if (c == NC - 1) {
+        // ---- epilogue: y = (running sum + last partial) 2^-e per token
+        pdl_wait();  // y belongs to earlier kernels
+        const int row = mt * GM_BM + quarter * 32 + lane;
+        for (int c0 = 0; c0 < a.NT; c0 += 16) {
+          uint32_t v[16], u[16];
+          tmem_ld16(pb + (uint32_t)c0, v);
+          if (c > 0) tmem_ld16(sb + (uint32_t)c0, u);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; j++) {
+            const int n = nt * a.NT + c0 + j;
+            const bool tok = n < a.T;
+            const float acc = c > 0 ? __uint_as_float(u[j]) + __uint_as_float(v[j]) : __uint_as_float(v[j]);
+            const float val = acc * (tok ? a.xscale[n] : 0.f);
+            if (a.mode == EPI_SWIGLU) {
+              const float up = __shfl_xor_sync(0xffffffffu, val, 1);
+              if (tok && !(row & 1) && row + 1 < a.rows)
+                a.y[(size_t)n * a.ldy + (row >> 1)] = (val / (1.0f + expf(-val))) * up;
+            } else if (tok && row < a.rows) {
+              float* py = a.y + (size_t)n * a.ldy + row;
+              *py = a.mode == EPI_RESID ? *py + val : val;
+            }
+          }
+        }
+        break;
+      }
+      // running sum += this chunk's partial (the first chunk's partial starts it)
+      for (int c0 = 0; c0 < a.NT; c0 += 16) {
+        uint32_t v[16], u[16];
+        tmem_ld16(pb + (uint32_t)c0, v);
+        if (c > 0) tmem_ld16(sb + (uint32_t)c0, u);
+        tmem_ld_wait();
+        if (c > 0) {
+#pragma unroll
+          for (int j = 0; j < 16; j++) v[j] = __float_as_uint(__uint_as_float(u[j]) + __uint_as_float(v[j]));
+        }
+        tmem_st16(sb + (uint32_t)c0, v);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&pempty[b]);  // the partial buffer may be overwritten
+    }
+    tc_fence_before();
   } else {
-    // ================= dequant (warps 2..5), then the epilogue
+    // ================= dequant (warps 2..5)
     const int dw = warp - 2, g = lane >> 2, c = lane & 3;
     const uint32_t off2 = KIND == MK_Q4 ? 0x64086408u : 0x64806480u;  // fp16 (1024 + bias) twice
     for (int k = 0; k < K; k++) {
@@ -279,34 +354,6 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
       __syncwarp();
       if (lane == 0) mbar_arrive(&afull[s]);
     }
-    // ---- epilogue: this warp reads TMEM lanes 32 (warp % 4) .. + 31 = rows of the M tile
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(&accbar, 0, &abort_flag)) && !abort_flag;
-    tc_fence_after();
-    if (ok) {
-      pdl_wait();  // y belongs to earlier kernels
-      const int quarter = warp & 3;
-      const int row = mt * GM_BM + quarter * 32 + lane;
-      for (int c0 = 0; c0 < a.NT; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int j = 0; j < 16; j++) {
-          const int n = nt * a.NT + c0 + j;
-          const bool tok = n < a.T;
-          const float val = __uint_as_float(v[j]) * (tok ? a.xscale[n] : 0.f);
-          if (a.mode == EPI_SWIGLU) {
-            const float up = __shfl_xor_sync(0xffffffffu, val, 1);
-            if (tok && !(row & 1) && row + 1 < a.rows)
-              a.y[(size_t)n * a.ldy + (row >> 1)] = (val / (1.0f + expf(-val))) * up;
-          } else if (tok && row < a.rows) {
-            float* py = a.y + (size_t)n * a.ldy + row;
-            *py = a.mode == EPI_RESID ? *py + val : val;
-          }
-        }
-      }
-    }
-    tc_fence_before();
   }
 
   __syncthreads();
@@ -330,6 +377,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
   }
   __syncthreads();
   if (warp == 1) {
+    if (lane == 0) {
+      // every MMA has completed (the commit of accbar follows the last one)
+      // before the TMEM is freed, on every path
+      volatile int never = 0;
+      mbar_wait(&accbar, 0, &never);
+    }
     __syncwarp();  // lane 0 rejoins the MMA warp before the warp-wide dealloc
     tc_fence_after();
     tmem_dealloc(tmem, a.tmem_cols);
@@ -463,8 +516,10 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   const int raw_bytes = a.raw_stages * GM_RT * REC;
   a.stages = std::min(GM_MAX_ST, (max_dyn - 1024 - raw_bytes) / (int)a.stage_bytes);
   TN_REQUIRE(a.stages >= 2, TN_EUNSUPPORTED, "gemm: %d bytes of shared memory is too little", max_dyn);
+  // TMEM: running sum at column 0, partial buffers at acc_cols and 2 acc_cols
+  a.acc_cols = (uint32_t)((NT + 31) / 32 * 32);
   a.tmem_cols = 32;
-  while ((int)a.tmem_cols < NT) a.tmem_cols <<= 1;
+  while (a.tmem_cols < 3 * a.acc_cols) a.tmem_cols <<= 1;
   // kind::f16 instruction descriptor: f32 accumulator (bit 4), A and B fp16
   // (formats 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
   a.idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);

@@ -124,7 +124,9 @@ int matvec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, i
            void* gemm_scratch, size_t gemm_scratch_bytes, cudaStream_t s);
 
 // ---- tcgen05 dequant-GEMM (tn_gemm.cu) for steps of many tokens
-constexpr int kGemmMinTokens = 3;
+// (below this the decode matvec, two tokens per launch, streams the weights
+// faster than the GEMM dequantises them: measured crossover near 14 tokens)
+constexpr int kGemmMinTokens = 16;
 bool gemm_ok(const Matrix& m, int T);
 // N tiling of T tokens: ntiles tiles of NT tokens (NT a multiple of 16, <= 128)
 void gemm_tiling(int T, int* NT, int* ntiles);

@@ -1,4 +1,4 @@
-"""The tcgen05 dequant-GEMM (steps of 3 or more tokens) against the oracle,
+"""The tcgen05 dequant-GEMM (steps of 16 or more tokens) against the oracle,
 through the C ABI (tn_matrix_matvec routes those token counts to it).
 
 Each token row of the product is compared with the oracle's matvec of the
@@ -54,9 +54,10 @@ def _run(pkg, ref, torch, quant, rows, cols, T, seed, scale=1.0, check_every=1):
 @pytest.mark.parametrize("quant,rows,cols,T", [
     ("q4_0", 128, 64, 16),     # one CTA, one K slice
     ("q8_0", 128, 64, 16),
-    ("q4_0", 40, 128, 5),      # a partial M tile, a partial N tile
-    ("q8_0", 24, 192, 3),
+    ("q4_0", 40, 128, 21),     # a partial M tile, a partial N tile
+    ("q8_0", 24, 192, 17),
     ("q4_0", 300, 4096, 33),   # one N tile of 48 (T rounded up to 16)
+    ("q4_0", 64, 28672, 16),   # the longest K (70B down): 112 chunks of accumulation
     ("q8_0", 1000, 8192, 64),
     ("q4_0", 4096, 4096, 128),
 ])
