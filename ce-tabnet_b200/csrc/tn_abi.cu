@@ -107,6 +107,7 @@ extern "C" int tn_matrix_matvec(const tn_matrix* m, int32_t n_tokens, const floa
       mm->gemm_bytes = 0;
       TN_CHECK_CUDA(cudaMalloc(&mm->gemm_scratch, need));
       mm->gemm_bytes = need;
+      TN_CHECK_CUDA(cudaMemset(mm->gemm_scratch, 0, need));  // the split-K counters start at zero
     }
   }
   return matvec(m->m, n_tokens, d_x, m->m.cols, d_y, m->m.rows, EPI_STORE, m->d_err, mm->gemm_scratch,

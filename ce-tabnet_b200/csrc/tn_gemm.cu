@@ -18,32 +18,40 @@
 // An activation row is scaled by a power of two so its largest magnitude lies
 // in [2^14, 2^15) and split likewise, x_hi = RN_fp16(x 2^e), x_lo =
 // RN_fp16(x 2^e - x_hi) (22 significant bits of x).  Three MMAs per K step
-// accumulate w_hi x_hi + w_hi x_lo + w_lo x_hi in one f32 accumulator; the
-// dropped w_lo x_lo is below 2^-22 of each product.  The result is scaled
-// back by 2^-e per token in the epilogue.
+// accumulate w_hi x_hi + w_hi x_lo + w_lo x_hi; the dropped w_lo x_lo is below
+// 2^-22 of each product.  The tensor core's additions into its f32
+// accumulator do not round to nearest (measured: an error that grows with the
+// number of accumulating MMAs, ~1e-4 of max |y| at K = 28672), so each chunk
+// of GM_CHUNK slices accumulates into one of two partial TMEM buffers
+// (ping-pong) and drain warps add every finished partial into a running f32
+// sum in TMEM with IEEE adds, in chunk order (measured ~1e-6 of max |y|).  The
+// result is scaled back by 2^-e per token in the epilogue.
 //
 // CTA = one 128-row M tile (8 record tiles of the matrix's fragment-ordered
-// layout) x one N tile of NT <= 128 tokens, K in slices of 64 (one block pair):
-//   warp 0       raw-weight producer: the 8 records of each slice (one bulk
-//                copy per record tile; weights do not depend on the previous
-//                kernel, so the first slices stream before the dependency wait)
+// layout) x one N tile of NT <= 128 tokens x one K split, K in slices of 64
+// (one block pair):
+//   warp 0       raw-weight producer: one TMA tensor copy per raw stage moves
+//                the records of 8 tiles x KSL slices (small bulk copies, one
+//                per record, cost ~75 ns each to issue: measured as the bound
+//                of an earlier version); weights do not depend on the previous
+//                kernel, so the first stages stream before the dependency wait
 //   warp 1       TMEM allocator and MMA issuer (one thread): 4 K16 steps x 3
-//                MMAs per slice; tcgen05.commit frees the slice's stage
-//   warps 2..5   dequant: records -> fp16 hi / lo tiles in the 128-byte
-//                swizzled K-major layout the MMA descriptors name
-//   warp 6       activation producer: the slice's x_hi / x_lo tile, written
+//                MMAs per slice; tcgen05.commit frees the slice's stage and,
+//                every GM_CHUNK slices, hands a partial to the drain
+//   warps 2..9   dequant, one record tile (16 rows) each: records -> fp16 hi /
+//                lo tiles in the 128-byte swizzled K-major layout the MMA
+//                descriptors name
+//   warp 10      activation producer: the slice's x_hi / x_lo tile, written
 //                pre-swizzled by k_gemm_prep, in one bulk copy
-//   warps 7..10  drain + epilogue.  The tensor core's additions into its f32
-//                accumulator do not round to nearest (measured: an error that
-//                grows with the number of accumulating MMAs, ~1e-4 of max |y|
-//                at K = 28672).  So each chunk of GM_CHUNK slices accumulates
-//                into one of two partial TMEM buffers (ping-pong), and these
-//                warps add every finished partial into a running f32 sum in
-//                TMEM with IEEE adds (tcgen05.ld / st), in chunk order; the
-//                last chunk's drain is the epilogue (scale, store / residual
-//                add / SwiGLU).
+//   warps 11..14 drain + epilogue (scale, store / residual add / SwiGLU).
+// Matrices with too few M tiles to fill the GPU split K over KS CTAs per
+// tile: each writes its partial to a workspace, and the last to arrive (a
+// counter per tile) sums the partials in split order -- deterministic -- and
+// runs the epilogue.
 // Every wait is bounded; a CTA that gives up drains its copies and MMAs,
 // frees its TMEM and raises the error flag.
+#include <cudaTypedefs.h>
+
 #include "tn_kernels.cuh"
 #include "tn_ptx.cuh"
 
@@ -51,11 +59,14 @@ namespace tn {
 
 constexpr int GM_BM = 128;                     // rows per CTA
 constexpr int GM_RT = GM_BM / 16;              // record tiles per CTA
-constexpr int GM_DQ_WARPS = 4;                 // dequant warps
+constexpr int GM_DQ_WARPS = GM_RT;             // dequant warps, one record tile each
 constexpr int GM_DR_WARPS = 4;                 // drain / epilogue warps
-constexpr int GM_THREADS = 11 * 32;
+constexpr int GM_WB = 2 + GM_DQ_WARPS;         // the activation producer
+constexpr int GM_WD = GM_WB + 1;               // first drain warp
+constexpr int GM_THREADS = (GM_WD + GM_DR_WARPS) * 32;
 constexpr int GM_CHUNK = 4;                    // K slices accumulated by the tensor core before a drain
 constexpr int GM_MAX_ST = 4, GM_MAX_RAW = 4;
+constexpr int GM_SPLIT_TILES = 320;            // most (tile, split) partials of a split-K launch
 constexpr uint32_t GM_A_BYTES = GM_BM * 128;   // one fp16 [128][64] swizzled tile
 
 struct GemmArgs {
@@ -63,11 +74,13 @@ struct GemmArgs {
   int rows, tiles, pairs;
   const uint8_t* xs;    // k_gemm_prep output: [n tile][pair][hi, lo][NT][64] fp16, swizzled
   const float* xscale;  // [T] 2^-e of each token row
-  int T, NT, ntiles;
+  int T, NT, ntiles, ks;
   float* y;
   int ldy, mode;
-  int stages, raw_stages;
+  int stages, raw_stages, ksl;  // A/B stages; raw stages of ksl slices
   uint32_t stage_bytes, tmem_cols, acc_cols, idesc;
+  float* ws;            // split-K partials [tile][split][NT][128]
+  int* cnt;             // split-K arrivals per (M tile, N tile), zero between launches
   int* err;
 };
 
@@ -118,8 +131,15 @@ __device__ __forceinline__ void dq4(uint32_t u, uint32_t d2, uint32_t off2, uint
   lo[1] = hfma2(v1, d2, hi[1] ^ 0x80008000u);
 }
 
+// the pipeline's waits are on its critical path: no suspend-time hint
+#ifndef GM_WAIT
+#define GM_WAIT mbar_wait_fast
+#endif
+
+__device__ __forceinline__ void drain_bar() { asm volatile("bar.sync 1, %0;" ::"n"(GM_DR_WARPS * 32) : "memory"); }
+
 template <int KIND>
-__global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
+__global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const __grid_constant__ CUtensorMap wmap) {
   constexpr int REC = tile_rec_bytes(KIND), AB = tile_a_bytes(KIND);
   extern __shared__ uint8_t gsm_dyn[];
   __shared__ __align__(8) uint64_t rfull[GM_MAX_RAW], rempty[GM_MAX_RAW];
@@ -128,17 +148,21 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
   __shared__ __align__(8) uint64_t accbar;
   __shared__ uint32_t tmem_base;
   __shared__ int last_raw[GM_MAX_RAW], last_b[GM_MAX_ST];
+  __shared__ int split_last;
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // the n tiles of one M tile are neighbours in launch order: they share the raw weights in L2
-  const int nt = (int)(blockIdx.x % a.ntiles), mt = (int)(blockIdx.x / a.ntiles);
+  // launch order: N tiles fastest, then K splits, then M tiles (the CTAs of
+  // one M tile are neighbours and share its raw weights in L2)
+  const int nt = (int)(blockIdx.x % a.ntiles);
+  const int sp = (int)((blockIdx.x / a.ntiles) % a.ks), mt = (int)(blockIdx.x / a.ntiles / a.ks);
   const int t0 = mt * GM_RT, ntl = min(GM_RT, a.tiles - t0);
-  const int K = a.pairs;  // slices
+  const int kb = (int)((int64_t)a.pairs * sp / a.ks), ke = (int)((int64_t)a.pairs * (sp + 1) / a.ks);
+  const int K = ke - kb;  // slices of this split
   const uint32_t sbase = (smem_u32(gsm_dyn) + 1023u) & ~1023u;
   uint8_t* const smem = gsm_dyn + (sbase - smem_u32(gsm_dyn));
   uint8_t* const raw = smem + (size_t)a.stages * a.stage_bytes;
-  const uint32_t raw_stage = GM_RT * REC;
+  const uint32_t raw_stage = (uint32_t)(GM_RT * a.ksl * REC);  // [8 tiles][ksl slices][record]
   const uint32_t bbytes = 2u * (uint32_t)a.NT * 128u;
 
   if (tid == 0) {
@@ -168,49 +192,57 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
   pdl_launch_dependents();
   const uint32_t tmem = tmem_base;
 
+  // The producer and MMA warps run their loops with all 32 lanes converged
+  // (waits on every lane, one lane issues); a lone lane whose warp-mates wait
+  // at the CTA barrier issues far slower (measured ~1 us per K slice).
   if (warp == 0) {
-    // ================= raw weights: 8 records per slice, raw_stages slices ahead
-    if (lane == 0) {
-      for (int k = 0; k < K; k++) {
-        const int r = k % a.raw_stages;
-        if (k >= a.raw_stages) {
-          if (!mbar_wait(&rempty[r], ((k / a.raw_stages) - 1) & 1, &abort_flag)) break;
-          // the dequant warps read this slot with generic loads; the refill is an
-          // async-proxy write: order the two proxies
-          fence_async_smem();
-        }
-        mbar_expect_tx(&rfull[r], (uint32_t)ntl * REC);
-        for (int j = 0; j < ntl; j++)
-          bulk_g2s(raw + (size_t)r * raw_stage + (size_t)j * REC,
-                   a.data + ((size_t)(t0 + j) * a.pairs + k) * REC, REC, &rfull[r]);
-        last_raw[r] = k;
+    // ================= raw weights: stage q holds slices q ksl .. of the 8 record tiles
+    if (lane == 0) tma_prefetch_map(&wmap);
+    const int NQ = (K + a.ksl - 1) / a.ksl;
+    for (int q = 0; q < NQ; q++) {
+      const int r = q % a.raw_stages;
+      if (q >= a.raw_stages) {
+        if (!__all_sync(0xffffffffu, GM_WAIT(&rempty[r], ((q / a.raw_stages) - 1) & 1, &abort_flag))) break;
+        // the dequant warps read this slot with generic loads; the refill is an
+        // async-proxy write: order the two proxies
+        fence_async_smem();
       }
+      if (lane == 0) {
+        // (the box is whole even where it reaches past the split or the last
+        // tile: tiles past the matrix read as zero, extra slices go unused)
+        mbar_expect_tx(&rfull[r], raw_stage);
+        tma_load_3d(raw + (size_t)r * raw_stage, &wmap, 0, kb + q * a.ksl, t0, &rfull[r]);
+        last_raw[r] = q;
+      }
+      __syncwarp();
     }
-  } else if (warp == 6) {
+  } else if (warp == GM_WB) {
     // ================= activations: the slice's x_hi | x_lo tile, one bulk copy
-    if (lane == 0) {
-      pdl_wait();  // xs is written by the previous kernel
-      for (int k = 0; k < K; k++) {
-        const int s = k % a.stages;
-        if (k >= a.stages && !mbar_wait(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag)) break;
+    pdl_wait();  // xs is written by the previous kernel
+    for (int k = 0; k < K; k++) {
+      const int s = k % a.stages;
+      if (k >= a.stages && !__all_sync(0xffffffffu, GM_WAIT(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag)))
+        break;
+      if (lane == 0) {
         mbar_expect_tx(&bfull[s], bbytes);
         bulk_g2s(smem + (size_t)s * a.stage_bytes + 2 * GM_A_BYTES,
-                 a.xs + ((size_t)nt * a.pairs + k) * bbytes, bbytes, &bfull[s]);
+                 a.xs + ((size_t)nt * a.pairs + kb + k) * bbytes, bbytes, &bfull[s]);
         last_b[s] = k;
       }
+      __syncwarp();
     }
   } else if (warp == 1) {
     // ================= MMA issuer
-    if (lane == 0) {
-      for (int k = 0; k < K; k++) {
-        // chunk c accumulates into partial buffer c & 1 (TMEM columns (1 + b) acc_cols ..)
-        const int c = k / GM_CHUNK, b = c & 1;
-        const bool first = k % GM_CHUNK == 0, last = k % GM_CHUNK == GM_CHUNK - 1 || k == K - 1;
-        if (first && c >= 2 && !mbar_wait(&pempty[b], ((c >> 1) - 1) & 1, &abort_flag)) break;
-        const int s = k % a.stages;
-        const uint32_t ph = (k / a.stages) & 1;
-        if (!mbar_wait(&afull[s], ph, &abort_flag) || !mbar_wait(&bfull[s], ph, &abort_flag)) break;
-        tc_fence_after();
+    for (int k = 0; k < K; k++) {
+      // chunk c accumulates into partial buffer c & 1 (TMEM columns (1 + b) acc_cols ..)
+      const int c = k / GM_CHUNK, b = c & 1;
+      const bool first = k % GM_CHUNK == 0, last = k % GM_CHUNK == GM_CHUNK - 1 || k == K - 1;
+      if (first && c >= 2 && !__all_sync(0xffffffffu, GM_WAIT(&pempty[b], ((c >> 1) - 1) & 1, &abort_flag))) break;
+      const int s = k % a.stages;
+      const uint32_t ph = (k / a.stages) & 1;
+      if (!__all_sync(0xffffffffu, GM_WAIT(&afull[s], ph, &abort_flag) && GM_WAIT(&bfull[s], ph, &abort_flag))) break;
+      tc_fence_after();
+      if (lane == 0) {
         const uint32_t d = tmem + (uint32_t)(1 + b) * a.acc_cols;
         const uint32_t st = sbase + (uint32_t)s * a.stage_bytes;
         const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + GM_A_BYTES);
@@ -226,48 +258,39 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
         umma_commit(&sempty[s]);  // the stage is free once these MMAs have read it
         if (last) umma_commit(&pfull[b]);  // the chunk's partial is complete
       }
-      // completion of every MMA issued above (also after giving up, so the
-      // TMEM is only freed when nothing writes it any more)
-      umma_commit(&accbar);
+      __syncwarp();
     }
-  } else if (warp >= 7) {
-    // ================= drain (warps 7..10): TMEM lanes 32 (warp % 4) .. + 31 = rows of the M tile
+    // completion of every MMA issued above (also after giving up, so the
+    // TMEM is only freed when nothing writes it any more)
+    if (lane == 0) umma_commit(&accbar);
+    __syncwarp();
+  } else if (warp >= GM_WD) {
+    // ================= drain: TMEM lanes 32 (warp % 4) .. + 31 = rows of the M tile
     const int quarter = warp & 3;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    const int rl = quarter * 32 + lane, row = mt * GM_BM + rl;  // M-tile row, matrix row
     const int NC = (K + GM_CHUNK - 1) / GM_CHUNK;
+    const size_t tile = (size_t)mt * a.ntiles + nt;
+    float* const wsp = a.ws + (tile * a.ks + sp) * (size_t)a.NT * GM_BM;  // this split's [NT][128] partial
+    // scale, then store / residual add / SwiGLU one value of (row, token n)
+    auto emit = [&](int n, float acc) {
+      const bool tok = n < a.T;
+      const float val = acc * (tok ? a.xscale[n] : 0.f);
+      if (a.mode == EPI_SWIGLU) {
+        const float up = __shfl_xor_sync(0xffffffffu, val, 1);
+        if (tok && !(row & 1) && row + 1 < a.rows) a.y[(size_t)n * a.ldy + (row >> 1)] = (val / (1.0f + expf(-val))) * up;
+      } else if (tok && row < a.rows) {
+        float* py = a.y + (size_t)n * a.ldy + row;
+        *py = a.mode == EPI_RESID ? *py + val : val;
+      }
+    };
+    bool done = false;
     for (int c = 0; c < NC; c++) {
       const int b = c & 1;
-      if (!__all_sync(0xffffffffu, mbar_wait(&pfull[b], (c >> 1) & 1, &abort_flag))) break;
+      if (!__all_sync(0xffffffffu, GM_WAIT(&pfull[b], (c >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
       const uint32_t pb = tmem + lanes + (uint32_t)(1 + b) * a.acc_cols, sb = tmem + lanes;
-      if (c == NC - 1) {
-        // ---- epilogue: y = (running sum + last partial) 2^-e per token
-        pdl_wait();  // y belongs to earlier kernels
-        const int row = mt * GM_BM + quarter * 32 + lane;
-        for (int c0 = 0; c0 < a.NT; c0 += 16) {
-          uint32_t v[16], u[16];
-          tmem_ld16(pb + (uint32_t)c0, v);
-          if (c > 0) tmem_ld16(sb + (uint32_t)c0, u);
-          tmem_ld_wait();
-#pragma unroll
-          for (int j = 0; j < 16; j++) {
-            const int n = nt * a.NT + c0 + j;
-            const bool tok = n < a.T;
-            const float acc = c > 0 ? __uint_as_float(u[j]) + __uint_as_float(v[j]) : __uint_as_float(v[j]);
-            const float val = acc * (tok ? a.xscale[n] : 0.f);
-            if (a.mode == EPI_SWIGLU) {
-              const float up = __shfl_xor_sync(0xffffffffu, val, 1);
-              if (tok && !(row & 1) && row + 1 < a.rows)
-                a.y[(size_t)n * a.ldy + (row >> 1)] = (val / (1.0f + expf(-val))) * up;
-            } else if (tok && row < a.rows) {
-              float* py = a.y + (size_t)n * a.ldy + row;
-              *py = a.mode == EPI_RESID ? *py + val : val;
-            }
-          }
-        }
-        break;
-      }
-      // running sum += this chunk's partial (the first chunk's partial starts it)
+      const bool fin = c == NC - 1;
       for (int c0 = 0; c0 < a.NT; c0 += 16) {
         uint32_t v[16], u[16];
         tmem_ld16(pb + (uint32_t)c0, v);
@@ -277,7 +300,20 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
 #pragma unroll
           for (int j = 0; j < 16; j++) v[j] = __float_as_uint(__uint_as_float(u[j]) + __uint_as_float(v[j]));
         }
-        tmem_st16(sb + (uint32_t)c0, v);
+        if (!fin) {
+          tmem_st16(sb + (uint32_t)c0, v);  // running sum of the chunks so far
+        } else if (a.ks == 1) {
+          pdl_wait();  // y belongs to earlier kernels
+#pragma unroll
+          for (int j = 0; j < 16; j++) emit(nt * a.NT + c0 + j, __uint_as_float(v[j]));
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; j++) wsp[(size_t)(c0 + j) * GM_BM + rl] = __uint_as_float(v[j]);
+        }
+      }
+      if (fin) {
+        done = true;
+        break;
       }
       tmem_st_wait();
       tc_fence_before();
@@ -285,31 +321,57 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
       if (lane == 0) mbar_arrive(&pempty[b]);  // the partial buffer may be overwritten
     }
     tc_fence_before();
-  } else {
-    // ================= dequant (warps 2..5)
-    const int dw = warp - 2, g = lane >> 2, c = lane & 3;
-    const uint32_t off2 = KIND == MK_Q4 ? 0x64086408u : 0x64806480u;  // fp16 (1024 + bias) twice
-    for (int k = 0; k < K; k++) {
-      const int r = k % a.raw_stages;
-      if (!__all_sync(0xffffffffu, mbar_wait(&rfull[r], (k / a.raw_stages) & 1, &abort_flag))) break;
-      // this lane's slots of record tiles 2 dw and 2 dw + 1
-      constexpr int WPS = AB / 128;  // 32-bit words per lane slot: 4 (q4) / 8 (q8)
-      uint32_t w[2][WPS], sc[2][2];
-#pragma unroll
-      for (int j = 0; j < 2; j++) {
-        const int tt = 2 * dw + j;
-        const uint8_t* rec = raw + (size_t)r * raw_stage + (size_t)tt * REC;
-#pragma unroll
-        for (int v = 0; v < WPS; v++)
-          w[j][v] = tt < ntl ? reinterpret_cast<const uint32_t*>(rec + lane * (AB / 32))[v] : 0u;
-#pragma unroll
-        for (int q = 0; q < 2; q++) sc[j][q] = tt < ntl ? reinterpret_cast<const uint32_t*>(rec + AB)[2 * g + q] : 0u;
+    if (a.ks > 1) {
+      // every drain warp reaches this barrier (also after giving up)
+      __threadfence();
+      drain_bar();
+      if (tid == GM_WD * 32) {
+        int last = 0;
+        if (done && !abort_flag) last = atom_add_acq_rel(a.cnt + tile, 1) == a.ks - 1;
+        split_last = last;
       }
+      drain_bar();
+      if (split_last) {
+        // the other splits' partials, in split order (deterministic)
+        __threadfence();
+        pdl_wait();
+        for (int n0 = 0; n0 < a.NT; n0++) {
+          float acc = 0.f;
+          for (int q = 0; q < a.ks; q++) acc += ld_relaxed(a.ws + ((tile * a.ks + q) * a.NT + n0) * GM_BM + rl);
+          emit(nt * a.NT + n0, acc);
+        }
+        if (tid == GM_WD * 32) a.cnt[tile] = 0;  // ready for the next launch
+      }
+    }
+  } else {
+    // ================= dequant (warps 2..9): record tile tt of the M tile
+    const int tt = warp - 2, g = lane >> 2, c = lane & 3;
+    const uint32_t off2 = KIND == MK_Q4 ? 0x64086408u : 0x64806480u;  // fp16 (1024 + bias) twice
+    // swizzled offsets of this lane's 8 four-element groups: [q][h][u]
+    uint32_t offs[2][2][2];
+#pragma unroll
+    for (int q = 0; q < 2; q++)
+#pragma unroll
+      for (int h = 0; h < 2; h++)
+#pragma unroll
+        for (int u = 0; u < 2; u++) offs[q][h][u] = sw128_off(tt * 16 + g + 8 * u, 32 * q + 16 * h + 4 * c);
+    const bool have = tt < ntl;
+    for (int k = 0; k < K; k++) {
+      const int q0 = k / a.ksl, i0 = k - q0 * a.ksl, r = q0 % a.raw_stages;
+      if (!__all_sync(0xffffffffu, GM_WAIT(&rfull[r], (q0 / a.raw_stages) & 1, &abort_flag))) break;
+      // this lane's slot of the record: 16 (q4) / 32 (q8) bytes, and its two scale words
+      constexpr int WPS = AB / 128;
+      uint32_t w[WPS], sc[2];
+      const uint8_t* rec = raw + (size_t)r * raw_stage + (size_t)(tt * a.ksl + i0) * REC;
+#pragma unroll
+      for (int v = 0; v < WPS; v++) w[v] = have ? reinterpret_cast<const uint32_t*>(rec + lane * (AB / 32))[v] : 0u;
+#pragma unroll
+      for (int q = 0; q < 2; q++) sc[q] = have ? reinterpret_cast<const uint32_t*>(rec + AB)[2 * g + q] : 0u;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&rempty[r]);
+      if (lane == 0 && (i0 == a.ksl - 1 || k == K - 1)) mbar_arrive(&rempty[r]);  // stage read to the end
       const int s = k % a.stages;
       if (k >= a.stages) {
-        if (!__all_sync(0xffffffffu, mbar_wait(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag))) break;
+        if (!__all_sync(0xffffffffu, GM_WAIT(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag))) break;
         // The tensor core read this stage through the async proxy; the stores
         // below go through the generic proxy.  Without this fence they may land
         // before the MMAs' reads that the commit reported complete (measured:
@@ -318,35 +380,27 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
       }
       const uint32_t st = sbase + (uint32_t)s * a.stage_bytes;
 #pragma unroll
-      for (int j = 0; j < 2; j++) {
-        const int tt = 2 * dw + j;
+      for (int q = 0; q < 2; q++) {
+        // scales of rows g and g + 8 of block 2p + q, each in both fp16 halves
+        const uint32_t dg = __byte_perm(sc[q], 0, 0x1010), dg8 = __byte_perm(sc[q], 0, 0x3232);
 #pragma unroll
-        for (int q = 0; q < 2; q++) {
-          // scales of rows g and g + 8 of block 2p + q, each in both fp16 halves
-          const uint32_t dg = __byte_perm(sc[j][q], 0, 0x1010), dg8 = __byte_perm(sc[j][q], 0, 0x3232);
+        for (int h = 0; h < 2; h++) {
 #pragma unroll
-          for (int h = 0; h < 2; h++) {
-            // elements 16 h + 4 c .. + 3 of block 2p + q = slice columns k0 .. k0 + 3
-            const int k0 = 32 * q + 16 * h + 4 * c;
-#pragma unroll
-            for (int u = 0; u < 2; u++) {
-              uint32_t bytes;
-              if (KIND == MK_Q4) {
-                // q4 word 2h + q: byte i = (s(row g) << 4) | s(row g + 8), s = n ^ 8
-                const uint32_t wd = w[j][2 * h + q];
-                bytes = (u == 0 ? (wd >> 4) : wd) & 0x0F0F0F0Fu;
-                bytes ^= 0x08080808u;  // n = s ^ 8, the unsigned nibble
-              } else {
-                // q8 word 4h + 2q + u: byte i = q8 value of row g + 8u; biased by 128
-                bytes = w[j][4 * h + 2 * q + u] ^ 0x80808080u;
-              }
-              uint32_t hi[2], lo[2];
-              dq4(bytes, u == 0 ? dg : dg8, off2, hi, lo);
-              const int row = tt * 16 + g + 8 * u;
-              const uint32_t off = sw128_off(row, k0);
-              sts64(st + off, hi[0], hi[1]);
-              sts64(st + GM_A_BYTES + off, lo[0], lo[1]);
+          for (int u = 0; u < 2; u++) {
+            // elements 16 h + 4 c .. + 3 of block 2p + q, row g + 8 u of the record tile
+            uint32_t bytes;
+            if (KIND == MK_Q4) {
+              // q4 word 2h + q: byte i = (s(row g) << 4) | s(row g + 8), s = n ^ 8
+              const uint32_t wd = w[2 * h + q];
+              bytes = ((u == 0 ? (wd >> 4) : wd) & 0x0F0F0F0Fu) ^ 0x08080808u;  // n = s ^ 8
+            } else {
+              // q8 word 4h + 2q + u: byte i = q8 value of row g + 8u; biased by 128
+              bytes = w[4 * h + 2 * q + u] ^ 0x80808080u;
             }
+            uint32_t hi[2], lo[2];
+            dq4(bytes, u == 0 ? dg : dg8, off2, hi, lo);
+            sts64(st + offs[q][h][u], hi[0], hi[1]);
+            sts64(st + GM_A_BYTES + offs[q][h][u], lo[0], lo[1]);
           }
         }
       }
@@ -360,19 +414,17 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
   if (tid == 0 && abort_flag) {
     // no copy may still be landing when the CTA exits
     for (int r = 0; r < a.raw_stages; r++) {
-      const int k = last_raw[r];
-      if (k < 0) continue;
+      const int q = last_raw[r];
+      if (q < 0) continue;
       abort_flag = 0;
-      if (!mbar_wait(&rfull[r], (k / a.raw_stages) & 1, &abort_flag)) break;
+      if (!GM_WAIT(&rfull[r], (q / a.raw_stages) & 1, &abort_flag)) break;
     }
     for (int s = 0; s < a.stages; s++) {
       const int k = last_b[s];
       if (k < 0) continue;
       abort_flag = 0;
-      if (!mbar_wait(&bfull[s], (k / a.stages) & 1, &abort_flag)) break;
+      if (!GM_WAIT(&bfull[s], (k / a.stages) & 1, &abort_flag)) break;
     }
-    abort_flag = 0;
-    mbar_wait(&accbar, 0, &abort_flag);  // the MMAs' completion (committed on every path)
     atomicExch(a.err, 1);
   }
   __syncthreads();
@@ -381,7 +433,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a) {
       // every MMA has completed (the commit of accbar follows the last one)
       // before the TMEM is freed, on every path
       volatile int never = 0;
-      mbar_wait(&accbar, 0, &never);
+      GM_WAIT(&accbar, 0, &never);
     }
     __syncwarp();  // lane 0 rejoins the MMA warp before the warp-wide dealloc
     tc_fence_after();
@@ -469,14 +521,71 @@ void gemm_tiling(int T, int* NT, int* ntiles) {
   *NT = ((((T + nt - 1) / nt) + 15) / 16) * 16;
 }
 
-size_t gemm_scratch_bytes(int T, int cols) {
+// scratch layout: prepared activations | per-token scales | split-K partials
+// (at most GM_SPLIT_TILES [NT][128] f32 tiles) | split-K arrival counters
+struct GemmScratch {
+  size_t xs, xscale, ws, cnt, total;
+};
+static GemmScratch gemm_layout(int T, int cols) {
   int NT, nt;
   gemm_tiling(T, &NT, &nt);
+  auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
   const size_t pairs = ((size_t)cols + 63) / 64;
-  return (size_t)nt * pairs * 2 * NT * 128 + (size_t)nt * NT * sizeof(float) + 256;
+  GemmScratch g;
+  g.xs = 0;
+  g.xscale = al((size_t)nt * pairs * 2 * NT * 128);
+  g.ws = g.xscale + al((size_t)nt * NT * sizeof(float));
+  g.cnt = g.ws + al((size_t)GM_SPLIT_TILES * NT * GM_BM * sizeof(float));
+  g.total = g.cnt + al((size_t)GM_SPLIT_TILES * sizeof(int));
+  return g;
 }
 
-bool gemm_ok(const Matrix& m, int T) { return (m.kind == MK_Q4 || m.kind == MK_Q8) && T >= kGemmMinTokens; }
+size_t gemm_scratch_bytes(int T, int cols) { return gemm_layout(T, cols).total; }
+
+size_t gemm_counter_offset(int T, int cols) { return gemm_layout(T, cols).cnt; }
+
+bool gemm_ok(const Matrix& m, int T) {
+  return (m.kind == MK_Q4 || m.kind == MK_Q8) && m.has_wmap && T >= kGemmMinTokens;
+}
+
+// cuTensorMapEncodeTiled from the driver (the runtime is linked statically;
+// the driver API is not linked)
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// The records as a 3-D tensor of 8-byte elements [tiles][pairs][REC / 8]
+// (innermost first: record bytes, pair, tile); a box is one raw stage of
+// 8 tiles x ksl pairs.  Global strides REC and pairs REC are multiples of 16,
+// the base is a cudaMalloc pointer, the inner coordinate is always 0.
+bool gemm_encode_maps(Matrix* m) {
+  auto fn = encode_fn();
+  if (!fn || !(m->kind == MK_Q4 || m->kind == MK_Q8)) return false;
+  const cuuint64_t rec = (cuuint64_t)tile_rec_bytes(m->kind);
+  const cuuint64_t dims[3] = {rec / 8, (cuuint64_t)m->pairs, (cuuint64_t)m->tiles};
+  const cuuint64_t strides[2] = {rec, rec * (cuuint64_t)m->pairs};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  for (int i = 0; i < 3; i++) {
+    const cuuint32_t box[3] = {(cuuint32_t)(rec / 8), (cuuint32_t)(1 << i), (cuuint32_t)GM_RT};
+    if (fn(&m->wmap[i], CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, m->data, dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return false;
+  }
+  return true;
+}
 
 int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, float* y, int ldy, int mode,
          void* scratch, size_t scratch_bytes, int* err, cudaStream_t s) {
@@ -491,9 +600,9 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   TN_REQUIRE((reinterpret_cast<uintptr_t>(scratch) & 255) == 0, TN_EINVAL, "gemm: scratch must be 256-byte aligned");
   int NT, nt;
   gemm_tiling(T, &NT, &nt);
+  const GemmScratch L = gemm_layout(T, m.cols);
   uint8_t* xs = (uint8_t*)scratch;
-  const size_t xs_bytes = (size_t)nt * m.pairs * 2 * NT * 128;
-  float* xscale = (float*)(xs + ((xs_bytes + 255) & ~(size_t)255));
+  float* xscale = (float*)(xs + L.xscale);
   TN_CHECK_CUDA(launch_pdl(k_gemm_prep, dim3(nt * NT), dim3(256), 0, s, x, ldx, rowsel, T, m.cols, m.pairs, NT, xs,
                            xscale));
   const int max_dyn = gemm_max_dyn();
@@ -512,8 +621,16 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   a.ldy = ldy;
   a.mode = mode;
   a.stage_bytes = 2 * GM_A_BYTES + 2u * (uint32_t)NT * 128u;
-  a.raw_stages = m.kind == MK_Q4 ? 4 : 3;
-  const int raw_bytes = a.raw_stages * GM_RT * REC;
+  // raw stages: the largest boxes that leave 3 A/B stages (4 x 2, 2 x 3, 1 x 3 slices)
+  static const int cfg[3][3] = {{2, 4, 2}, {1, 2, 3}, {0, 1, 3}};  // map index, ksl, raw stages
+  int mi = 0;
+  for (int c = 0; c < 3; c++) {
+    mi = cfg[c][0];
+    a.ksl = cfg[c][1];
+    a.raw_stages = cfg[c][2];
+    if ((max_dyn - 1024 - a.raw_stages * GM_RT * a.ksl * REC) / (int)a.stage_bytes >= 3) break;
+  }
+  const int raw_bytes = a.raw_stages * GM_RT * a.ksl * REC;
   a.stages = std::min(GM_MAX_ST, (max_dyn - 1024 - raw_bytes) / (int)a.stage_bytes);
   TN_REQUIRE(a.stages >= 2, TN_EUNSUPPORTED, "gemm: %d bytes of shared memory is too little", max_dyn);
   // TMEM: running sum at column 0, partial buffers at acc_cols and 2 acc_cols
@@ -524,12 +641,27 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   // (formats 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
   a.idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
   a.err = err;
+  // split K when the (M tile, N tile) grid fills at most half the SMs: at most
+  // one wave, at least two accumulation chunks per split, and at most
+  // GM_SPLIT_TILES partials in the workspace
+  const int mtiles = (m.tiles + GM_RT - 1) / GM_RT, base = mtiles * nt, sms = num_sms();
+  // (never past one wave: a CTA's start-up and drain make a second wave dearer
+  // than the longer K range it saves)
+  int ks = 1;
+  if (2 * base <= sms) {
+    ks = sms / base;
+    ks = std::min(ks, std::max(1, m.pairs / (2 * GM_CHUNK)));
+    ks = std::max(1, std::min(ks, GM_SPLIT_TILES / base));
+  }
+  a.ks = ks;
+  a.ws = (float*)(xs + L.ws);
+  a.cnt = (int*)(xs + L.cnt);
   const size_t smem = (size_t)a.stages * a.stage_bytes + raw_bytes + 1024;
-  const int grid = ((m.tiles + GM_RT - 1) / GM_RT) * nt;
+  const int grid = mtiles * ks * nt;
   if (m.kind == MK_Q4)
-    TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q4>, dim3(grid), dim3(GM_THREADS), smem, s, a));
+    TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q4>, dim3(grid), dim3(GM_THREADS), smem, s, a, m.wmap[mi]));
   else
-    TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q8>, dim3(grid), dim3(GM_THREADS), smem, s, a));
+    TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q8>, dim3(grid), dim3(GM_THREADS), smem, s, a, m.wmap[mi]));
   return TN_OK;
 }
 

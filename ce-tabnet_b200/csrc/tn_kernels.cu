@@ -199,6 +199,7 @@ int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
   if (m->kind == MK_Q4 || m->kind == MK_Q8) {
     const int rc = mm_prepare(m);
     if (rc != TN_OK) return rc;
+    m->has_wmap = gemm_encode_maps(m);  // without them the GEMM is not used
     if (m->ws_floats) {
       const size_t wsb = m->ws_floats * sizeof(float);
       TN_CHECK_CUDA(cudaMalloc(&m->ws, wsb));

@@ -1,6 +1,8 @@
 // tn_kernels.cuh -- device data structures and launchers of the stage engine.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the encoder is fetched from the driver at run time)
+
 #include "tn_common.cuh"
 
 namespace tn {
@@ -97,6 +99,10 @@ struct Matrix {
   float* ws = nullptr;
   size_t cnt_ints = 0;
   int* cnt = nullptr;
+  // MK_Q4 / MK_Q8: TMA maps of the records as a [tiles][pairs][record] tensor,
+  // boxes of 8 tiles x 1 / 2 / 4 pairs (wmap[0..2]: the GEMM's raw stages)
+  CUtensorMap wmap[3];
+  bool has_wmap = false;
 };
 
 // bytes per 32-element block of the data plane (row-major kinds)
@@ -105,6 +111,8 @@ __host__ __device__ constexpr int kind_block_bytes(int k) {
 }
 
 int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s);
+// the GEMM's TMA maps of a q4_0 / q8_0 matrix (tn_gemm.cu); false if the driver cannot encode them
+bool gemm_encode_maps(Matrix* m);
 // launch shape of the tensor-core matvec of a q4_0 / q8_0 matrix (at allocation)
 int mm_prepare(Matrix* m);
 // Repack src_rows rows of a packed tensor (device memory, reference layout,
@@ -133,6 +141,9 @@ void gemm_tiling(int T, int* NT, int* ntiles);
 // scratch of a T-token GEMM over `cols` columns: the prepared fp16 hi / lo
 // activation tiles and the per-token scales
 size_t gemm_scratch_bytes(int T, int cols);
+// byte offset of the split-K arrival counters in that scratch: zero them when
+// the scratch is allocated (every launch leaves them at zero)
+size_t gemm_counter_offset(int T, int cols);
 // y = W x (rows of x at rowsel[t] if given) with a STORE / RESID / SWIGLU epilogue
 int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, float* y, int ldy, int mode,
          void* scratch, size_t scratch_bytes, int* err, cudaStream_t s);

@@ -735,6 +735,7 @@ static int forward_impl(tn_stage* st, const tn_fwd_req* reqs, int n, tn_fwd_out*
         matrix_reset_counters(L.down, s);
       }
       matrix_reset_counters(st->lm_head, s);
+      if (st->gemm_ws) TN_CHECK_CUDA(cudaMemsetAsync(st->gemm_ws, 0, st->gemm_ws_bytes, s));
       TN_CHECK_CUDA(cudaStreamSynchronize(s));
       set_error("a kernel's bounded wait on its copy pipeline gave up; the step's outputs are invalid");
       return TN_ETIMEOUT;

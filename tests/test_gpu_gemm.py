@@ -75,6 +75,38 @@ def test_gemm_large(pkg, ref, torch_cuda, quant, rows, cols, T):
     _run(pkg, ref, torch_cuda, quant, rows, cols, T, seed=rows ^ cols ^ T, check_every=max(1, T // 12))
 
 
+@pytest.mark.parametrize("quant,rows,cols,T", [
+    ("q4_0", 4096, 14336, 16),   # 32 M tiles: K split 5 ways
+    ("q4_0", 128, 8192, 16),     # one M tile: K split 16 ways
+    ("q8_0", 1024, 4096, 200),   # 8 M tiles x 2 N tiles, split 8 ways
+])
+def test_gemm_split_k_deterministic(pkg, ref, torch_cuda, quant, rows, cols, T):
+    """Matrices with too few 128-row tiles to fill the GPU split K over
+    several CTAs; the last to arrive sums the partials in split order.  Three
+    launches back to back (no synchronisation between them) give identical
+    bits, and match the oracle."""
+    torch = torch_cuda
+    lib = pkg._lib.load()
+    buf = _synth(pkg, rows, cols, quant, 41)
+    h = C.c_void_p()
+    pkg._lib.check(lib.tn_matrix_create(0, pkg._lib.QUANT[quant], rows, cols, buf.ctypes.data, buf.nbytes, 0,
+                                        C.byref(h)))
+    try:
+        x = np.random.default_rng(42).standard_normal((T, cols)).astype(np.float32)
+        dx = torch.from_numpy(x).cuda()
+        outs = [torch.full((T, rows), float("nan"), dtype=torch.float32, device="cuda") for _ in range(3)]
+        for dy in outs:
+            pkg._lib.check(lib.tn_matrix_matvec(h, T, dx.data_ptr(), dy.data_ptr(), None))
+        torch.cuda.synchronize()
+        got = [o.cpu().numpy() for o in outs]
+        assert np.array_equal(got[0], got[1]) and np.array_equal(got[0], got[2])
+        for t in sorted({0, T // 2, T - 1}):
+            want = ref.matvec(buf, quant, rows, cols, x[t])
+            assert float(np.max(np.abs(got[0][t] - want)) / np.max(np.abs(want))) < MATVEC_TOL
+    finally:
+        lib.tn_matrix_free(h)
+
+
 def test_gemm_activation_range(pkg, ref, torch_cuda):
     """Rows of very different magnitudes (each token row is scaled by its own
     power of two before the fp16 split)."""
