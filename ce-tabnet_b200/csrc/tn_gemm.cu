@@ -3,9 +3,9 @@
 // positions and fused micro-batches.
 //
 // The matvec of web/inference-worker.js:523-527 for T tokens at once,
-// Y[t][r] = sum_k W[r][k] X[t][k], as D[M = rows][N = tokens] = A B^T with
-// A the weights and B the activations, both K-major fp16 in shared memory and
-// D in f32 TMEM columns.
+// Y[t][r] = sum_k W[r][k] X[t][k], as D[M = rows][N = tokens] = A B^T: A the
+// dequantised weights in tensor memory, B the activations K-major fp16 in
+// shared memory, D f32 in tensor memory.
 //
 // Exactness.  A q4_0 weight is (n - 8) d with d an fp16 scale, a q8_0 weight
 // q d: a multiple of the last place of d with at most 14 (q4) / 18 (q8)
@@ -32,15 +32,18 @@
 // (one block pair):
 //   warp 0       raw-weight producer: one TMA tensor copy per raw stage moves
 //                the records of 8 tiles x KSL slices (small bulk copies, one
-//                per record, cost ~75 ns each to issue: measured as the bound
-//                of an earlier version); weights do not depend on the previous
-//                kernel, so the first stages stream before the dependency wait
-//   warp 1       TMEM allocator and MMA issuer (one thread): 4 K16 steps x 3
-//                MMAs per slice; tcgen05.commit frees the slice's stage and,
-//                every GM_CHUNK slices, hands a partial to the drain
-//   warps 2..9   dequant, one record tile (16 rows) each: records -> fp16 hi /
-//                lo tiles in the 128-byte swizzled K-major layout the MMA
-//                descriptors name
+//                per record, cost ~75 ns each to issue); weights do not depend
+//                on the previous kernel, so the first stages stream before the
+//                dependency wait
+//   warp 1       TMEM allocator and MMA issuer (one elected lane): 4 K16 steps x
+//                3 MMAs per slice; tcgen05.commit frees the slice's A and B
+//                stages and, every GM_CHUNK slices, hands a partial to the drain
+//   warps 2..9   dequant: two warps per TMEM lane quarter, one K half each; a
+//                lane dequantises 32 weights of its row and stores their fp16
+//                hi / lo halves into the A stage in tensor memory (tcgen05.st).
+//                Keeping A out of shared memory matters: with A written to and
+//                read from shared memory every slice cost ~1 us whatever the
+//                token count (shared-memory bandwidth)
 //   warp 10      activation producer: the slice's x_hi / x_lo tile, written
 //                pre-swizzled by k_gemm_prep, in one bulk copy
 //   warps 11..14 drain + epilogue (scale, store / residual add / SwiGLU).
@@ -59,15 +62,15 @@ namespace tn {
 
 constexpr int GM_BM = 128;                     // rows per CTA
 constexpr int GM_RT = GM_BM / 16;              // record tiles per CTA
-constexpr int GM_DQ_WARPS = GM_RT;             // dequant warps, one record tile each
+constexpr int GM_DQ_WARPS = 8;                 // dequant warps: 4 lane quarters x 2 K halves
 constexpr int GM_DR_WARPS = 4;                 // drain / epilogue warps
 constexpr int GM_WB = 2 + GM_DQ_WARPS;         // the activation producer
 constexpr int GM_WD = GM_WB + 1;               // first drain warp
 constexpr int GM_THREADS = (GM_WD + GM_DR_WARPS) * 32;
 constexpr int GM_CHUNK = 4;                    // K slices accumulated by the tensor core before a drain
-constexpr int GM_MAX_ST = 4, GM_MAX_RAW = 4;
+constexpr int GM_MAX_SA = 4, GM_MAX_SB = 6, GM_MAX_RAW = 12;
+constexpr int GM_A_COLS = 64;                  // TMEM columns of one A stage: hi 32 | lo 32
 constexpr int GM_SPLIT_TILES = 320;            // most (tile, split) partials of a split-K launch
-constexpr uint32_t GM_A_BYTES = GM_BM * 128;   // one fp16 [128][64] swizzled tile
 
 struct GemmArgs {
   const uint8_t* data;  // fragment-ordered records of the matrix
@@ -77,8 +80,8 @@ struct GemmArgs {
   int T, NT, ntiles, ks;
   float* y;
   int ldy, mode;
-  int stages, raw_stages, ksl;  // A/B stages; raw stages of ksl slices
-  uint32_t stage_bytes, tmem_cols, acc_cols, idesc;
+  int sa, sb, raw_stages, ksl;  // A stages (TMEM), B stages (smem), raw stages of ksl slices
+  uint32_t acc_cols, a_col0, idesc;
   float* ws;            // split-K partials [tile][split][NT][128]
   int* cnt;             // split-K arrivals per (M tile, N tile), zero between launches
   int* err;
@@ -143,11 +146,12 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
   constexpr int REC = tile_rec_bytes(KIND), AB = tile_a_bytes(KIND);
   extern __shared__ uint8_t gsm_dyn[];
   __shared__ __align__(8) uint64_t rfull[GM_MAX_RAW], rempty[GM_MAX_RAW];
-  __shared__ __align__(8) uint64_t afull[GM_MAX_ST], bfull[GM_MAX_ST], sempty[GM_MAX_ST];
+  __shared__ __align__(8) uint64_t afull[GM_MAX_SA], aempty[GM_MAX_SA];
+  __shared__ __align__(8) uint64_t bfull[GM_MAX_SB], bempty[GM_MAX_SB];
   __shared__ __align__(8) uint64_t pfull[2], pempty[2];
   __shared__ __align__(8) uint64_t accbar;
   __shared__ uint32_t tmem_base;
-  __shared__ int last_raw[GM_MAX_RAW], last_b[GM_MAX_ST];
+  __shared__ int last_raw[GM_MAX_RAW], last_b[GM_MAX_SB];
   __shared__ int split_last;
   __shared__ volatile int abort_flag;
 
@@ -156,14 +160,14 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
   // one M tile are neighbours and share its raw weights in L2)
   const int nt = (int)(blockIdx.x % a.ntiles);
   const int sp = (int)((blockIdx.x / a.ntiles) % a.ks), mt = (int)(blockIdx.x / a.ntiles / a.ks);
-  const int t0 = mt * GM_RT, ntl = min(GM_RT, a.tiles - t0);
+  const int t0 = mt * GM_RT;
   const int kb = (int)((int64_t)a.pairs * sp / a.ks), ke = (int)((int64_t)a.pairs * (sp + 1) / a.ks);
   const int K = ke - kb;  // slices of this split
   const uint32_t sbase = (smem_u32(gsm_dyn) + 1023u) & ~1023u;
   uint8_t* const smem = gsm_dyn + (sbase - smem_u32(gsm_dyn));
-  uint8_t* const raw = smem + (size_t)a.stages * a.stage_bytes;
-  const uint32_t raw_stage = (uint32_t)(GM_RT * a.ksl * REC);  // [8 tiles][ksl slices][record]
   const uint32_t bbytes = 2u * (uint32_t)a.NT * 128u;
+  uint8_t* const raw = smem + (size_t)a.sb * bbytes;
+  const uint32_t raw_stage = (uint32_t)(GM_RT * a.ksl * REC);  // [8 tiles][ksl slices][record]
 
   if (tid == 0) {
     abort_flag = 0;
@@ -172,10 +176,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       mbar_init(&rempty[r], GM_DQ_WARPS);
       last_raw[r] = -1;
     }
-    for (int s = 0; s < a.stages; s++) {
+    for (int s = 0; s < a.sa; s++) {
       mbar_init(&afull[s], GM_DQ_WARPS);
+      mbar_init(&aempty[s], 1);
+    }
+    for (int s = 0; s < a.sb; s++) {
       mbar_init(&bfull[s], 1);
-      mbar_init(&sempty[s], 1);
+      mbar_init(&bempty[s], 1);
       last_b[s] = -1;
     }
     for (int b = 0; b < 2; b++) {
@@ -185,7 +192,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
     mbar_init(&accbar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) tmem_alloc(&tmem_base, a.tmem_cols);
+  if (warp == 1) tmem_alloc(&tmem_base, 512);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -193,8 +200,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
   const uint32_t tmem = tmem_base;
 
   // The producer and MMA warps run their loops with all 32 lanes converged
-  // (waits on every lane, one lane issues); a lone lane whose warp-mates wait
-  // at the CTA barrier issues far slower (measured ~1 us per K slice).
+  // (waits on every lane, one lane issues).
   if (warp == 0) {
     // ================= raw weights: stage q holds slices q ksl .. of the 8 record tiles
     if (lane == 0) tma_prefetch_map(&wmap);
@@ -220,13 +226,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
     // ================= activations: the slice's x_hi | x_lo tile, one bulk copy
     pdl_wait();  // xs is written by the previous kernel
     for (int k = 0; k < K; k++) {
-      const int s = k % a.stages;
-      if (k >= a.stages && !__all_sync(0xffffffffu, GM_WAIT(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag)))
-        break;
+      const int s = k % a.sb;
+      if (k >= a.sb && !__all_sync(0xffffffffu, GM_WAIT(&bempty[s], ((k / a.sb) - 1) & 1, &abort_flag))) break;
       if (lane == 0) {
         mbar_expect_tx(&bfull[s], bbytes);
-        bulk_g2s(smem + (size_t)s * a.stage_bytes + 2 * GM_A_BYTES,
-                 a.xs + ((size_t)nt * a.pairs + kb + k) * bbytes, bbytes, &bfull[s]);
+        bulk_g2s(smem + (size_t)s * bbytes, a.xs + ((size_t)nt * a.pairs + kb + k) * bbytes, bbytes, &bfull[s]);
         last_b[s] = k;
       }
       __syncwarp();
@@ -238,24 +242,27 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       const int c = k / GM_CHUNK, b = c & 1;
       const bool first = k % GM_CHUNK == 0, last = k % GM_CHUNK == GM_CHUNK - 1 || k == K - 1;
       if (first && c >= 2 && !__all_sync(0xffffffffu, GM_WAIT(&pempty[b], ((c >> 1) - 1) & 1, &abort_flag))) break;
-      const int s = k % a.stages;
-      const uint32_t ph = (k / a.stages) & 1;
-      if (!__all_sync(0xffffffffu, GM_WAIT(&afull[s], ph, &abort_flag) && GM_WAIT(&bfull[s], ph, &abort_flag))) break;
+      const int sa = k % a.sa, sb = k % a.sb;
+      if (!__all_sync(0xffffffffu, GM_WAIT(&afull[sa], (k / a.sa) & 1, &abort_flag) &&
+                                       GM_WAIT(&bfull[sb], (k / a.sb) & 1, &abort_flag)))
+        break;
       tc_fence_after();
       if (lane == 0) {
         const uint32_t d = tmem + (uint32_t)(1 + b) * a.acc_cols;
-        const uint32_t st = sbase + (uint32_t)s * a.stage_bytes;
-        const uint64_t ahi = sw128_desc(st), alo = sw128_desc(st + GM_A_BYTES);
-        const uint64_t bhi = sw128_desc(st + 2 * GM_A_BYTES), blo = sw128_desc(st + 2 * GM_A_BYTES + bbytes / 2);
+        const uint32_t ahi = tmem + a.a_col0 + (uint32_t)sa * GM_A_COLS, alo = ahi + GM_A_COLS / 2;
+        const uint32_t st = sbase + (uint32_t)sb * bbytes;
+        const uint64_t bhi = sw128_desc(st), blo = sw128_desc(st + bbytes / 2);
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-          // a K16 step is 32 bytes further along the swizzled rows (descriptor units of 16 bytes)
+          // a K16 step: 8 TMEM columns of A, 32 bytes further along B's swizzled rows
           const uint64_t dj = (uint64_t)(2 * j);
-          umma_f16(d, ahi + dj, bhi + dj, a.idesc, !(first && j == 0));
-          umma_f16(d, ahi + dj, blo + dj, a.idesc, 1u);
-          umma_f16(d, alo + dj, bhi + dj, a.idesc, 1u);
+          const uint32_t aj = (uint32_t)(8 * j);
+          umma_f16_ts(d, ahi + aj, bhi + dj, a.idesc, !(first && j == 0));
+          umma_f16_ts(d, ahi + aj, blo + dj, a.idesc, 1u);
+          umma_f16_ts(d, alo + aj, bhi + dj, a.idesc, 1u);
         }
-        umma_commit(&sempty[s]);  // the stage is free once these MMAs have read it
+        umma_commit(&aempty[sa]);  // the stages are free once these MMAs have read them
+        umma_commit(&bempty[sb]);
         if (last) umma_commit(&pfull[b]);  // the chunk's partial is complete
       }
       __syncwarp();
@@ -289,19 +296,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       const int b = c & 1;
       if (!__all_sync(0xffffffffu, GM_WAIT(&pfull[b], (c >> 1) & 1, &abort_flag))) break;
       tc_fence_after();
-      const uint32_t pb = tmem + lanes + (uint32_t)(1 + b) * a.acc_cols, sb = tmem + lanes;
+      const uint32_t pb = tmem + lanes + (uint32_t)(1 + b) * a.acc_cols, sbuf = tmem + lanes;
       const bool fin = c == NC - 1;
       for (int c0 = 0; c0 < a.NT; c0 += 16) {
         uint32_t v[16], u[16];
         tmem_ld16(pb + (uint32_t)c0, v);
-        if (c > 0) tmem_ld16(sb + (uint32_t)c0, u);
+        if (c > 0) tmem_ld16(sbuf + (uint32_t)c0, u);
         tmem_ld_wait();
         if (c > 0) {
 #pragma unroll
           for (int j = 0; j < 16; j++) v[j] = __float_as_uint(__uint_as_float(u[j]) + __uint_as_float(v[j]));
         }
         if (!fin) {
-          tmem_st16(sb + (uint32_t)c0, v);  // running sum of the chunks so far
+          tmem_st16(sbuf + (uint32_t)c0, v);  // running sum of the chunks so far
         } else if (a.ks == 1) {
           pdl_wait();  // y belongs to earlier kernels
 #pragma unroll
@@ -344,69 +351,73 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       }
     }
   } else {
-    // ================= dequant (warps 2..9): record tile tt of the M tile
-    const int tt = warp - 2, g = lane >> 2, c = lane & 3;
+    // ================= dequant (warps 2..9): row quarter * 32 + lane of the M tile, K half kh
+    const int quarter = warp & 3, kh = (warp - 2) >> 2;
+    const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
+    const int m = quarter * 32 + lane;             // M-tile row
+    const int tt = m >> 4, g = m & 7, u = (m >> 3) & 1;  // record tile, row g + 8 u of it
     const uint32_t off2 = KIND == MK_Q4 ? 0x64086408u : 0x64806480u;  // fp16 (1024 + bias) twice
-    // swizzled offsets of this lane's 8 four-element groups: [q][h][u]
-    uint32_t offs[2][2][2];
+    for (int k = 0; k < K; k++) {
+      const int q0 = k / a.ksl, i0 = k - q0 * a.ksl, r = q0 % a.raw_stages;
+      // (a barrier wait costs hundreds of cycles even when the phase is complete:
+      // one per raw stage, not one per slice)
+      if (i0 == 0 && !__all_sync(0xffffffffu, GM_WAIT(&rfull[r], (q0 / a.raw_stages) & 1, &abort_flag))) break;
+      // block 2p + kh of this row: lane slots 4 g + c of the record (c = 0..3), word
+      // 2h + kh (q4) / 4h + 2kh + u (q8) for element half h, and the row's scale;
+      // each slot is read as whole 16-byte vectors
+      const uint8_t* rec = raw + (size_t)r * raw_stage + (size_t)(tt * a.ksl + i0) * REC;
+      uint32_t w[2][4];
 #pragma unroll
-    for (int q = 0; q < 2; q++)
+      for (int c = 0; c < 4; c++) {
+        const uint4* slot = reinterpret_cast<const uint4*>(rec + (4 * g + c) * (AB / 32));
+        if (KIND == MK_Q4) {
+          const uint4 v = slot[0];  // words 0..3 = (h, q) = (0,0) (0,1) (1,0) (1,1)
+          w[0][c] = kh ? v.y : v.x;
+          w[1][c] = kh ? v.w : v.z;
+        } else {
+          const uint4 v0 = slot[0], v1 = slot[1];  // words 4h + 2q + u
+          w[0][c] = kh ? (u ? v0.w : v0.z) : (u ? v0.y : v0.x);
+          w[1][c] = kh ? (u ? v1.w : v1.z) : (u ? v1.y : v1.x);
+        }
+      }
+      const uint32_t sc = reinterpret_cast<const uint32_t*>(rec + AB)[2 * g + kh];
+      __syncwarp();
+      if (lane == 0 && (i0 == a.ksl - 1 || k == K - 1)) mbar_arrive(&rempty[r]);  // stage read to the end
+      const int sa = k % a.sa;
+      if (k >= a.sa) {
+        if (!__all_sync(0xffffffffu, GM_WAIT(&aempty[sa], ((k / a.sa) - 1) & 1, &abort_flag))) break;
+        tc_fence_after();
+      }
+      const uint32_t d2 = __byte_perm(sc, 0, u ? 0x3232 : 0x1010);  // this row's scale, both halves
+      // element e = 16 h + 4 c + i of the block = K column e of this half: fp16
+      // pair (e, e + 1) goes to column e / 2
+      uint32_t hi[16], lo[16];
 #pragma unroll
       for (int h = 0; h < 2; h++)
 #pragma unroll
-        for (int u = 0; u < 2; u++) offs[q][h][u] = sw128_off(tt * 16 + g + 8 * u, 32 * q + 16 * h + 4 * c);
-    const bool have = tt < ntl;
-    for (int k = 0; k < K; k++) {
-      const int q0 = k / a.ksl, i0 = k - q0 * a.ksl, r = q0 % a.raw_stages;
-      if (!__all_sync(0xffffffffu, GM_WAIT(&rfull[r], (q0 / a.raw_stages) & 1, &abort_flag))) break;
-      // this lane's slot of the record: 16 (q4) / 32 (q8) bytes, and its two scale words
-      constexpr int WPS = AB / 128;
-      uint32_t w[WPS], sc[2];
-      const uint8_t* rec = raw + (size_t)r * raw_stage + (size_t)(tt * a.ksl + i0) * REC;
-#pragma unroll
-      for (int v = 0; v < WPS; v++) w[v] = have ? reinterpret_cast<const uint32_t*>(rec + lane * (AB / 32))[v] : 0u;
-#pragma unroll
-      for (int q = 0; q < 2; q++) sc[q] = have ? reinterpret_cast<const uint32_t*>(rec + AB)[2 * g + q] : 0u;
-      __syncwarp();
-      if (lane == 0 && (i0 == a.ksl - 1 || k == K - 1)) mbar_arrive(&rempty[r]);  // stage read to the end
-      const int s = k % a.stages;
-      if (k >= a.stages) {
-        if (!__all_sync(0xffffffffu, GM_WAIT(&sempty[s], ((k / a.stages) - 1) & 1, &abort_flag))) break;
-        // The tensor core read this stage through the async proxy; the stores
-        // below go through the generic proxy.  Without this fence they may land
-        // before the MMAs' reads that the commit reported complete (measured:
-        // the first record tile each warp rewrites, in the last K16 steps).
-        fence_async_smem();
-      }
-      const uint32_t st = sbase + (uint32_t)s * a.stage_bytes;
-#pragma unroll
-      for (int q = 0; q < 2; q++) {
-        // scales of rows g and g + 8 of block 2p + q, each in both fp16 halves
-        const uint32_t dg = __byte_perm(sc[q], 0, 0x1010), dg8 = __byte_perm(sc[q], 0, 0x3232);
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-#pragma unroll
-          for (int u = 0; u < 2; u++) {
-            // elements 16 h + 4 c .. + 3 of block 2p + q, row g + 8 u of the record tile
-            uint32_t bytes;
-            if (KIND == MK_Q4) {
-              // q4 word 2h + q: byte i = (s(row g) << 4) | s(row g + 8), s = n ^ 8
-              const uint32_t wd = w[2 * h + q];
-              bytes = ((u == 0 ? (wd >> 4) : wd) & 0x0F0F0F0Fu) ^ 0x08080808u;  // n = s ^ 8
-            } else {
-              // q8 word 4h + 2q + u: byte i = q8 value of row g + 8u; biased by 128
-              bytes = w[4 * h + 2 * q + u] ^ 0x80808080u;
-            }
-            uint32_t hi[2], lo[2];
-            dq4(bytes, u == 0 ? dg : dg8, off2, hi, lo);
-            sts64(st + offs[q][h][u], hi[0], hi[1]);
-            sts64(st + GM_A_BYTES + offs[q][h][u], lo[0], lo[1]);
+        for (int c = 0; c < 4; c++) {
+          uint32_t bytes;
+          if (KIND == MK_Q4) {
+            // byte i = (s(row g) << 4) | s(row g + 8), s = n ^ 8
+            bytes = (((u == 0) ? (w[h][c] >> 4) : w[h][c]) & 0x0F0F0F0Fu) ^ 0x08080808u;
+          } else {
+            bytes = w[h][c] ^ 0x80808080u;  // q8 value of row g + 8 u, biased by 128
           }
+          uint32_t ph[2], pl[2];
+          dq4(bytes, d2, off2, ph, pl);
+          const int col = 8 * h + 2 * c;
+          hi[col] = ph[0];
+          hi[col + 1] = ph[1];
+          lo[col] = pl[0];
+          lo[col + 1] = pl[1];
         }
-      }
-      fence_async_smem();
+      const uint32_t abase = tmem + lanes + a.a_col0 + (uint32_t)sa * GM_A_COLS + (uint32_t)(16 * kh);
+      tmem_st16(abase, hi);
+      tmem_st16(abase + GM_A_COLS / 2, lo);
+      tmem_st_wait();
+      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&afull[s]);
+      if (lane == 0) mbar_arrive(&afull[sa]);
     }
   }
 
@@ -419,11 +430,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       abort_flag = 0;
       if (!GM_WAIT(&rfull[r], (q / a.raw_stages) & 1, &abort_flag)) break;
     }
-    for (int s = 0; s < a.stages; s++) {
+    for (int s = 0; s < a.sb; s++) {
       const int k = last_b[s];
       if (k < 0) continue;
       abort_flag = 0;
-      if (!GM_WAIT(&bfull[s], (k / a.stages) & 1, &abort_flag)) break;
+      if (!GM_WAIT(&bfull[s], (k / a.sb) & 1, &abort_flag)) break;
     }
     atomicExch(a.err, 1);
   }
@@ -437,7 +448,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
     }
     __syncwarp();  // lane 0 rejoins the MMA warp before the warp-wide dealloc
     tc_fence_after();
-    tmem_dealloc(tmem, a.tmem_cols);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -620,23 +631,23 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   a.y = y;
   a.ldy = ldy;
   a.mode = mode;
-  a.stage_bytes = 2 * GM_A_BYTES + 2u * (uint32_t)NT * 128u;
-  // raw stages: the largest boxes that leave 3 A/B stages (4 x 2, 2 x 3, 1 x 3 slices)
-  static const int cfg[3][3] = {{2, 4, 2}, {1, 2, 3}, {0, 1, 3}};  // map index, ksl, raw stages
-  int mi = 0;
-  for (int c = 0; c < 3; c++) {
-    mi = cfg[c][0];
-    a.ksl = cfg[c][1];
-    a.raw_stages = cfg[c][2];
-    if ((max_dyn - 1024 - a.raw_stages * GM_RT * a.ksl * REC) / (int)a.stage_bytes >= 3) break;
-  }
-  const int raw_bytes = a.raw_stages * GM_RT * a.ksl * REC;
-  a.stages = std::min(GM_MAX_ST, (max_dyn - 1024 - raw_bytes) / (int)a.stage_bytes);
-  TN_REQUIRE(a.stages >= 2, TN_EUNSUPPORTED, "gemm: %d bytes of shared memory is too little", max_dyn);
-  // TMEM: running sum at column 0, partial buffers at acc_cols and 2 acc_cols
+  // TMEM: running sum at column 0, partial buffers at acc_cols and 2 acc_cols,
+  // then the A stages (64 columns each) in the rest of the 512 columns
   a.acc_cols = (uint32_t)((NT + 31) / 32 * 32);
-  a.tmem_cols = 32;
-  while (a.tmem_cols < 3 * a.acc_cols) a.tmem_cols <<= 1;
+  a.a_col0 = 3 * a.acc_cols;
+  a.sa = std::min(GM_MAX_SA, (int)((512 - a.a_col0) / GM_A_COLS));
+  TN_REQUIRE(a.sa >= 2, TN_EUNSUPPORTED, "gemm: no room for two A stages in tensor memory");
+  // shared memory: a few B stages, then as many raw stages (~18 KB boxes) as fit
+  // (a copy's loaded latency is several microseconds: the ring must be deep)
+  const int bb = 2 * NT * 128;
+  const int mi = 2;  // boxes of 4 slices (one stage wait per 4 slices)
+  a.ksl = 1 << mi;
+  a.sb = NT <= 64 ? 4 : 3;
+  const int raw_stage_b = GM_RT * a.ksl * REC;
+  a.raw_stages = std::min(GM_MAX_RAW, (max_dyn - 1024 - a.sb * bb) / raw_stage_b);
+  const int raw_bytes = a.raw_stages * raw_stage_b;
+  TN_REQUIRE(a.raw_stages >= 2, TN_EUNSUPPORTED, "gemm: no room for two raw stages in shared memory");
+  TN_REQUIRE(a.sb >= 2, TN_EUNSUPPORTED, "gemm: %d bytes of shared memory is too little", max_dyn);
   // kind::f16 instruction descriptor: f32 accumulator (bit 4), A and B fp16
   // (formats 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
   a.idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
@@ -656,7 +667,7 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   a.ks = ks;
   a.ws = (float*)(xs + L.ws);
   a.cnt = (int*)(xs + L.cnt);
-  const size_t smem = (size_t)a.stages * a.stage_bytes + raw_bytes + 1024;
+  const size_t smem = (size_t)a.sb * bb + raw_bytes + 1024;
   const int grid = mtiles * ks * nt;
   if (m.kind == MK_Q4)
     TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q4>, dim3(grid), dim3(GM_THREADS), smem, s, a, m.wmap[mi]));
