@@ -170,7 +170,7 @@ __global__ void k_repack_plain(const uint8_t* __restrict__ src, int quant, int s
 
 static void mv_prepare(Matrix* m);
 
-int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
+int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s, bool own_ws) {
   TN_REQUIRE(rows > 0 && cols > 0, TN_EINVAL, "matrix: bad shape %d x %d", rows, cols);
   TN_REQUIRE(quant_bytes(1, src_quant) != 0, TN_EUNSUPPORTED, "unsupported quant %d", src_quant);
   m->rows = rows;
@@ -200,7 +200,8 @@ int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s) {
     const int rc = mm_prepare(m);
     if (rc != TN_OK) return rc;
     m->has_wmap = gemm_encode_maps(m);  // without them the GEMM is not used
-    if (m->ws_floats) {
+    m->ws_owned = own_ws;
+    if (m->ws_floats && own_ws) {
       const size_t wsb = m->ws_floats * sizeof(float);
       TN_CHECK_CUDA(cudaMalloc(&m->ws, wsb));
       TN_CHECK_CUDA(cudaMemsetAsync(m->ws, 0, wsb, s));
@@ -240,8 +241,10 @@ int matrix_repack(Matrix* m, const uint8_t* d_src, int src_quant, int src_rows, 
 
 void matrix_free(Matrix* m) {
   if (m->data) cudaFree(m->data);
-  if (m->ws) cudaFree(m->ws);
-  if (m->cnt) cudaFree(m->cnt);
+  if (m->ws_owned) {
+    if (m->ws) cudaFree(m->ws);
+    if (m->cnt) cudaFree(m->cnt);
+  }
   m->data = nullptr;
   m->ws = nullptr;
   m->cnt = nullptr;

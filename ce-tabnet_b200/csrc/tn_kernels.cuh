@@ -74,7 +74,7 @@ inline cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 bl
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
-// Launch shape of the tensor-core matvec for one token count (1 or 2): K is
+// Launch shape of the tensor-core matvec for one token count (1, 2 or 4): K is
 // cut into ks chunks of ckp block pairs (a chunk's activation digits fill one
 // shared-memory table), a chunk into nsc sub-chunks of scp pairs (one
 // shared-memory stage each).
@@ -92,13 +92,17 @@ struct Matrix {
   uint8_t* data = nullptr;
   size_t bytes = 0;
   int occ[2] = {0, 0};       // resident CTAs per SM of the CUDA-core matvec (MK_F16 / MK_F32)
-  MmShape mm[2];             // tensor-core matvec (MK_Q4 / MK_Q8), 1 and 2 tokens
-  // cross-CTA partial sums [chunk][tile][part 0 / 1][32] and per-tile arrival
-  // counters (zero between launches: the CTA that completes a tile resets it)
+  MmShape mm[3];             // tensor-core matvec (MK_Q4 / MK_Q8), 1, 2 and 4 token columns
+  // cross-CTA partial sums [chunk][tile][part 0 / 1][32 x token pairs] and
+  // per-tile arrival counters (zero between launches: the CTA that completes
+  // a tile resets them).  Matrices whose launches are ordered on one stream
+  // may share one pair of buffers (ws_owned false): every access follows the
+  // wait for the previous kernel.
   size_t ws_floats = 0;
   float* ws = nullptr;
   size_t cnt_ints = 0;
   int* cnt = nullptr;
+  bool ws_owned = true;
   // MK_Q4 / MK_Q8: TMA maps of the records as a [tiles][pairs][record] tensor,
   // boxes of 8 tiles x 1 / 2 / 4 pairs (wmap[0..2]: the GEMM's raw stages)
   CUtensorMap wmap[3];
@@ -110,7 +114,9 @@ __host__ __device__ constexpr int kind_block_bytes(int k) {
   return k == MK_Q4 ? 16 : (k == MK_Q8 ? 32 : (k == MK_F16 ? 64 : 128));
 }
 
-int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s);
+// own_ws false: ws / cnt are left for the caller to point at shared buffers
+// of at least ws_floats / cnt_ints elements (zeroed)
+int matrix_alloc(Matrix* m, int src_quant, int rows, int cols, cudaStream_t s, bool own_ws = true);
 // the GEMM's TMA maps of a q4_0 / q8_0 matrix (tn_gemm.cu); false if the driver cannot encode them
 bool gemm_encode_maps(Matrix* m);
 // launch shape of the tensor-core matvec of a q4_0 / q8_0 matrix (at allocation)

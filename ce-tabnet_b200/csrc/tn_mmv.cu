@@ -15,8 +15,10 @@
 //     largest magnitude lies in [2^26, 2^27), rounded to the integer X and
 //     split into four base-128 digits X = d0 + 2^7 d1 + 2^14 d2 + 2^21 d3
 //     (d0..d2 in [0, 127], d3 signed), one B column per digit.  With one
-//     token the 8 columns are (block parity, digit); with two tokens each
-//     block parity gets its own instruction and the columns are (token, digit).
+//     token the 8 columns are (block parity, digit); with 2 or 4 tokens
+//     each block parity and each pair of tokens gets its own instruction
+//     (the other parity's half of K multiplies zeros) and the columns are
+//     (token, digit).
 //   C starts at the bit pattern of 1.5 * 2^23: every per-block column sum
 //   |S| < 2^19, so the s32 result read as f32 is exactly 1.5 * 2^23 + S and
 //   one FADD recovers S without an integer->float conversion.  S times the
@@ -25,23 +27,23 @@
 //   tile is done.  The only rounding against an f32 dot product is that of
 //   x to 27 bits relative to its chunk maximum.
 //
-// Work split: K is cut into chunks of up to 8192 elements (one token; 4096
-// for two) whose activation digits fill a 33 KB shared-memory table; a chunk
-// of a 16-row tile into sub-chunks of up to 32 (q4) / 16 (q8) block pairs,
-// one ring stage each.  Every CTA works on one chunk (one digit table, built
-// once) and streams a contiguous run of its (tile, sub-chunk) units, so a
-// tile's chunk is usually summed inside one CTA.  A producer warp streams
+// Work split: K is cut into chunks of up to 8192 / TT elements (TT = 1, 2 or
+// 4 token columns) whose activation digits fill a 33 KB shared-memory table;
+// a chunk of a 16-row tile into sub-chunks of up to 32 (q4) / 16 (q8) block
+// pairs, one ring stage each.  Every CTA works on one chunk (one digit table,
+// built once) and streams a contiguous run of its (tile, sub-chunk) units, so
+// a tile's chunk is usually summed inside one CTA.  A producer warp streams
 // each unit's records (one contiguous bulk copy) into the ring with a decoded
 // descriptor of the unit (full / empty mbarriers; a stage is handed back as
 // soon as the consumers hold its operands in registers); eight consumer warps
 // split every unit's pairs, accumulate a tile's chunk in registers and hand
-// the per-warp row sums to an epilogue warp through mbarrier-guarded buffers.  The epilogue warp sums the
-// eight warps in fixed order; a tile whose chunk is whole in this CTA and the
-// only chunk is final at once (fused epilogue: store / residual add / SwiGLU /
-// RoPE + KV append); other pieces go to a workspace, arrivals are counted per
-// tile with release-atomics (batched over four pieces), and the arrival that
-// completes a tile sums its pieces in (chunk, part) order -- deterministic --
-// and runs the fused epilogue.
+// the per-warp row sums to an epilogue warp through mbarrier-guarded buffers.
+// The epilogue warp sums the eight warps in fixed order; a tile whose chunk is
+// whole in this CTA and the only chunk is final at once (fused epilogue:
+// store / residual add / SwiGLU / RoPE + KV append); other pieces go to a
+// workspace, arrivals are counted per tile with release-atomics (batched over
+// four pieces), and the arrival that completes a tile sums its pieces in
+// (chunk, part) order -- deterministic -- and runs the fused epilogue.
 #include <cfloat>
 #include <type_traits>
 
@@ -70,8 +72,10 @@ constexpr int MMV_MAX_SMEM = 200 * 1024;
 constexpr int MMV_CE = 8192;                           // activation elements (x tokens) per K chunk
 constexpr int kMagic = 0x4B400000;                     // bits of 1.5 * 2^23
 constexpr float kMagicF = 12582912.0f;
-// most block pairs per sub-chunk (one ring stage)
-__host__ __device__ constexpr int mmv_sc(int kind) { return kind == MK_Q4 ? 32 : 16; }
+// most block pairs per sub-chunk (one ring stage), at most a chunk
+__host__ __device__ constexpr int mmv_sc(int kind, int tt) {
+  return (kind == MK_Q4 ? 32 : 16) < MMV_CE / tt / 64 ? (kind == MK_Q4 ? 32 : 16) : MMV_CE / tt / 64;
+}
 
 struct MmvArgs {
   const uint8_t* data;
@@ -136,21 +140,30 @@ __host__ __device__ __forceinline__ int mmv_pool0(int nsu, int gk, int nsc) {
   const int p = (gk * (q - q / 4) + nsc - 1) / nsc * nsc;  // a tile boundary
   return p < nsu ? p : nsu;
 }
+// bytes of the per-warp row-sum buffers at the start of dynamic shared memory
+__host__ __device__ constexpr int mmv_red_bytes(int tt) { return (MMV_NB * MMV_NW * 16 * tt * 4 + 127) / 128 * 128; }
 constexpr int kPieceEnd = 1 << 16;  // unit descriptor flag (with the sub-chunk): the last unit of a piece
 
 template <int KIND, int TT>
 __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
   constexpr int AB = tile_a_bytes(KIND), REC = tile_rec_bytes(KIND);
-  constexpr int SC = mmv_sc(KIND), PPW = SC / MMV_NW, NV = 16 * TT, NC = MMV_NW * 32;
+  constexpr int SC = mmv_sc(KIND, TT), PPW = SC / MMV_NW, NV = 16 * TT, NC = MMV_NW * 32;
+  // B column groups of 8 columns (tokens 2 cg, 2 cg + 1 x 4 digits; one token:
+  // 2 block parities x 4 digits), and 32-value groups of a tile's row sums
+  // (the epilogue lanes; also the workspace stride of a part)
+  constexpr int NG = TT == 1 ? 1 : TT / 2;
+  static_assert(TT == 1 || TT == 2 || TT == 4, "1, 2 or 4 token columns");
   constexpr int CP = MMV_CE / TT / 64;     // most pairs per chunk
   constexpr int DS = CP * 16 + 8;          // words per digit plane (skewed against bank conflicts)
   constexpr int ZERO = TT * 4 * DS;        // two zero words after the planes
   constexpr unsigned FULL = 0xffffffffu;
-  extern __shared__ __align__(128) uint8_t ring[];
+  // dynamic shared memory: the per-warp row sums, then the ring
+  extern __shared__ __align__(128) uint8_t dyn_smem[];
+  float(*red)[MMV_NW][NV] = reinterpret_cast<float(*)[MMV_NW][NV]>(dyn_smem);  // [MMV_NB][MMV_NW][NV]
+  uint8_t* const ring = dyn_smem + mmv_red_bytes(TT);
   // digit planes of the current chunk: word ((tt*4 + digit)*DS + ((p*2 + q)*4 + c)*2 + h)
   // holds that digit of elements 16h + 4c .. 16h + 4c + 3 of block 2p + q
   __shared__ __align__(16) uint32_t planes[TT * 4 * DS + 2];
-  __shared__ float red[MMV_NB][MMV_NW][NV];
   __shared__ __align__(8) uint64_t full[MMV_MAX_STAGES];
   __shared__ __align__(8) uint64_t empty[MMV_MAX_STAGES];
   __shared__ __align__(8) uint64_t red_full[MMV_NB];
@@ -443,8 +456,9 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     };
 
     // this lane's B columns: one token: g = (block parity sel, digit dg), the
-    // other parity's half of B read from the zero words; two tokens: g =
-    // (token sel, digit dg), one instruction per block parity
+    // other parity's half of B read from the zero words; two or more tokens:
+    // column group cg of g = (token 2 cg + sel, digit dg), one instruction per
+    // block parity and column group
     const int sel = g >> 2, dg = g & 3;
     int boff[2], binc[2];
     if (TT == 1) {
@@ -461,10 +475,12 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     const float wlo = (c & 1) ? 16384.f : 1.f, whi = (c & 1) ? 2097152.f : 128.f;
     setup(kc0);  // the only chunk this CTA works on
     int pi = 0, sc0 = -1;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int k = 0;; k++) {
-      const int st = k % a.stages;
-      if (!__all_sync(FULL, mbar_wait(&full[st], (k / a.stages) & 1, &abort_flag))) break;
+    float acc[NG][4];
+#pragma unroll
+    for (int cg = 0; cg < NG; cg++) acc[cg][0] = acc[cg][1] = acc[cg][2] = acc[cg][3] = 0.f;
+    // ring stage st of the current unit and the parity of its fill
+    for (int st = 0, ph = 0;; (++st == a.stages) ? (st = 0, ph ^= 1) : 0) {
+      if (!__all_sync(FULL, mbar_wait(&full[st], ph, &abort_flag))) break;
       const int4 d = udesc[st];
       if (d.x < 0) break;
       const int t = d.x, sc = d.y & (kPieceEnd - 1), first = d.z, n = d.w;
@@ -475,15 +491,18 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
         // This warp's pairs are slots j * NW + warp of the stage; slots past the
         // sub-chunk's n pairs are skipped (n is the same for the whole warp).
         constexpr int WV = AB / 512;  // 16-byte words per lane per pair
+        constexpr int NQ = TT == 1 ? 1 : 2;
         uint4 wv[PPW][WV];
-        uint32_t sw[PPW][TT];
-        uint2 bq[PPW][2];
+        uint32_t sw[PPW][NQ];  // one token: this lane's block parity; else both
+        uint2 bq[PPW][2];      // up to two tokens: the B words, read here
+        int pcs[PPW];          // more tokens: the pair, B read at the instruction
         const uint8_t* wbase = sbase + (size_t)warp * REC;
 #pragma unroll
         for (int j = 0; j < PPW; j++) {
           if (n < SC && j * MMV_NW + warp >= n) break;
           const uint8_t* rec = wbase + j * MMV_NW * REC;
           const int pc = min(first + j * MMV_NW + warp, CP - 1);  // chunk-local pair
+          pcs[j] = pc;
 #pragma unroll
           for (int v = 0; v < WV; v++) wv[j][v] = *reinterpret_cast<const uint4*>(rec + lane * 16 * WV + 16 * v);
           if (TT == 1) {
@@ -491,10 +510,12 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
           } else {
             const uint2 s2 = *reinterpret_cast<const uint2*>(rec + AB + 8 * g);
             sw[j][0] = s2.x;
-            sw[j][TT - 1] = s2.y;
+            sw[j][NQ - 1] = s2.y;
           }
+          if (TT <= 2) {
 #pragma unroll
-          for (int q = 0; q < 2; q++) bq[j][q] = *reinterpret_cast<const uint2*>(&planes[boff[q] + pc * binc[q]]);
+            for (int q = 0; q < 2; q++) bq[j][q] = *reinterpret_cast<const uint2*>(&planes[boff[q] + pc * binc[q]]);
+          }
         }
         // the operands are in registers: hand the stage back to the producer
         // now, so the ring refills while this warp computes
@@ -528,21 +549,28 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
               A[1][3] = w1.w;
             }
 #pragma unroll
-            for (int q = 0; q < TT; q++) {
-              int D[4] = {kMagic, kMagic, kMagic, kMagic};
-              if (TT == 1) {
-                mma_s8(D, A[0], bq[j][0].x, bq[j][1].x);
-                mma_s8(D, A[1], bq[j][0].y, bq[j][1].y);
-              } else {
-                mma_s8(D, A[0], q == 0 ? bq[j][0].x : 0u, q == 1 ? bq[j][1].x : 0u);
-                mma_s8(D, A[1], q == 0 ? bq[j][0].y : 0u, q == 1 ? bq[j][1].y : 0u);
-              }
+            for (int q = 0; q < NQ; q++) {
               const uint32_t s32 = sw[j][q];
               const float2 d = __half22float2(*reinterpret_cast<const __half2*>(&s32));  // (row g, row g + 8)
-              acc[0] = fmaf(d.x, __int_as_float(D[0]) - kMagicF, acc[0]);
-              acc[1] = fmaf(d.x, __int_as_float(D[1]) - kMagicF, acc[1]);
-              acc[2] = fmaf(d.y, __int_as_float(D[2]) - kMagicF, acc[2]);
-              acc[3] = fmaf(d.y, __int_as_float(D[3]) - kMagicF, acc[3]);
+#pragma unroll
+              for (int cg = 0; cg < NG; cg++) {
+                int D[4] = {kMagic, kMagic, kMagic, kMagic};
+                if (TT == 1) {
+                  mma_s8(D, A[0], bq[j][0].x, bq[j][1].x);
+                  mma_s8(D, A[1], bq[j][0].y, bq[j][1].y);
+                } else {
+                  // block parity q alone: the other half of K multiplies zeros
+                  const uint2 b = TT == 2 ? bq[j][q]
+                                          : *reinterpret_cast<const uint2*>(
+                                                &planes[boff[q] + cg * 8 * DS + pcs[j] * 16]);
+                  mma_s8(D, A[0], q == 0 ? b.x : 0u, q == 1 ? b.x : 0u);
+                  mma_s8(D, A[1], q == 0 ? b.y : 0u, q == 1 ? b.y : 0u);
+                }
+                acc[cg][0] = fmaf(d.x, __int_as_float(D[0]) - kMagicF, acc[cg][0]);
+                acc[cg][1] = fmaf(d.x, __int_as_float(D[1]) - kMagicF, acc[cg][1]);
+                acc[cg][2] = fmaf(d.y, __int_as_float(D[2]) - kMagicF, acc[cg][2]);
+                acc[cg][3] = fmaf(d.y, __int_as_float(D[3]) - kMagicF, acc[cg][3]);
+              }
             }
           }
         };
@@ -552,22 +580,33 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
       if (!(d.y & kPieceEnd)) continue;  // the piece goes on
       // end of a piece: recombine the digit columns, sum the lanes of a row,
       // undo the 2^s scaling, hand the 16 (x TT) row sums to the epilogue
-      float vg = fmaf(acc[1], whi, acc[0] * wlo), vh = fmaf(acc[3], whi, acc[2] * wlo);
-      vg += __shfl_xor_sync(FULL, vg, 1);
-      vh += __shfl_xor_sync(FULL, vh, 1);
-      if (TT == 1) {
-        vg += __shfl_xor_sync(FULL, vg, 2);
-        vh += __shfl_xor_sync(FULL, vh, 2);
+      float vg[NG], vh[NG];
+#pragma unroll
+      for (int cg = 0; cg < NG; cg++) {
+        vg[cg] = fmaf(acc[cg][1], whi, acc[cg][0] * wlo);
+        vh[cg] = fmaf(acc[cg][3], whi, acc[cg][2] * wlo);
+        vg[cg] += __shfl_xor_sync(FULL, vg[cg], 1);
+        vh[cg] += __shfl_xor_sync(FULL, vh[cg], 1);
+        if (TT == 1) {
+          vg[cg] += __shfl_xor_sync(FULL, vg[cg], 2);
+          vh[cg] += __shfl_xor_sync(FULL, vh[cg], 2);
+        }
+        // token 2 cg + (c >> 1) of the group
+        constexpr int T1 = TT == 1 ? 0 : 1;
+        const float sa = (c >> 1) == 0 ? fa[2 * cg] : fa[2 * cg + T1];
+        const float sb = (c >> 1) == 0 ? fb[2 * cg] : fb[2 * cg + T1];
+        vg[cg] = (vg[cg] * sa) * sb;
+        vh[cg] = (vh[cg] * sa) * sb;
       }
-      const int tt = TT == 1 ? 0 : (c >> 1);
-      const float sa = (TT == 1 || tt == 0) ? fa[0] : fa[TT - 1], sb = (TT == 1 || tt == 0) ? fb[0] : fb[TT - 1];
-      vg = (vg * sa) * sb;
-      vh = (vh * sa) * sb;
       const int b = pi % MMV_NB;
       if (pi >= MMV_NB) mbar_wait(&red_empty[b], ((pi / MMV_NB) - 1) & 1, &abort_flag);
       if ((c & (TT == 1 ? 3 : 1)) == 0) {
-        red[b][warp][tt * 16 + g] = vg;
-        red[b][warp][tt * 16 + g + 8] = vh;
+#pragma unroll
+        for (int cg = 0; cg < NG; cg++) {
+          const int tt = TT == 1 ? 0 : 2 * cg + (c >> 1);
+          red[b][warp][tt * 16 + g] = vg[cg];
+          red[b][warp][tt * 16 + g + 8] = vh[cg];
+        }
       }
       if (warp == 0 && lane == 0) {
         rmeta[b][0] = t;
@@ -578,7 +617,8 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
       if (lane == 0) mbar_arrive(&red_full[b]);
       pi++;
       sc0 = -1;
-      acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+#pragma unroll
+      for (int cg = 0; cg < NG; cg++) acc[cg][0] = acc[cg][1] = acc[cg][2] = acc[cg][3] = 0.f;
     }
     // no more pieces
     {
@@ -597,23 +637,40 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     static_assert(MMV_NE == 1, "one epilogue warp");
     pdl_wait();  // y, the KV cache and the step's row table belong to earlier kernels
     const int target = a.ks * a.nsc;
-    // RMSNorm factor of this lane's token, from the consumers' sums of squares
-    double inv = 1.0;
+    // RMSNorm factor of this lane's token in each value group, from the
+    // consumers' sums of squares
+    double inv[NG];
+#pragma unroll
+    for (int q = 0; q < NG; q++) inv[q] = 1.0;
     if (a.f.norm_w) {
       if (__all_sync(FULL, mbar_wait(&ss_bar, 0, &abort_flag))) {
-        const int tt = min(lane >> 4, TT - 1);
-        double tot = 0.0;
-        for (int w = 0; w < MMV_NW; w++) tot += sred[w][tt];
-        inv = 1.0 / sqrt(tot / a.cols + 1e-5);
+#pragma unroll
+        for (int q = 0; q < NG; q++) {
+          const int tt = min(2 * q + (lane >> 4), TT - 1);
+          double tot = 0.0;
+          for (int w = 0; w < MMV_NW; w++) tot += sred[w][tt];
+          inv[q] = 1.0 / sqrt(tot / a.cols + 1e-5);
+        }
       }
     }
-    auto finish = [&](int t, float v) {
-      const int rr = lane & 15, tt = lane >> 4, row = t * 16 + rr;
-      v = (float)((double)v * inv);
-      const float partner = __shfl_xor_sync(FULL, v, 1);
-      if (lane < NV && tt < a.T && row < a.rows) mmv_store(a, row, tt, v, partner);
+    // lane l of value group q: row l & 15 of the tile, token 2 q + (l >> 4)
+    auto finish = [&](int t, const float (&vv)[NG]) {
+      const int rr = lane & 15, row = t * 16 + rr;
+#pragma unroll
+      for (int q = 0; q < NG; q++) {
+        const int tt = 2 * q + (lane >> 4);
+        const float v = (float)((double)vv[q] * inv[q]);
+        const float partner = __shfl_xor_sync(FULL, v, 1);
+        if (lane < NV && tt < a.T && row < a.rows) mmv_store(a, row, tt, v, partner);
+      }
     };
-    float vb[MMV_UB] = {};
+    // workspace: [chunk][tile][part][NG * 32]; a chunk of one sub-chunk is
+    // never split between CTAs, so it has one part
+    const int np = a.nsc > 1 ? 2 : 1;
+    auto wsp = [&](int kc, int t, int part) {
+      return a.ws + (((size_t)kc * a.tiles + t) * np + part) * (NG * 32) + lane;
+    };
+    float vb[MMV_UB][NG] = {};
     int tb[MMV_UB] = {}, ub[MMV_UB] = {};
     bool fb_[MMV_UB] = {};
     int nbat = 0;
@@ -642,19 +699,27 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
         for (int i = 0; i < MMV_UB; i++) {
           if (!((fin >> i) & 1u)) continue;
           const int t = tb[i];
-          float v = 0.f;
-          if (lane < NV) {
-            // the tile's partials in (chunk, part) order; eight loads in flight at a time
-            for (int q0 = 0; q0 < 2 * a.ks; q0 += 8) {
-              float pv[8];
+          // the tile's partials, summed in (chunk, part) order; 8 partials
+          // (x NG values) in flight at once
+          constexpr int PB = 8;
+          float v[NG];
 #pragma unroll
-              for (int j = 0; j < 8; j++) {
-                const int q = q0 + j;
-                pv[j] = q < 2 * a.ks ? ld_relaxed(a.ws + (((size_t)(q >> 1) * a.tiles + t) * 2 + (q & 1)) * 32 + lane)
-                                     : 0.f;
+          for (int q = 0; q < NG; q++) v[q] = 0.f;
+          if (lane < NV) {
+            const int tot = a.ks * np;
+            for (int p0 = 0; p0 < tot; p0 += PB) {
+              float pv[PB][NG];
+#pragma unroll
+              for (int j = 0; j < PB; j++) {
+                const int p = p0 + j;
+                const float* src = wsp(min(p, tot - 1) / np, t, min(p, tot - 1) % np);
+#pragma unroll
+                for (int q = 0; q < NG; q++) pv[j][q] = p < tot ? ld_relaxed(src + q * 32) : 0.f;
               }
 #pragma unroll
-              for (int j = 0; j < 8; j++) v += pv[j];
+              for (int j = 0; j < PB; j++)
+#pragma unroll
+                for (int q = 0; q < NG; q++) v[q] += pv[j][q];
             }
           }
           if (lane == i) a.cnt[t] = 0;  // ready for the next launch
@@ -673,23 +738,35 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
         break;
       }
       if (t < 0) break;
-      float v = 0.f;
-      if (lane < NV) {
+      float v[NG];
 #pragma unroll
-        for (int w = 0; w < MMV_NW; w++) v += red[b][w][lane];
+      for (int q = 0; q < NG; q++) {
+        v[q] = 0.f;
+        if (lane < NV) {
+#pragma unroll
+          for (int w = 0; w < MMV_NW; w++) v[q] += red[b][w][q * 32 + lane];
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_empty[b]);
       const bool whole = sc0 == 0 && cnt_u == a.nsc;
       if (!(whole && a.ks == 1) && lane < NV) {
-        float* w0 = a.ws + (((size_t)kc0 * a.tiles + t) * 2 + (sc0 == 0 ? 0 : 1)) * 32 + lane;
-        *w0 = v;
-        if (whole) w0[32] = 0.f;  // no second part
+        float* w0 = wsp(kc0, t, sc0 == 0 ? 0 : 1);
+#pragma unroll
+        for (int q = 0; q < NG; q++) {
+          w0[q * 32] = v[q];
+          if (whole && np == 2) w0[NG * 32 + q * 32] = 0.f;  // no second part
+        }
       }
-      vb[nbat] = v;
-      tb[nbat] = t;
-      ub[nbat] = cnt_u;
-      fb_[nbat] = whole;
+#pragma unroll
+      for (int i = 0; i < MMV_UB; i++)  // (register arrays: constant indexes)
+        if (i == nbat) {
+#pragma unroll
+          for (int q = 0; q < NG; q++) vb[i][q] = v[q];
+          tb[i] = t;
+          ub[i] = cnt_u;
+          fb_[i] = whole;
+        }
       if (++nbat == MMV_UB) flush();
     }
     if (nbat) flush();
@@ -741,10 +818,11 @@ static void mmv_pick(MmShape* sh) {
   const int stage = (int)sh->stage_bytes, max_dyn = mmv_max_dyn<KIND, TT>();
   if (cudaFuncSetAttribute(k_mmv<KIND, TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn) != cudaSuccess)
     cudaGetLastError();
+  const int rb = mmv_red_bytes(TT);
   int best_s = 2, best_o = 0;
-  for (int s = std::min(MMV_MAX_STAGES, max_dyn / stage); s >= 2; s--) {
+  for (int s = std::min(MMV_MAX_STAGES, (max_dyn - rb) / stage); s >= 2; s--) {
     // (s goes down: the first depth that reaches an occupancy is the deepest one)
-    const int o = std::min(mmv_occ<KIND, TT>(s * stage), 2);
+    const int o = std::min(mmv_occ<KIND, TT>(rb + s * stage), 2);
     if (o > best_o) {
       best_o = o;
       best_s = s;
@@ -753,7 +831,7 @@ static void mmv_pick(MmShape* sh) {
   }
   if (best_o == 0) best_o = 1;
   sh->stages = best_s;
-  sh->smem = best_s * stage;
+  sh->smem = rb + best_s * stage;
   sh->ctas = best_o;
 }
 
@@ -761,26 +839,29 @@ int mm_prepare(Matrix* m) {
   TN_REQUIRE(m->kind == MK_Q4 || m->kind == MK_Q8, TN_EINVAL, "mm_prepare: kind %d", m->kind);
   int ks_max = 1;
   size_t ws = 0;
-  for (int tt = 1; tt <= 2; tt++) {
-    MmShape& sh = m->mm[tt - 1];
-    const int cp = MMV_CE / tt / 64, scmax = mmv_sc(m->kind);
+  for (int i = 0; i < 3; i++) {
+    const int tt = 1 << i;
+    MmShape& sh = m->mm[i];
+    const int cp = MMV_CE / tt / 64, scmax = mmv_sc(m->kind, tt);
     sh.ks = (m->pairs + cp - 1) / cp;
     sh.ckp = (m->pairs + sh.ks - 1) / sh.ks;
     sh.nsc = (sh.ckp + scmax - 1) / scmax;
     sh.scp = (sh.ckp + sh.nsc - 1) / sh.nsc;
     sh.stage_bytes = (uint32_t)scmax * tile_rec_bytes(m->kind);  // room for a full sub-chunk
-    ws = std::max(ws, (size_t)sh.ks * m->tiles * 2 * 32);
+    ws = std::max(ws, (size_t)sh.ks * m->tiles * 2 * 32 * std::max(1, tt / 2));
     ks_max = std::max(ks_max, sh.ks);
     // (set once per matrix, outside any stream capture)
     if (m->kind == MK_Q4) {
       if (tt == 1) mmv_pick<MK_Q4, 1>(&sh);
-      else mmv_pick<MK_Q4, 2>(&sh);
+      else if (tt == 2) mmv_pick<MK_Q4, 2>(&sh);
+      else mmv_pick<MK_Q4, 4>(&sh);
     } else {
       if (tt == 1) mmv_pick<MK_Q8, 1>(&sh);
-      else mmv_pick<MK_Q8, 2>(&sh);
+      else if (tt == 2) mmv_pick<MK_Q8, 2>(&sh);
+      else mmv_pick<MK_Q8, 4>(&sh);
     }
   }
-  m->ws_floats = ws;                          // two 32-float parts per (chunk, tile)
+  m->ws_floats = ws;                          // two parts per (chunk, tile)
   m->cnt_ints = (size_t)m->tiles + 2 * ks_max;  // per-tile arrivals, per-chunk tickets and done counts
   return TN_OK;
 }
@@ -788,7 +869,7 @@ int mm_prepare(Matrix* m) {
 template <int KIND, int TT>
 static int launch_mmv(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode,
                       const MvFuse& f, int* err, cudaStream_t s) {
-  const MmShape& sh = m.mm[TT - 1];
+  const MmShape& sh = m.mm[TT == 1 ? 0 : TT == 2 ? 1 : 2];
   // at most one CTA per (tile, chunk), at least one per chunk
   const int grid = std::max(sh.ks, std::min(m.tiles * sh.ks, sh.ctas * num_sms()));
   const MmvArgs a{m.data, m.rows, m.tiles, m.pairs, m.cols, T, x, ldx, y, ldy, mode, sh.ks, sh.ckp, sh.nsc,
@@ -797,7 +878,15 @@ static int launch_mmv(const Matrix& m, int T, const float* x, int ldx, float* y,
   return TN_OK;
 }
 
-bool matvec_dec_ok(const Matrix& m, int T) { return (m.kind == MK_Q4 || m.kind == MK_Q8) && T >= 1 && T <= 2; }
+bool matvec_dec_ok(const Matrix& m, int T) { return (m.kind == MK_Q4 || m.kind == MK_Q8) && T >= 1 && T <= 8; }
+
+template <int KIND>
+static int launch_mmv_n(const Matrix& m, int n, const float* x, int ldx, float* y, int ldy, int mode,
+                        const MvFuse& f, int* err, cudaStream_t s) {
+  if (n == 1) return launch_mmv<KIND, 1>(m, n, x, ldx, y, ldy, mode, f, err, s);
+  if (n == 2) return launch_mmv<KIND, 2>(m, n, x, ldx, y, ldy, mode, f, err, s);
+  return launch_mmv<KIND, 4>(m, n, x, ldx, y, ldy, mode, f, err, s);
+}
 
 int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ldy, int mode, const MvFuse& f,
                int* err, cudaStream_t s) {
@@ -805,9 +894,11 @@ int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ld
   TN_REQUIRE(mode != EPI_SWIGLU || (m.rows & 1) == 0, TN_EINVAL, "swiglu needs paired rows");
   TN_REQUIRE(err, TN_EINVAL, "matvec_dec: error flag required");
   TN_REQUIRE(m.ws && m.cnt, TN_ESTATE, "matvec_dec: cross-CTA workspace missing");
-  // tokens two at a time; each launch streams the whole matrix
-  for (int t0 = 0; t0 < T; t0 += 2) {
-    const int n = std::min(2, T - t0);
+  // up to four tokens per launch (1, 2 or 4 token columns); each launch
+  // streams the whole matrix.  (Eight columns cost as much as two launches
+  // of four: the per-record digit work, not the weight stream, bounds them.)
+  for (int t0 = 0; t0 < T; t0 += 4) {
+    const int n = std::min(4, T - t0);
     MvFuse g = f;
     const float* xj = x;
     if (f.rowsel) g.rowsel = f.rowsel + t0;
@@ -816,13 +907,8 @@ int matvec_dec(const Matrix& m, int T, const float* x, int ldx, float* y, int ld
     if (f.cs) g.cs = f.cs + (size_t)t0 * (f.hd / 2);
     if (f.q_out) g.q_out = f.q_out + (size_t)t0 * f.q_dim;
     float* yj = y + (size_t)t0 * ldy;
-    int rc;
-    if (m.kind == MK_Q4)
-      rc = n == 1 ? launch_mmv<MK_Q4, 1>(m, n, xj, ldx, yj, ldy, mode, g, err, s)
-                  : launch_mmv<MK_Q4, 2>(m, n, xj, ldx, yj, ldy, mode, g, err, s);
-    else
-      rc = n == 1 ? launch_mmv<MK_Q8, 1>(m, n, xj, ldx, yj, ldy, mode, g, err, s)
-                  : launch_mmv<MK_Q8, 2>(m, n, xj, ldx, yj, ldy, mode, g, err, s);
+    const int rc = m.kind == MK_Q4 ? launch_mmv_n<MK_Q4>(m, n, xj, ldx, yj, ldy, mode, g, err, s)
+                                   : launch_mmv_n<MK_Q8>(m, n, xj, ldx, yj, ldy, mode, g, err, s);
     if (rc != TN_OK) return rc;
   }
   return TN_OK;

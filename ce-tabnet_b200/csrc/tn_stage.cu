@@ -200,19 +200,19 @@ static int load_layer(tn_stage* st, const tn_stage_spec* sp, int li, uint8_t* st
   LayerW& W = st->layers[li];
   const int q = lw.quant;
   // wq | wk | wv fused into one [qDim + 2 kvDim, H] matrix
-  if ((rc = matrix_alloc(&W.qkv, q, st->qDim + 2 * st->kvDim, st->H, st->stream))) return rc;
+  if ((rc = matrix_alloc(&W.qkv, q, st->qDim + 2 * st->kvDim, st->H, st->stream, false))) return rc;
   // (q and k rows pair-interleaved per head for the RoPE epilogue: stride -hd)
   if ((rc = matrix_repack(&W.qkv, src + L.off[1], q, st->qDim, 0, -st->hd, st->stream))) return rc;
   if ((rc = matrix_repack(&W.qkv, src + L.off[2], q, st->kvDim, st->qDim, -st->hd, st->stream))) return rc;
   if ((rc = matrix_repack(&W.qkv, src + L.off[3], q, st->kvDim, st->qDim + st->kvDim, 1, st->stream)))
     return rc;
-  if ((rc = matrix_alloc(&W.o, q, st->H, st->qDim, st->stream))) return rc;
+  if ((rc = matrix_alloc(&W.o, q, st->H, st->qDim, st->stream, false))) return rc;
   if ((rc = matrix_repack(&W.o, src + L.off[4], q, st->H, 0, 1, st->stream))) return rc;
   // w_gate / w_up interleaved by row: (2i, 2i+1) = (gate_i, up_i) for the SwiGLU epilogue
-  if ((rc = matrix_alloc(&W.gu, q, 2 * st->F, st->H, st->stream))) return rc;
+  if ((rc = matrix_alloc(&W.gu, q, 2 * st->F, st->H, st->stream, false))) return rc;
   if ((rc = matrix_repack(&W.gu, src + L.off[6], q, st->F, 0, 2, st->stream))) return rc;
   if ((rc = matrix_repack(&W.gu, src + L.off[7], q, st->F, 1, 2, st->stream))) return rc;
-  if ((rc = matrix_alloc(&W.down, q, st->H, st->F, st->stream))) return rc;
+  if ((rc = matrix_alloc(&W.down, q, st->H, st->F, st->stream, false))) return rc;
   if ((rc = matrix_repack(&W.down, src + L.off[8], q, st->H, 0, 1, st->stream))) return rc;
   // norms: f16 bits -> f32 (exact)
   TN_CHECK_CUDA(cudaMalloc(&W.attn_norm, align256(st->H * sizeof(float))));
@@ -302,7 +302,7 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   const uint8_t* src = nullptr;
   if (st->first) {
     if ((rc = stage_src(sp, sp->embed, embed_bytes, staging, st->stream, &src))) return rc;
-    if ((rc = matrix_alloc(&st->embed, sp->embed_quant, st->V, st->H, st->stream))) return rc;
+    if ((rc = matrix_alloc(&st->embed, sp->embed_quant, st->V, st->H, st->stream, false))) return rc;
     if ((rc = matrix_repack(&st->embed, src, sp->embed_quant, st->V, 0, 1, st->stream))) return rc;
     TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
     st->weight_bytes += st->embed.bytes;
@@ -310,7 +310,7 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   }
   if (st->last) {
     if ((rc = stage_src(sp, sp->lm_head, head_bytes, staging, st->stream, &src))) return rc;
-    if ((rc = matrix_alloc(&st->lm_head, sp->lm_head_quant, st->V, st->H, st->stream))) return rc;
+    if ((rc = matrix_alloc(&st->lm_head, sp->lm_head_quant, st->V, st->H, st->stream, false))) return rc;
     if ((rc = matrix_repack(&st->lm_head, src, sp->lm_head_quant, st->V, 0, 1, st->stream))) return rc;
     TN_CHECK_CUDA(cudaStreamSynchronize(st->stream));
     if ((rc = stage_src(sp, sp->norm, (uint64_t)st->H * 2, staging, st->stream, &src))) return rc;
@@ -356,6 +356,28 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
     const int kmax = std::max(st->H, std::max(st->qDim, st->F));
     st->gemm_ws_bytes = gemm_scratch_bytes(T, kmax);
     if ((rc = dalloc(st, (char**)&st->gemm_ws, st->gemm_ws_bytes))) return rc;
+  }
+  // one cross-CTA workspace for every decode matvec of the stage (its
+  // launches are ordered on the stage stream)
+  {
+    size_t wsf = 0, cnti = 0;
+    std::vector<Matrix*> ms;
+    for (auto& L : st->layers) ms.insert(ms.end(), {&L.qkv, &L.o, &L.gu, &L.down});
+    if (st->first) ms.push_back(&st->embed);
+    if (st->last) ms.push_back(&st->lm_head);
+    for (Matrix* m : ms) {
+      wsf = std::max(wsf, m->ws_floats);
+      cnti = std::max(cnti, m->cnt_ints);
+    }
+    float* ws = nullptr;
+    int* cnt = nullptr;
+    if (wsf && (rc = dalloc(st, &ws, wsf))) return rc;
+    if (cnti && (rc = dalloc(st, &cnt, cnti))) return rc;
+    for (Matrix* m : ms)
+      if (m->ws_floats) {
+        m->ws = ws;
+        m->cnt = cnt;
+      }
   }
   if ((rc = dalloc(st, &st->freq, (size_t)(st->hd / 2)))) return rc;
   // RoPE frequencies theta^(-2i/hd) in double (web/inference-worker.js:533)

@@ -77,7 +77,7 @@ def _maxrel(a, b):
     ("q4_0", 4096, 4096), ("q4_0", 14336, 4096), ("q4_0", 4096, 14336), ("q8_0", 4096, 4096),
     ("q8_0", 1000, 8192), ("q4_0", 8, 28672), ("q8_0", 256, 688), ("f16", 300, 200), ("f32", 77, 96),
 ])
-@pytest.mark.parametrize("T", [1, 2, 3, 8])
+@pytest.mark.parametrize("T", [1, 2, 3, 5, 8, 11])
 def test_matvec_vs_oracle(pkg, ref, torch_cuda, quant, rows, cols, T):
     torch = torch_cuda
     buf = _synth_matrix(pkg, rows, cols, quant, seed=rows + cols)

@@ -114,7 +114,7 @@ def test_tiny_two_stages_hop_all(pkg, ref, tiny):
     pkg.freeStage(b)
 
 
-@pytest.mark.parametrize("n_seqs", [2, 4])
+@pytest.mark.parametrize("n_seqs", [2, 4, 6, 8])
 def test_batch_equals_individual(pkg, ref, tiny, n_seqs):
     m, w = tiny
     one, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
