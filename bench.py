@@ -64,6 +64,7 @@ def parse_args(argv=None):
     p.add_argument("--tokens", default="1,4,16,64,512", help="matvec sweep: token counts")
     p.add_argument("--ctx", default="512,2048,8192,32768", help="attention sweep: cached positions")
     p.add_argument("--seqs", default="1,8,64", help="attention sweep: concurrent rows")
+    p.add_argument("--kv", default="f32,f16", help="attention sweep: KV cache element types")
     p.add_argument("--reps", type=int, default=20, help="kernel sweeps: timed launches per point")
     return p.parse_args(argv)
 
@@ -249,50 +250,52 @@ def micro_attn(args):
     clocks = ClockSampler(physical_gpu(0))
     clocks.start()
     points = []
-    for ctx in _ints(args.ctx):
-        for seqs in _ints(args.seqs):
-            slot_bytes = 2 * nKV * ctx * hd * 4
-            groups = max(1, int(2 * L2_BYTES // (slot_bytes * seqs)) + 1)
-            n_slots = groups * seqs
-            gen = torch.Generator(device="cuda").manual_seed(ctx + seqs)
-            K = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen)
-            V = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen)
-            q = torch.randn((seqs, nH * hd), device="cuda", generator=gen)
-            out = torch.empty_like(q)
-            lens = torch.full((seqs,), ctx, dtype=torch.int32, device="cuda")
-            slots = [torch.arange(g0 * seqs, (g0 + 1) * seqs, dtype=torch.int32, device="cuda") for g0 in range(groups)]
-            nbytes = lib.tn_attention_scratch_bytes(seqs, nH, nKV, hd, ctx)
-            scratch = torch.empty(max(nbytes, 256), dtype=torch.uint8, device="cuda")
+    for kv, ctx, seqs in [(k, c, n) for k in args.kv.split(",") for c in _ints(args.ctx) for n in _ints(args.seqs)]:
+        eb = 2 if kv == "f16" else 4
+        slot_bytes = 2 * nKV * ctx * hd * eb
+        groups = max(1, int(2 * L2_BYTES // (slot_bytes * seqs)) + 1)
+        n_slots = groups * seqs
+        gen = torch.Generator(device="cuda").manual_seed(ctx + seqs)
+        dt = torch.float16 if kv == "f16" else torch.float32
+        K = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen).to(dt)
+        V = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen).to(dt)
+        fn = lib.tn_attention_f16 if kv == "f16" else lib.tn_attention
+        q = torch.randn((seqs, nH * hd), device="cuda", generator=gen)
+        out = torch.empty_like(q)
+        lens = torch.full((seqs,), ctx, dtype=torch.int32, device="cuda")
+        slots = [torch.arange(g0 * seqs, (g0 + 1) * seqs, dtype=torch.int32, device="cuda") for g0 in range(groups)]
+        nbytes = lib.tn_attention_scratch_bytes(seqs, nH, nKV, hd, ctx)
+        scratch = torch.empty(max(nbytes, 256), dtype=torch.uint8, device="cuda")
 
-            def call(i):
-                P.check(lib.tn_attention(seqs, n_slots, nH, nKV, hd, ctx, q.data_ptr(), K.data_ptr(), V.data_ptr(),
-                                         slots[i % groups].data_ptr(), lens.data_ptr(), out.data_ptr(),
-                                         scratch.data_ptr(), nbytes, None))
+        def call(i):
+            P.check(fn(seqs, n_slots, nH, nKV, hd, ctx, q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                       slots[i % groups].data_ptr(), lens.data_ptr(), out.data_ptr(), scratch.data_ptr(), nbytes,
+                       None))
 
-            for i in range(max(3, args.warmup)):
-                call(i)
-            torch.cuda.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for i in range(args.reps):
-                call(i)
-            e1.record()
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) / args.reps * 1e3
-            byts = seqs * ctx * 2 * nKV * hd * 4 + 2 * seqs * nH * hd * 4
-            gbs = byts / us / 1e3
-            points.append({"ctx": ctx, "seqs": seqs, "us": round(us, 2), "GB_s": round(gbs, 1),
-                           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
-                                        "frac": round(gbs / hbm, 4), "peak_source": hbm_kind},
-                           "arena_MB": round(n_slots * slot_bytes / 1e6, 1)})
-            print(f"# attn ctx={ctx} seqs={seqs}: {us:.1f} us, {gbs:.0f} GB/s", file=sys.stderr, flush=True)
-            del K, V
-            torch.cuda.empty_cache()
+        for i in range(max(3, args.warmup)):
+            call(i)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for i in range(args.reps):
+            call(i)
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / args.reps * 1e3
+        byts = seqs * ctx * 2 * nKV * hd * eb + 2 * seqs * nH * hd * 4
+        gbs = byts / us / 1e3
+        points.append({"kv": kv, "ctx": ctx, "seqs": seqs, "us": round(us, 2), "GB_s": round(gbs, 1),
+                       "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                    "frac": round(gbs / hbm, 4), "peak_source": hbm_kind},
+                       "arena_MB": round(n_slots * slot_bytes / 1e6, 1)})
+        print(f"# attn kv={kv} ctx={ctx} seqs={seqs}: {us:.1f} us, {gbs:.0f} GB/s", file=sys.stderr, flush=True)
+        del K, V
+        torch.cuda.empty_cache()
     clk = clocks.stop()
-    print(json.dumps({"micro": "attn", "metric": "GQA decode attention HBM GB/s (32/8 heads x 128, f32 KV)",
+    print(json.dumps({"micro": "attn", "metric": "GQA decode attention HBM GB/s (32/8 heads x 128, f32 / fp16 KV)",
                       "unit": "GB/s", "points": points, "clocks": clk, "reps": args.reps,
                       "config": {"l2": "launches rotate over sequence slots of an arena > 2 x L2",
-                                 "values": "q, K, V f32 N(0,1)"}}), flush=True)
+                                 "values": "q f32, K / V N(0,1) stored as the point's kv type"}}), flush=True)
     return 0
 
 

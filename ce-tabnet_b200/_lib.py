@@ -21,6 +21,7 @@ TN_HOP_LAST, TN_HOP_ALL = 0, 1
 TN_FLAG_NO_GRAPHS = 1
 TN_FLAG_PROFILE = 2
 TN_FLAG_NO_FUSED_DECODE = 4
+TN_FLAG_KV_F16 = 8
 PROF_CLASSES = ["matvec_qkv", "matvec_o", "matvec_gate_up", "matvec_down", "matvec_lm_head", "attention",
                 "rmsnorm", "rope_kv", "other"]
 TN_TAG_EMBED, TN_TAG_NORM, TN_TAG_LM_HEAD = 1, 2, 3
@@ -117,6 +118,9 @@ SIGNATURES = [
     ("tn_attention", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_uint64, C.c_void_p]),
+    ("tn_attention_f16", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                   C.c_void_p, C.c_uint64, C.c_void_p]),
     ("tn_attention_static", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                       C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                       C.c_void_p]),

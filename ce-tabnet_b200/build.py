@@ -18,7 +18,7 @@ PKG = Path(__file__).resolve().parent
 CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 LIB = PKG / "libtabnet_stage.so"
-SOURCES = ["tn_synth.cu", "tn_kernels.cu", "tn_mmv.cu", "tn_gemm.cu", "tn_stage.cu", "tn_abi.cu"]
+SOURCES = ["tn_synth.cu", "tn_kernels.cu", "tn_mmv.cu", "tn_gemm.cu", "tn_attn.cu", "tn_stage.cu", "tn_abi.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + [
     "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",

@@ -20,9 +20,12 @@ struct DevSwitch {
   }
 };
 
+// the row table of tn_attention's rows; also zeroes the split arrival counters
 __global__ void k_rows_from_slots(const int32_t* __restrict__ slot, const int32_t* __restrict__ len, int n,
-                                  int n_slots, int max_ctx, RowInfo* __restrict__ rows) {
+                                  int n_slots, int max_ctx, RowInfo* __restrict__ rows, int* __restrict__ cnt,
+                                  int n_cnt) {
   const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  for (int i = r; i < n_cnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
   if (r >= n) return;
   int s = slot[r], l = len[r];
   if (s < 0 || s >= n_slots || l < 1) {
@@ -146,45 +149,94 @@ extern "C" void tn_matrix_free(tn_matrix* m) {
 }
 
 // caller scratch: the row table (the splits merge on chip)
-static size_t attn_total_scratch(int n_rows) { return ((size_t)n_rows * sizeof(RowInfo) + 255) & ~(size_t)255; }
+// tn_attention's scratch: the row table (16 bytes a row), the split arrival
+// counters and the split partials, each 256-byte aligned
+struct AttnScratch {
+  AttnPlan plan;
+  size_t cnt_off = 0, ws_off = 0, total = 0;
+};
+static size_t al256(size_t x) { return (x + 255) & ~(size_t)255; }
+static AttnScratch attn_scratch(int n_rows, int nH, int nKV, int hd, int max_ctx, int kv_type,
+                                size_t cap = SIZE_MAX) {
+  AttnScratch a;
+  a.cnt_off = al256((size_t)n_rows * sizeof(RowInfo));
+  const size_t cnt_bytes = al256((size_t)n_rows * std::max(1, nKV) * sizeof(int));
+  a.ws_off = a.cnt_off + cnt_bytes;
+  const size_t room = cap > a.ws_off ? (cap - a.ws_off) / sizeof(float) : 0;
+  a.plan = attn_plan(n_rows, nH, nKV, hd, max_ctx, kv_type, room);
+  a.total = a.plan.splits > 1 ? a.ws_off + al256(a.plan.ws_floats * sizeof(float)) : a.cnt_off;
+  return a;
+}
 
-// row table, then the one-kernel attention
+// row table (and zeroed split counters), then the one-kernel attention
 static int attn_run(int n_rows, int n_slots, int n_heads, int n_kv_heads, int head_dim, int max_ctx, const float* d_q,
-                    const float* d_k, const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
-                    void* scratch, cudaStream_t s) {
-  RowInfo* rows = (RowInfo*)scratch;
-  k_rows_from_slots<<<(n_rows + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows);
+                    const void* d_k, const void* d_v, int kv_type, const int32_t* d_slot, const int32_t* d_len,
+                    float* d_out, void* scratch, size_t scratch_bytes, cudaStream_t s) {
+  const AttnScratch sc = attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, kv_type, scratch_bytes);
+  TN_REQUIRE(sc.total <= scratch_bytes, TN_EINVAL, "attention: scratch of %zu bytes, %zu needed", scratch_bytes,
+             sc.total);
+  char* base = (char*)scratch;
+  RowInfo* rows = (RowInfo*)base;
+  int* cnt = sc.plan.splits > 1 ? (int*)(base + sc.cnt_off) : nullptr;
+  float* ws = sc.plan.splits > 1 ? (float*)(base + sc.ws_off) : nullptr;
+  const int n_cnt = cnt ? (int)sc.plan.cnt_ints : 0;
+  const int work = std::max(n_rows, n_cnt);
+  k_rows_from_slots<<<(work + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows, cnt, n_cnt);
   TN_CHECK_LAUNCH();
   const size_t kvh_stride = (size_t)max_ctx * head_dim;
-  return attention(d_q, n_heads * head_dim, d_k, d_v, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows, n_heads,
-                   n_kv_heads, head_dim, attn_splits(n_rows, n_kv_heads, max_ctx), d_out, n_heads * head_dim, s);
+  return attention(d_q, n_heads * head_dim, d_k, d_v, kv_type, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows,
+                   n_heads, n_kv_heads, head_dim, sc.plan, d_out, n_heads * head_dim, ws, cnt, s);
+}
+
+static int attn_check(const char* fn, int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
+                      int32_t head_dim, int32_t max_ctx, const void* d_q, const void* d_k, const void* d_v,
+                      const int32_t* d_slot, const int32_t* d_len, const float* d_out) {
+  TN_REQUIRE(n_rows >= 0 && n_slots > 0 && n_heads > 0 && n_kv_heads > 0 && max_ctx > 0, TN_EINVAL,
+             "%s: bad sizes", fn);
+  TN_REQUIRE(d_q && d_k && d_v && d_slot && d_len && d_out, TN_EINVAL, "%s: null pointer", fn);
+  TN_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128, TN_EUNSUPPORTED, "%s: head_dim %d unsupported",
+             fn, head_dim);
+  return TN_OK;
 }
 
 extern "C" uint64_t tn_attention_scratch_bytes(int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,
                                                int32_t head_dim, int32_t max_ctx) {
   if (n_rows <= 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || max_ctx <= 0) return 0;
-  return attn_total_scratch(n_rows);
+  // (enough for either cache element type)
+  return std::max(attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, KV_F32).total,
+                  attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, KV_F16).total);
+}
+
+static int attn_entry(const char* fn, int kv_type, int32_t n_rows, int32_t n_slots, int32_t n_heads,
+                      int32_t n_kv_heads, int32_t head_dim, int32_t max_ctx, const float* d_q, const void* d_k,
+                      const void* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out, void* d_scratch,
+                      uint64_t scratch_bytes, void* stream) {
+  clear_error();
+  int rc = attn_check(fn, n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v, d_slot, d_len,
+                      d_out);
+  if (rc) return rc;
+  TN_REQUIRE(d_scratch, TN_EINVAL, "%s: null scratch", fn);
+  TN_REQUIRE((reinterpret_cast<uintptr_t>(d_scratch) & 255) == 0, TN_EINVAL, "%s: scratch must be 256-byte aligned",
+             fn);
+  if (n_rows == 0) return TN_OK;
+  return attn_run(n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v, kv_type, d_slot, d_len,
+                  d_out, d_scratch, scratch_bytes, (cudaStream_t)stream);
 }
 
 extern "C" int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
                             int32_t head_dim, int32_t max_ctx, const float* d_q, const float* d_k,
                             const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
                             void* d_scratch, uint64_t scratch_bytes, void* stream) {
-  clear_error();
-  TN_REQUIRE(n_rows >= 0 && n_slots > 0 && n_heads > 0 && n_kv_heads > 0 && max_ctx > 0, TN_EINVAL,
-             "tn_attention: bad sizes");
-  TN_REQUIRE(d_q && d_k && d_v && d_slot && d_len && d_out && d_scratch, TN_EINVAL,
-             "tn_attention: null pointer");
-  TN_REQUIRE((reinterpret_cast<uintptr_t>(d_scratch) & 255) == 0, TN_EINVAL,
-             "tn_attention: scratch must be 256-byte aligned");
-  TN_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128, TN_EUNSUPPORTED,
-             "tn_attention: head_dim %d unsupported", head_dim);
-  if (n_rows == 0) return TN_OK;
-  const size_t need = attn_total_scratch(n_rows);
-  TN_REQUIRE(scratch_bytes >= need, TN_EINVAL, "tn_attention: scratch of %llu bytes, %zu needed",
-             (unsigned long long)scratch_bytes, need);
-  return attn_run(n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v, d_slot, d_len, d_out,
-                  d_scratch, (cudaStream_t)stream);
+  return attn_entry("tn_attention", KV_F32, n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v,
+                    d_slot, d_len, d_out, d_scratch, scratch_bytes, stream);
+}
+
+extern "C" int tn_attention_f16(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
+                                int32_t head_dim, int32_t max_ctx, const float* d_q, const uint16_t* d_k,
+                                const uint16_t* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
+                                void* d_scratch, uint64_t scratch_bytes, void* stream) {
+  return attn_entry("tn_attention_f16", KV_F16, n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k,
+                    d_v, d_slot, d_len, d_out, d_scratch, scratch_bytes, stream);
 }
 
 // ---- tn_attention_static: attention with its scratch in a fixed device array,
@@ -219,22 +271,22 @@ extern "C" int tn_attention_static(int32_t n_rows, int32_t n_slots, int32_t n_he
                                    const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
                                    void* stream) {
   clear_error();
-  TN_REQUIRE(n_rows >= 0 && n_slots > 0 && n_heads > 0 && n_kv_heads > 0 && max_ctx > 0, TN_EINVAL,
-             "tn_attention_static: bad sizes");
-  TN_REQUIRE(d_q && d_k && d_v && d_slot && d_len && d_out, TN_EINVAL, "tn_attention_static: null pointer");
-  TN_REQUIRE(head_dim == 32 || head_dim == 64 || head_dim == 128, TN_EUNSUPPORTED,
-             "tn_attention_static: head_dim %d unsupported", head_dim);
+  int rc = attn_check("tn_attention_static", n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v,
+                      d_slot, d_len, d_out);
+  if (rc) return rc;
   if (n_rows == 0) return TN_OK;
-  const size_t need = attn_total_scratch(n_rows);
+  // the split count is bounded so that the partials fit the fixed array
+  const size_t need = attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, KV_F32,
+                                   TN_ATTENTION_STATIC_SCRATCH_BYTES).total;
   TN_REQUIRE(need <= TN_ATTENTION_STATIC_SCRATCH_BYTES, TN_ECAPACITY,
              "tn_attention_static: %d rows need %zu bytes of scratch, above the fixed %u; "
              "use tn_attention with caller scratch",
              n_rows, need, (unsigned)TN_ATTENTION_STATIC_SCRATCH_BYTES);
   void* scratch = nullptr;
-  const int rc = attn_static_scratch(&scratch);
+  rc = attn_static_scratch(&scratch);
   if (rc) return rc;
-  return attn_run(n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v, d_slot, d_len, d_out,
-                  scratch, (cudaStream_t)stream);
+  return attn_run(n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v, KV_F32, d_slot, d_len,
+                  d_out, scratch, TN_ATTENTION_STATIC_SCRATCH_BYTES, (cudaStream_t)stream);
 }
 
 extern "C" int tn_hop_encode(const float* d_in, uint16_t* d_out, uint64_t n, void* stream) {

@@ -1,0 +1,426 @@
+// tn_attn.cu -- one-query GQA decode attention over the KV cache.
+//
+// The attention of web/inference-worker.js:556-564 (scores q.k / sqrt(hd),
+// softmax over the row's cached positions, weighted sum of V) for T query
+// rows at once, each row over its own sequence slot and length.  The cache
+// holds f32 rows (the reference's format, :554 and :640-653) or, opt-in,
+// fp16 rows (half the bytes; values rounded to nearest even on append).
+//
+// Work split.  CTA (split, KV head, row) streams its share of the row's
+// positions; the split count S is chosen so that the grid fills every SM
+// (one decoding row of an 8-KV-head model is 8 x S CTAs).  Within a CTA each
+// of the 8 warps takes a contiguous part of that share.  A lane holds HD/32
+// dimensions of q for the G query heads of the KV head; a warp step covers
+// PS = 32/G positions: the PS x G partial dot products of a lane are
+// reduce-scattered over the warp so that lane l ends with the full score of
+// (position l / G, head l % G) -- every exp is computed once -- and an online
+// softmax per head rescales the lane's G x HD/32 output accumulators.  The
+// warps merge in shared memory.  With one split the CTA writes the output;
+// otherwise it writes its partial (unnormalised output, running max and sum
+// per head) to a workspace, and the CTA that arrives last at the (row, KV
+// head) -- a release / acquire counter -- merges the S partials in split
+// order (deterministic) and resets the counter for the next launch.
+#include <atomic>
+#include <cfloat>
+
+#include <cuda_fp16.h>
+
+#include "tn_kernels.cuh"
+#include "tn_ptx.cuh"
+
+namespace tn {
+
+constexpr int ATT_WARPS = 8;
+constexpr int ATT_THREADS = ATT_WARPS * 32;
+constexpr int ATT_MAX_SPLITS = 32;
+
+struct AttnArgs {
+  const float* q;
+  int ldq;
+  const void* kc;  // KT elements
+  const void* vc;
+  size_t slot_stride, kvh_stride;  // in elements
+  const RowInfo* rows;
+  int S, nkv;
+  float scale;
+  float* out;
+  int ldo;
+  float* ws;  // partials [row][KV head][split][pstride] (S > 1)
+  int* cnt;   // arrivals per (row, KV head), zero between launches (S > 1)
+  int pstride;
+};
+
+// floats of one partial: G x HD outputs, G maxima, G sums (16-byte multiple)
+__host__ __device__ constexpr int attn_pstride(int G, int HD) { return (G * HD + 2 * G + 3) / 4 * 4; }
+
+// DPL consecutive elements of a cached row, as floats
+template <typename KT, int DPL>
+struct KvVec;
+template <>
+struct KvVec<float, 4> {
+  using Raw = float4;
+  static __device__ __forceinline__ Raw load(const float* p) { return *reinterpret_cast<const float4*>(p); }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[4]) {
+    o[0] = r.x;
+    o[1] = r.y;
+    o[2] = r.z;
+    o[3] = r.w;
+  }
+};
+template <>
+struct KvVec<float, 2> {
+  using Raw = float2;
+  static __device__ __forceinline__ Raw load(const float* p) { return *reinterpret_cast<const float2*>(p); }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[2]) {
+    o[0] = r.x;
+    o[1] = r.y;
+  }
+};
+template <>
+struct KvVec<float, 1> {
+  using Raw = float;
+  static __device__ __forceinline__ Raw load(const float* p) { return *p; }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[1]) { o[0] = r; }
+};
+template <>
+struct KvVec<__half, 4> {
+  using Raw = uint2;
+  static __device__ __forceinline__ Raw load(const __half* p) { return *reinterpret_cast<const uint2*>(p); }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[4]) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&r.y));
+    o[0] = a.x;
+    o[1] = a.y;
+    o[2] = b.x;
+    o[3] = b.y;
+  }
+};
+template <>
+struct KvVec<__half, 2> {
+  using Raw = uint32_t;
+  static __device__ __forceinline__ Raw load(const __half* p) { return *reinterpret_cast<const uint32_t*>(p); }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[2]) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&r));
+    o[0] = a.x;
+    o[1] = a.y;
+  }
+};
+template <>
+struct KvVec<__half, 1> {
+  using Raw = __half;
+  static __device__ __forceinline__ Raw load(const __half* p) { return *p; }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[1]) { o[0] = __half2float(r); }
+};
+
+// after the loop lane holds the warp sum of v[lane >> (5 - log2 N)]
+template <int N>
+__device__ __forceinline__ float attn_reduce_scatter(float (&v)[N], int lane) {
+#pragma unroll
+  for (int n = N, o = 16; n > 1; n >>= 1, o >>= 1) {
+    const bool upper = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; i++) {
+      const float send = upper ? v[i] : v[i + n / 2];
+      const float keep = upper ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  constexpr int LOGN = N == 1 ? 0 : (N == 2 ? 1 : (N == 4 ? 2 : (N == 8 ? 3 : (N == 16 ? 4 : 5))));
+  float r = v[0];
+#pragma unroll
+  for (int o = 16 >> LOGN; o >= 1; o >>= 1) r += __shfl_xor_sync(0xffffffffu, r, o);
+  return r;
+}
+
+template <int HD, int G, typename KT>
+__global__ void __launch_bounds__(ATT_THREADS) k_attn(const AttnArgs a) {
+  constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD;
+  using Vec = KvVec<KT, DPL>;
+  using Raw = typename Vec::Raw;
+  // prefetch the next step's K / V rows when they fit in 16 registers each
+  constexpr bool PF = PS * (((int)sizeof(Raw) + 3) / 4) <= 16;
+  constexpr unsigned FULL = 0xffffffffu;
+  __shared__ float s_m[ATT_WARPS][G], s_l[ATT_WARPS][G];
+  __shared__ __align__(16) float s_o[ATT_WARPS][GH];
+  __shared__ float s_w[ATT_WARPS][G];  // merge weights exp(m - M) of the warps
+  __shared__ float s_M[G], s_L[G];
+  __shared__ float s_part[2][ATT_MAX_SPLITS][G];  // the splits' maxima and sums (last arriver)
+  __shared__ int s_last;
+  // grid.x = (row, KV head, split), splits innermost
+  const int S = a.S;
+  const int split = (int)(blockIdx.x % S), kvh = (int)((blockIdx.x / S) % a.nkv), t = (int)(blockIdx.x / (S * a.nkv));
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  pdl_launch_dependents();
+  pdl_wait();  // q and the cache rows of this step come from the previous kernels
+  const RowInfo ri = a.rows[t];
+  const int L = ri.len;
+  const int lo = (int)((int64_t)L * split / S), hi = (int)((int64_t)L * (split + 1) / S);
+  const int wlo = lo + (int)((int64_t)(hi - lo) * warp / ATT_WARPS);
+  const int whi = lo + (int)((int64_t)(hi - lo) * (warp + 1) / ATT_WARPS);
+  const KT* kb = reinterpret_cast<const KT*>(a.kc) + ri.slot * a.slot_stride + kvh * a.kvh_stride + lane * DPL;
+  const KT* vb = reinterpret_cast<const KT*>(a.vc) + ri.slot * a.slot_stride + kvh * a.kvh_stride + lane * DPL;
+
+  float qr[G][DPL], acc[G][DPL];
+#pragma unroll
+  for (int h = 0; h < G; h++)
+#pragma unroll
+    for (int d = 0; d < DPL; d++) {
+      qr[h][d] = a.q[(size_t)t * a.ldq + (kvh * G + h) * HD + lane * DPL + d];
+      acc[h][d] = 0.f;
+    }
+  // this lane's (head, position) after the reduce-scatter; its head's running
+  // max / sum live in every lane of that head
+  const int my_p = lane / G;
+  float m_run = -INFINITY, l_run = 0.f;
+  Raw kn[PF ? PS : 1], vn[PF ? PS : 1];
+  auto load_step = [&](int p0, Raw (&kd)[PF ? PS : 1], Raw (&vd)[PF ? PS : 1]) {
+#pragma unroll
+    for (int i = 0; i < (PF ? PS : 1); i++) {
+      const int p = min(p0 + i, whi - 1);  // past the end: a valid row, masked below
+      kd[i] = Vec::load(kb + (size_t)p * HD);
+      vd[i] = Vec::load(vb + (size_t)p * HD);
+    }
+  };
+  if (PF && wlo < whi) load_step(wlo, kn, vn);
+  for (int p0 = wlo; p0 < whi; p0 += PS) {
+    float kr[PS][DPL], vr[PS][DPL];
+    if constexpr (PF) {
+#pragma unroll
+      for (int i = 0; i < PS; i++) {
+        Vec::cvt(kn[i % (PF ? PS : 1)], kr[i]);
+        Vec::cvt(vn[i % (PF ? PS : 1)], vr[i]);
+      }
+      if (p0 + PS < whi) load_step(p0 + PS, kn, vn);
+    } else {
+      Raw kw[PS], vw[PS];
+#pragma unroll
+      for (int i = 0; i < PS; i++) {
+        const int p = min(p0 + i, whi - 1);
+        kw[i] = Vec::load(kb + (size_t)p * HD);
+        vw[i] = Vec::load(vb + (size_t)p * HD);
+      }
+#pragma unroll
+      for (int i = 0; i < PS; i++) {
+        Vec::cvt(kw[i], kr[i]);
+        Vec::cvt(vw[i], vr[i]);
+      }
+    }
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < PS; i++)
+#pragma unroll
+      for (int h = 0; h < G; h++) {
+        float s = 0.f;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) s = fmaf(qr[h][d], kr[i][d], s);
+        v[i * G + h] = s;
+      }
+    const float sc = attn_reduce_scatter<32>(v, lane) * a.scale;
+    const float s = p0 + my_p < whi ? sc : -INFINITY;
+    float mx = s;
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
+    const float m_new = fmaxf(m_run, mx);  // finite: position p0 is always valid
+    const float p = s == -INFINITY ? 0.f : expf(s - m_new);
+    const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
+    float ps = p;
+#pragma unroll
+    for (int o = G; o < 32; o <<= 1) ps += __shfl_xor_sync(FULL, ps, o);
+    l_run = l_run * alpha + ps;
+    m_run = m_new;
+#pragma unroll
+    for (int h = 0; h < G; h++) {
+      const float al = __shfl_sync(FULL, alpha, h);
+#pragma unroll
+      for (int d = 0; d < DPL; d++) acc[h][d] *= al;
+    }
+#pragma unroll
+    for (int i = 0; i < PS; i++)
+#pragma unroll
+      for (int h = 0; h < G; h++) {
+        const float w = __shfl_sync(FULL, p, i * G + h);
+#pragma unroll
+        for (int d = 0; d < DPL; d++) acc[h][d] = fmaf(w, vr[i][d], acc[h][d]);
+      }
+  }
+  // merge the warps: the CTA's partial is the output relative to its
+  // per-head max M, with the sum L
+  if (lane < G) {
+    s_m[warp][lane] = m_run;
+    s_l[warp][lane] = l_run;
+  }
+#pragma unroll
+  for (int h = 0; h < G; h++)
+#pragma unroll
+    for (int d = 0; d < DPL; d++) s_o[warp][h * HD + lane * DPL + d] = acc[h][d];
+  __syncthreads();
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, s_m[w][tid]);
+    float Lsum = 0.f;
+    for (int w = 0; w < ATT_WARPS; w++) {
+      const float f = s_m[w][tid] == -INFINITY ? 0.f : expf(s_m[w][tid] - M);
+      s_w[w][tid] = f;
+      Lsum += s_l[w][tid] * f;
+    }
+    s_M[tid] = M;
+    s_L[tid] = Lsum;
+  }
+  __syncthreads();
+  const size_t pbase = ((size_t)t * a.nkv + kvh) * S;  // this (row, KV head)'s first partial
+  float* const wp = a.ws + (pbase + split) * a.pstride;
+  for (int e = tid; e < GH; e += ATT_THREADS) {
+    const int h = e / HD;
+    float o = 0.f;
+    for (int w = 0; w < ATT_WARPS; w++) o = fmaf(s_o[w][e], s_w[w][h], o);
+    if (S == 1) a.out[(size_t)t * a.ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
+    else wp[e] = o;
+  }
+  if (S == 1) return;
+  if (tid < G) {
+    wp[GH + tid] = s_M[tid];
+    wp[GH + G + tid] = s_L[tid];
+  }
+  // publish the partial; the last of the S CTAs to arrive merges
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atom_add_acq_rel(a.cnt + (size_t)t * a.nkv + kvh, 1) == S - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* w0 = a.ws + pbase * a.pstride;
+  for (int i = tid; i < 2 * S * G; i += ATT_THREADS) {
+    const int c = i / (2 * G), r = i % (2 * G);
+    s_part[r / G][c][r % G] = __ldcg(w0 + (size_t)c * a.pstride + GH + r);
+  }
+  __syncthreads();
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int c = 0; c < S; c++) M = fmaxf(M, s_part[0][c][tid]);
+    float Lsum = 0.f;
+    for (int c = 0; c < S; c++) {
+      const float mc = s_part[0][c][tid];
+      const float f = mc == -INFINITY ? 0.f : expf(mc - M);
+      Lsum += s_part[1][c][tid] * f;
+      s_part[0][c][tid] = f;  // (column tid is read and rewritten by this thread only)
+    }
+    s_L[tid] = Lsum;
+  }
+  __syncthreads();
+  for (int e = tid; e < GH; e += ATT_THREADS) {
+    const int h = e / HD;
+    float o = 0.f;
+    for (int c0 = 0; c0 < S; c0 += 8) {
+      float pv[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) pv[j] = c0 + j < S ? __ldcg(w0 + (size_t)(c0 + j) * a.pstride + e) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+        if (c0 + j < S) o = fmaf(pv[j], s_part[0][c0 + j][h], o);
+    }
+    a.out[(size_t)t * a.ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
+  }
+  if (tid == 0) a.cnt[(size_t)t * a.nkv + kvh] = 0;  // ready for the next launch
+}
+
+// ---------------------------------------------------------------- host side
+using AttnLaunch = cudaError_t (*)(const AttnArgs&, dim3, cudaStream_t);
+struct AttnKernel {
+  const void* fn = nullptr;
+  AttnLaunch launch = nullptr;
+};
+
+template <int HD, int G, typename KT>
+static cudaError_t attn_launch_t(const AttnArgs& a, dim3 grid, cudaStream_t s) {
+  return launch_pdl(k_attn<HD, G, KT>, grid, dim3(ATT_THREADS), 0, s, a);
+}
+template <int HD, int G, typename KT>
+static AttnKernel attn_k() {
+  return AttnKernel{(const void*)k_attn<HD, G, KT>, attn_launch_t<HD, G, KT>};
+}
+template <int HD, typename KT>
+static bool attn_kernel_hd(int G, AttnKernel* k) {
+  switch (G) {
+    case 1: *k = attn_k<HD, 1, KT>(); return true;
+    case 2: *k = attn_k<HD, 2, KT>(); return true;
+    case 4: *k = attn_k<HD, 4, KT>(); return true;
+    case 8: *k = attn_k<HD, 8, KT>(); return true;
+    case 16:
+      if (HD > 64) return false;  // 16 x 128 accumulators do not fit a lane
+      *k = attn_k<(HD > 64 ? 64 : HD), 16, KT>();
+      return true;
+    default: return false;
+  }
+}
+template <typename KT>
+static bool attn_kernel_kt(int hd, int G, AttnKernel* k) {
+  switch (hd) {
+    case 32: return attn_kernel_hd<32, KT>(G, k);
+    case 64: return attn_kernel_hd<64, KT>(G, k);
+    case 128: return attn_kernel_hd<128, KT>(G, k);
+    default: return false;
+  }
+}
+static bool attn_kernel(int hd, int G, int kv_type, AttnKernel* k) {
+  return kv_type == KV_F16 ? attn_kernel_kt<__half>(hd, G, k) : attn_kernel_kt<float>(hd, G, k);
+}
+
+// resident CTAs per SM of a variant (looked up once per variant)
+static int attn_occupancy(int hd, int G, int kv_type) {
+  static std::atomic<int> cache[3][5][2];
+  const int hi = hd == 32 ? 0 : hd == 64 ? 1 : 2, gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : G == 8 ? 3 : 4;
+  std::atomic<int>& c = cache[hi][gi][kv_type == KV_F16 ? 1 : 0];
+  int o = c.load(std::memory_order_relaxed);
+  if (o > 0) return o;
+  AttnKernel k;
+  o = 1;
+  if (attn_kernel(hd, G, kv_type, &k) &&
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k.fn, ATT_THREADS, 0) != cudaSuccess) {
+    cudaGetLastError();
+    o = 1;
+  }
+  o = std::max(1, o);
+  c.store(o, std::memory_order_relaxed);
+  return o;
+}
+
+AttnPlan attn_plan(int T, int nH, int nKV, int hd, int max_ctx, int kv_type, size_t ws_cap_floats) {
+  AttnPlan p;
+  if (T <= 0 || nKV <= 0 || nH % nKV != 0) return p;
+  const int G = nH / nKV, PS = 32 / std::max(1, std::min(G, 32));
+  // splits so that the grid covers every SM's resident CTAs once, each split
+  // at least one warp step per warp of the longest row
+  const int64_t rows_kv = (int64_t)T * nKV;
+  const int64_t target = (int64_t)attn_occupancy(hd, G, kv_type) * num_sms();
+  int S = (int)std::max<int64_t>(1, (target + rows_kv - 1) / rows_kv);
+  S = std::min(S, std::max(1, (max_ctx + ATT_WARPS * PS - 1) / (ATT_WARPS * PS)));
+  S = std::min(S, ATT_MAX_SPLITS);
+  const size_t per = (size_t)rows_kv * attn_pstride(G, hd);
+  while (S > 1 && per * S > ws_cap_floats) S--;
+  p.splits = S;
+  p.ws_floats = S > 1 ? per * S : 0;
+  p.cnt_ints = S > 1 ? (size_t)rows_kv : 0;
+  return p;
+}
+
+int attention(const float* q, int ldq, const void* kc, const void* vc, int kv_type, size_t slot_stride,
+              size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, const AttnPlan& plan,
+              float* out, int ldo, float* ws, int* cnt, cudaStream_t s) {
+  if (T <= 0) return TN_OK;
+  TN_REQUIRE(nKV > 0 && nH % nKV == 0, TN_EUNSUPPORTED, "attention: n_heads %% n_kv_heads != 0");
+  TN_REQUIRE(plan.splits >= 1 && plan.splits <= ATT_MAX_SPLITS, TN_EINVAL, "attention: %d splits", plan.splits);
+  TN_REQUIRE(plan.splits == 1 || (ws && cnt), TN_EINVAL, "attention: split workspace missing");
+  const int G = nH / nKV;
+  AttnKernel k;
+  if (!attn_kernel(hd, G, kv_type, &k)) {
+    set_error("attention: %d query heads per KV head with head_dim %d unsupported", G, hd);
+    return TN_EUNSUPPORTED;
+  }
+  const AttnArgs a{q,   ldq, kc,  vc,         slot_stride, kvh_stride, rows, plan.splits, nKV, (float)(1.0 / sqrt((double)hd)),
+                   out, ldo, ws, cnt, attn_pstride(G, hd)};
+  const dim3 grid((unsigned)((int64_t)plan.splits * nKV * T));
+  TN_CHECK_CUDA(k.launch(a, grid, s));
+  return TN_OK;
+}
+
+}  // namespace tn

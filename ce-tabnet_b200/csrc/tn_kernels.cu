@@ -7,11 +7,7 @@
 // rotation, softmax normaliser of the sampler) are evaluated in double here too.
 #include <cfloat>
 
-#include <cooperative_groups.h>
-
 #include "tn_kernels.cuh"
-
-namespace cg = cooperative_groups;
 
 namespace tn {
 
@@ -602,9 +598,9 @@ int rope_table(const RowInfo* rows, const double* freq, int half, int T, double2
 // ropeCpu (web/inference-worker.js:528-540) on q and k, then the KV push of
 // :554 into the cache at the row's KV index.  Rotations in double, unfused.
 __global__ void k_rope_kv(const float* __restrict__ qkv, int ldqkv, const RowInfo* __restrict__ rows,
-                          const double2* __restrict__ cs, float* __restrict__ q_out,
-                          float* __restrict__ kc, float* __restrict__ vc, size_t slot_stride,
-                          size_t kvh_stride, int nH, int nKV, int hd) {
+                          const double2* __restrict__ cs, float* __restrict__ q_out, void* __restrict__ kc,
+                          void* __restrict__ vc, int kv_type, size_t slot_stride, size_t kvh_stride, int nH,
+                          int nKV, int hd) {
   const int t = blockIdx.x;
   const RowInfo ri = rows[t];
   const int half = hd >> 1, qDim = nH * hd, kvDim = nKV * hd;
@@ -627,271 +623,24 @@ __global__ void k_rope_kv(const float* __restrict__ qkv, int ldqkv, const RowInf
         qo[i] = o0;
         qo[half + i] = o1;
       } else {
-        float* ko = kc + ri.slot * slot_stride + head * kvh_stride + (size_t)ri.kv_idx * hd;
-        ko[i] = o0;
-        ko[half + i] = o1;
+        const size_t ko = ri.slot * slot_stride + head * kvh_stride + (size_t)ri.kv_idx * hd;
+        kv_store(kc, ko + i, kv_type, o0);
+        kv_store(kc, ko + half + i, kv_type, o1);
       }
     } else {
       const int d = k - nq - nk, head = d / hd, e = d % hd;
-      vc[ri.slot * slot_stride + head * kvh_stride + (size_t)ri.kv_idx * hd + e] =
-          src[qDim + kvDim + d];
+      kv_store(vc, ri.slot * slot_stride + head * kvh_stride + (size_t)ri.kv_idx * hd + e, kv_type,
+               src[qDim + kvDim + d]);
     }
   }
 }
 
-int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs, float* q_out, float* kc,
-            float* vc, size_t slot_stride, size_t kvh_stride, int nH, int nKV, int hd, int T,
-            cudaStream_t s) {
+int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs, float* q_out, void* kc, void* vc,
+            int kv_type, size_t slot_stride, size_t kvh_stride, int nH, int nKV, int hd, int T, cudaStream_t s) {
   if (T <= 0) return TN_OK;
-  k_rope_kv<<<T, 256, 0, s>>>(qkv, ldqkv, rows, cs, q_out, kc, vc, slot_stride, kvh_stride, nH, nKV, hd);
+  k_rope_kv<<<T, 256, 0, s>>>(qkv, ldqkv, rows, cs, q_out, kc, vc, kv_type, slot_stride, kvh_stride, nH, nKV, hd);
   TN_CHECK_LAUNCH();
   return TN_OK;
-}
-
-// ================================================================ attention
-// One-query GQA attention (web/inference-worker.js:556-564) for T rows in one
-// kernel.  CTA (split, KV head, row) takes its share of the row's cached
-// positions, and each of its 8 warps a contiguous part of that share.  A lane
-// holds HD/32 dimensions of q for the G query heads of the KV head; a warp
-// step covers PS = 32/G positions: the PS x G partial dot products of a lane
-// are reduce-scattered over the warp so that lane l ends with the full score
-// of (position l / G, head l % G) -- every exp is computed once -- and an
-// online softmax per head rescales the lane's G x HD/32 output accumulators.
-// The warps merge in shared memory; with several splits, the splits of a
-// (row, KV head) run as one thread-block cluster and merge through
-// distributed shared memory, in split order (deterministic).
-constexpr int ATT_WARPS = 8;
-
-template <int HD, int G>
-__global__ void __launch_bounds__(ATT_WARPS * 32)
-    k_attn(const float* __restrict__ q, int ldq, const float* __restrict__ kc, const float* __restrict__ vc,
-           size_t slot_stride, size_t kvh_stride, const RowInfo* __restrict__ rows, int S, int nkv, float scale,
-           float* __restrict__ out, int ldo) {
-  constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD;
-  constexpr unsigned FULL = 0xffffffffu;
-  __shared__ float s_m[ATT_WARPS][G], s_l[ATT_WARPS][G];
-  __shared__ __align__(16) float s_o[ATT_WARPS][GH];
-  __shared__ float s_w[ATT_WARPS][G];  // merge weights exp(m - M) of the warps
-  __shared__ float s_M[G], s_L[G];
-  // grid.x = (row, KV head, split), splits innermost: the S splits of a
-  // (row, KV head) are one cluster, and rows are not bounded by gridDim.z
-  const int split = (int)(blockIdx.x % S), kvh = (int)((blockIdx.x / S) % nkv), t = (int)(blockIdx.x / (S * nkv));
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  pdl_launch_dependents();
-  pdl_wait();  // q and the cache rows of this step come from the previous kernels
-  const RowInfo ri = rows[t];
-  const int L = ri.len;
-  const int lo = (int)((int64_t)L * split / S), hi = (int)((int64_t)L * (split + 1) / S);
-  const int wlo = lo + (int)((int64_t)(hi - lo) * warp / ATT_WARPS);
-  const int whi = lo + (int)((int64_t)(hi - lo) * (warp + 1) / ATT_WARPS);
-  const float* kb = kc + ri.slot * slot_stride + kvh * kvh_stride + lane * DPL;
-  const float* vb = vc + ri.slot * slot_stride + kvh * kvh_stride + lane * DPL;
-
-  float qr[G][DPL], acc[G][DPL];
-#pragma unroll
-  for (int h = 0; h < G; h++)
-#pragma unroll
-    for (int d = 0; d < DPL; d++) {
-      qr[h][d] = q[(size_t)t * ldq + (kvh * G + h) * HD + lane * DPL + d];
-      acc[h][d] = 0.f;
-    }
-  auto load_row = [&](const float* base, int p, float (&r)[DPL]) {
-    if (DPL == 4) {
-      const float4 v = *reinterpret_cast<const float4*>(base + (size_t)p * HD);
-      r[0] = v.x;
-      r[DPL > 1 ? 1 : 0] = v.y;
-      r[DPL > 2 ? 2 : 0] = v.z;
-      r[DPL > 3 ? 3 : 0] = v.w;
-    } else if (DPL == 2) {
-      const float2 v = *reinterpret_cast<const float2*>(base + (size_t)p * HD);
-      r[0] = v.x;
-      r[DPL > 1 ? 1 : 0] = v.y;
-    } else {
-      r[0] = base[(size_t)p * HD];
-    }
-  };
-  // this lane's (head, position) after the reduce-scatter; its head's running
-  // max / sum live in every lane of that head
-  const int my_p = lane / G;
-  float m_run = -INFINITY, l_run = 0.f;
-  // when a step's rows fit in registers twice, the next step's K / V rows are
-  // loaded while the current step computes
-  constexpr bool PF = PS * DPL <= 16;
-  float kn[PF ? PS : 1][DPL], vn[PF ? PS : 1][DPL];
-  auto load_step = [&](int p0, float (&kd)[PF ? PS : 1][DPL], float (&vd)[PF ? PS : 1][DPL]) {
-#pragma unroll
-    for (int i = 0; i < (PF ? PS : 1); i++) {
-      const int p = min(p0 + i, whi - 1);  // past the end: a valid row, masked below
-      load_row(kb, p, kd[i]);
-      load_row(vb, p, vd[i]);
-    }
-  };
-  if (PF && wlo < whi) load_step(wlo, kn, vn);
-  for (int p0 = wlo; p0 < whi; p0 += PS) {
-    float kr[PS][DPL], vr[PS][DPL];
-    if constexpr (PF) {
-#pragma unroll
-      for (int i = 0; i < PS; i++)
-#pragma unroll
-        for (int d = 0; d < DPL; d++) {
-          kr[i][d] = kn[i % (PF ? PS : 1)][d];
-          vr[i][d] = vn[i % (PF ? PS : 1)][d];
-        }
-      if (p0 + PS < whi) load_step(p0 + PS, kn, vn);
-    } else {
-#pragma unroll
-      for (int i = 0; i < PS; i++) {
-        const int p = min(p0 + i, whi - 1);
-        load_row(kb, p, kr[i]);
-        load_row(vb, p, vr[i]);
-      }
-    }
-    float v[32];
-#pragma unroll
-    for (int i = 0; i < PS; i++)
-#pragma unroll
-      for (int h = 0; h < G; h++) {
-        float s = 0.f;
-#pragma unroll
-        for (int d = 0; d < DPL; d++) s = fmaf(qr[h][d], kr[i][d], s);
-        v[i * G + h] = s;
-      }
-    const float sc = warp_reduce_scatter<32>(v, lane) * scale;
-    const float s = p0 + my_p < whi ? sc : -INFINITY;
-    float mx = s;
-#pragma unroll
-    for (int o = G; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(FULL, mx, o));
-    const float m_new = fmaxf(m_run, mx);  // finite: position p0 is always valid
-    const float p = s == -INFINITY ? 0.f : expf(s - m_new);
-    const float alpha = m_run == -INFINITY ? 0.f : expf(m_run - m_new);
-    float ps = p;
-#pragma unroll
-    for (int o = G; o < 32; o <<= 1) ps += __shfl_xor_sync(FULL, ps, o);
-    l_run = l_run * alpha + ps;
-    m_run = m_new;
-#pragma unroll
-    for (int h = 0; h < G; h++) {
-      const float a = __shfl_sync(FULL, alpha, h);
-#pragma unroll
-      for (int d = 0; d < DPL; d++) acc[h][d] *= a;
-    }
-#pragma unroll
-    for (int i = 0; i < PS; i++)
-#pragma unroll
-      for (int h = 0; h < G; h++) {
-        const float w = __shfl_sync(FULL, p, i * G + h);
-#pragma unroll
-        for (int d = 0; d < DPL; d++) acc[h][d] = fmaf(w, vr[i][d], acc[h][d]);
-      }
-  }
-  // merge the warps; the CTA's partial (unnormalised output relative to its
-  // per-head max, the max, the sum) stays in shared memory
-  if (lane < G) {
-    s_m[warp][lane] = m_run;
-    s_l[warp][lane] = l_run;
-  }
-#pragma unroll
-  for (int h = 0; h < G; h++)
-#pragma unroll
-    for (int d = 0; d < DPL; d++) s_o[warp][h * HD + lane * DPL + d] = acc[h][d];
-  __syncthreads();
-  if (tid < G) {
-    float M = -INFINITY;
-    for (int w = 0; w < ATT_WARPS; w++) M = fmaxf(M, s_m[w][tid]);
-    float Lsum = 0.f;
-    for (int w = 0; w < ATT_WARPS; w++) {
-      const float f = s_m[w][tid] == -INFINITY ? 0.f : expf(s_m[w][tid] - M);
-      s_w[w][tid] = f;
-      Lsum += s_l[w][tid] * f;
-    }
-    s_M[tid] = M;
-    s_L[tid] = Lsum;
-  }
-  __syncthreads();
-  float* const c_o = s_o[0];  // element e is read and rewritten by one thread only
-  for (int e = tid; e < GH; e += ATT_WARPS * 32) {
-    const int h = e / HD;
-    float o = 0.f;
-    for (int w = 0; w < ATT_WARPS; w++) o = fmaf(s_o[w][e], s_w[w][h], o);
-    if (S == 1) out[(size_t)t * ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
-    else c_o[e] = o;
-  }
-  if (S == 1) return;
-  // The splits of this (row, KV head) are one thread-block cluster: after the
-  // barrier, split r finalises outputs [r GH / S, (r + 1) GH / S) from every
-  // split's partial, read from the others' shared memory in split order.
-  cg::cluster_group cluster = cg::this_cluster();
-  cluster.sync();
-  for (int e = GH * split / S + tid; e < GH * (split + 1) / S; e += ATT_WARPS * 32) {
-    const int h = e / HD;
-    float M = -INFINITY;
-    for (int c = 0; c < S; c++) M = fmaxf(M, *cluster.map_shared_rank(&s_M[h], c));
-    float Lsum = 0.f, o = 0.f;
-    for (int c = 0; c < S; c++) {
-      const float mc = *cluster.map_shared_rank(&s_M[h], c);
-      const float f = mc == -INFINITY ? 0.f : expf(mc - M);
-      Lsum += *cluster.map_shared_rank(&s_L[h], c) * f;
-      o = fmaf(*cluster.map_shared_rank(&c_o[e], c), f, o);
-    }
-    out[(size_t)t * ldo + (kvh * G + h) * HD + e % HD] = Lsum > 0.f ? o / Lsum : 0.f;
-  }
-  cluster.sync();  // no CTA leaves while another still reads its shared memory
-}
-
-int attn_splits(int T, int nKV, int max_ctx) {
-  // about one CTA per SM, at least 128 positions of the longest row per split,
-  // at most a portable cluster (8) of splits
-  const int want = (num_sms() + T * nKV - 1) / (T * nKV);
-  const int cap = std::max(1, std::min(8, (max_ctx + 127) / 128));
-  return std::max(1, std::min(want, cap));
-}
-
-template <int HD>
-static int launch_attn_hd(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
-                          size_t kvh_stride, const RowInfo* rows, int T, int nKV, int G, int n_splits, float* out,
-                          int ldo, cudaStream_t s) {
-  const dim3 grid((unsigned)(n_splits * nKV * T));
-  const float scale = (float)(1.0 / sqrt((double)HD));
-  cudaError_t e;
-  switch (G) {
-#define TN_ATT_CASE(g)                                                                                          \
-  case g:                                                                                                       \
-    e = launch_pdl_cluster(k_attn<HD, g>, grid, dim3(ATT_WARPS * 32), 0, n_splits, s, q, ldq, kc, vc,       \
-                           slot_stride, kvh_stride, rows, n_splits, nKV, scale, out, ldo);                       \
-    break;
-    TN_ATT_CASE(1)
-    TN_ATT_CASE(2)
-    TN_ATT_CASE(4)
-    TN_ATT_CASE(8)
-#undef TN_ATT_CASE
-    case 16:
-      if (HD <= 64) {
-        e = launch_pdl_cluster(k_attn<HD <= 64 ? HD : 64, 16>, grid, dim3(ATT_WARPS * 32), 0, n_splits, s, q, ldq,
-                               kc, vc, slot_stride, kvh_stride, rows, n_splits, nKV, scale, out, ldo);
-        break;
-      }
-      [[fallthrough]];
-    default:
-      set_error("attention: %d query heads per KV head with head_dim %d unsupported", G, HD);
-      return TN_EUNSUPPORTED;
-  }
-  TN_CHECK_CUDA(e);
-  return TN_OK;
-}
-
-int attention(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
-              size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, int n_splits,
-              float* out, int ldo, cudaStream_t s) {
-  if (T <= 0) return TN_OK;
-  TN_REQUIRE(nH % nKV == 0, TN_EUNSUPPORTED, "attention: n_heads %% n_kv_heads != 0");
-  TN_REQUIRE(n_splits >= 1 && n_splits <= 8, TN_EINVAL, "attention: %d splits", n_splits);
-  const int G = nH / nKV;
-  switch (hd) {
-    case 32: return launch_attn_hd<32>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, s);
-    case 64: return launch_attn_hd<64>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, s);
-    case 128: return launch_attn_hd<128>(q, ldq, kc, vc, slot_stride, kvh_stride, rows, T, nKV, G, n_splits, out, ldo, s);
-    default: set_error("attention: head_dim %d unsupported", hd); return TN_EUNSUPPORTED;
-  }
 }
 
 // ================================================================ hop codec

@@ -3,6 +3,8 @@
 
 #include <cuda.h>  // CUtensorMap (the encoder is fetched from the driver at run time)
 
+#include <cuda_fp16.h>
+
 #include "tn_common.cuh"
 
 namespace tn {
@@ -154,6 +156,15 @@ size_t gemm_counter_offset(int T, int cols);
 int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, float* y, int ldy, int mode,
          void* scratch, size_t scratch_bytes, int* err, cudaStream_t s);
 
+// Element type of a KV cache: f32 (the reference's rows) or, opt-in, fp16
+// (rounded to nearest even when appended).
+enum KvType { KV_F32 = 0, KV_F16 = 1 };
+__host__ __device__ constexpr size_t kv_elem_bytes(int kv_type) { return kv_type == KV_F16 ? 2 : 4; }
+__device__ __forceinline__ void kv_store(void* base, size_t i, int kv_type, float v) {
+  if (kv_type == KV_F16) reinterpret_cast<__half*>(base)[i] = __float2half_rn(v);
+  else reinterpret_cast<float*>(base)[i] = v;
+}
+
 // per-row bookkeeping of a step: KV slot, RoPE position, KV write index, attention length
 struct RowInfo {
   int slot, pos, kv_idx, len;
@@ -175,8 +186,9 @@ struct MvFuse {
   const RowInfo* rinfo = nullptr;
   const double2* cs = nullptr;
   float* q_out = nullptr;
-  float* kc = nullptr;
-  float* vc = nullptr;
+  void* kc = nullptr;  // kv_type elements
+  void* vc = nullptr;
+  int kv_type = KV_F32;
   size_t slot_stride = 0, kvh_stride = 0;
   int q_dim = 0, kv_dim = 0, hd = 0;
 };
@@ -191,17 +203,25 @@ int embed_rows(const Matrix& emb, const int* ids, int T, float* out, int ldo, in
                cudaStream_t s);
 int rope_table(const RowInfo* rows, const double* freq, int half, int T, double2* cs, cudaStream_t s);
 int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs, float* q_out,
-            float* kc, float* vc, size_t slot_stride, size_t kvh_stride, int nH, int nKV, int hd, int T,
-            cudaStream_t s);
+            void* kc, void* vc, int kv_type, size_t slot_stride, size_t kvh_stride, int nH, int nKV, int hd,
+            int T, cudaStream_t s);
 
 // One-query GQA attention (web/inference-worker.js:556-564) for T rows, one
-// kernel: CTA (split, KV head, row) over its share of the row's positions;
-// the splits of a (row, KV head) form a thread-block cluster and merge in
-// split order through distributed shared memory (n_splits <= 8).
-int attn_splits(int T, int nKV, int max_ctx);
-int attention(const float* q, int ldq, const float* kc, const float* vc, size_t slot_stride,
-              size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, int n_splits,
-              float* out, int ldo, cudaStream_t s);
+// kernel (tn_attn.cu): CTA (split, KV head, row) over its share of the row's
+// positions; with several splits the last CTA of a (row, KV head) to finish
+// merges the partials from a workspace in split order.
+struct AttnPlan {
+  int splits = 1;
+  size_t ws_floats = 0;  // partials of the split rows
+  size_t cnt_ints = 0;   // arrival counters, zero between launches
+};
+// splits for T rows over caches of up to max_ctx positions; a workspace of at
+// most ws_cap_floats floats bounds them
+AttnPlan attn_plan(int T, int nH, int nKV, int hd, int max_ctx, int kv_type, size_t ws_cap_floats = SIZE_MAX);
+// kc / vc: kv_type elements; strides in elements
+int attention(const float* q, int ldq, const void* kc, const void* vc, int kv_type, size_t slot_stride,
+              size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, const AttnPlan& plan,
+              float* out, int ldo, float* ws, int* cnt, cudaStream_t s);
 
 int hop_encode_rows(const float* h, int ldh, const int* rowsel, int T, int H, uint16_t* out,
                     cudaStream_t s);

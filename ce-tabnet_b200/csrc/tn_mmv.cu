@@ -113,13 +113,19 @@ __device__ __forceinline__ void mmv_store(const MmvArgs& a, int row, int tt, flo
       const double av = v, bv = partner;
       const float o0 = (float)__dsub_rn(__dmul_rn(av, c.x), __dmul_rn(bv, c.y));
       const float o1 = (float)__dadd_rn(__dmul_rn(av, c.y), __dmul_rn(bv, c.x));
-      float* dst = isq ? f.q_out + (size_t)tt * f.q_dim + head * f.hd
-                       : f.kc + ri.slot * f.slot_stride + head * f.kvh_stride + (size_t)ri.kv_idx * f.hd;
-      dst[i] = o0;
-      dst[half + i] = o1;
+      if (isq) {
+        float* dst = f.q_out + (size_t)tt * f.q_dim + head * f.hd;
+        dst[i] = o0;
+        dst[half + i] = o1;
+      } else {
+        const size_t ko = ri.slot * f.slot_stride + head * f.kvh_stride + (size_t)ri.kv_idx * f.hd;
+        kv_store(f.kc, ko + i, f.kv_type, o0);
+        kv_store(f.kc, ko + half + i, f.kv_type, o1);
+      }
     } else {
       const int dv = row - f.q_dim - f.kv_dim;
-      f.vc[ri.slot * f.slot_stride + (dv / f.hd) * f.kvh_stride + (size_t)ri.kv_idx * f.hd + dv % f.hd] = v;
+      kv_store(f.vc, ri.slot * f.slot_stride + (dv / f.hd) * f.kvh_stride + (size_t)ri.kv_idx * f.hd + dv % f.hd,
+               f.kv_type, v);
     }
   }
 }

@@ -84,8 +84,13 @@ struct tn_stage {
   Matrix embed, lm_head;
   float* final_norm = nullptr;
   // KV arena
-  float* kc = nullptr;
-  float* vc = nullptr;
+  char* kc = nullptr;  // kv_type elements
+  char* vc = nullptr;
+  int kv_type = KV_F32;
+  // split-attention partials and arrival counters (zero between launches)
+  float* attn_ws = nullptr;
+  int* attn_cnt = nullptr;
+  size_t attn_ws_floats = 0;
   size_t kvh_stride = 0, layer_stride = 0, slot_stride = 0;
   // activations
   float *h = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *act = nullptr,
@@ -253,6 +258,7 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   st->max_seqs = sp->max_seqs > 0 ? sp->max_seqs : 16;
   st->max_T = sp->max_tokens_per_step > 0 ? sp->max_tokens_per_step : 512;
   st->flags = sp->flags;
+  st->kv_type = (sp->flags & TN_FLAG_KV_F16) ? KV_F16 : KV_F32;
   TN_REQUIRE(st->hd == 32 || st->hd == 64 || st->hd == 128, TN_EUNSUPPORTED,
              "head_dim %d unsupported (32, 64, 128)", st->hd);
   TN_REQUIRE(st->nH % st->nKV == 0 && (st->nH / st->nKV) <= 16 &&
@@ -327,12 +333,13 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   st->slot_stride = st->layer_stride * std::max(1, st->nL);
   const size_t kv_elems = st->slot_stride * st->max_seqs;
   if (st->nL > 0) {
-    cudaError_t e1 = cudaMalloc(&st->kc, kv_elems * sizeof(float));
-    cudaError_t e2 = e1 == cudaSuccess ? cudaMalloc(&st->vc, kv_elems * sizeof(float)) : e1;
+    const size_t eb = kv_elem_bytes(st->kv_type);
+    cudaError_t e1 = cudaMalloc(&st->kc, kv_elems * eb);
+    cudaError_t e2 = e1 == cudaSuccess ? cudaMalloc(&st->vc, kv_elems * eb) : e1;
     TN_REQUIRE(e1 == cudaSuccess && e2 == cudaSuccess, TN_ENOMEM,
-               "KV arena of 2 x %zu bytes (max_seqs %d x max_ctx %d): %s", kv_elems * sizeof(float),
+               "KV arena of 2 x %zu bytes (max_seqs %d x max_ctx %d): %s", kv_elems * eb,
                st->max_seqs, st->max_ctx, cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
-    st->kv_bytes = 2 * kv_elems * sizeof(float);
+    st->kv_bytes = 2 * kv_elems * eb;
   }
 
   // activations for max_T rows
@@ -378,6 +385,18 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
         m->ws = ws;
         m->cnt = cnt;
       }
+  }
+  // split-attention workspace: the largest over every row count of a step
+  {
+    size_t wsf = 0, cnti = 0;
+    for (int t = 1; t <= T; t++) {
+      const AttnPlan p = attn_plan(t, st->nH, st->nKV, st->hd, st->max_ctx, st->kv_type);
+      wsf = std::max(wsf, p.ws_floats);
+      cnti = std::max(cnti, p.cnt_ints);
+    }
+    st->attn_ws_floats = wsf;
+    if (wsf && (rc = dalloc(st, &st->attn_ws, wsf))) return rc;
+    if (cnti && (rc = dalloc(st, &st->attn_cnt, cnti))) return rc;
   }
   if ((rc = dalloc(st, &st->freq, (size_t)(st->hd / 2)))) return rc;
   // RoPE frequencies theta^(-2i/hd) in double (web/inference-worker.js:533)
@@ -464,11 +483,12 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
   else
     TN_STEP_LAUNCH(TN_PROF_OTHER, 1, hop_decode(st->hid_in, (uint64_t)T * H, st->h, s));
   TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1, rope_table(rows, st->freq, st->hd / 2, T, st->cs, s));
-  const int ns = attn_splits(T, st->nKV, st->max_ctx);
+  const AttnPlan ap = attn_plan(T, st->nH, st->nKV, st->hd, st->max_ctx, st->kv_type, st->attn_ws_floats);
+  const size_t eb = kv_elem_bytes(st->kv_type);
   for (int l = 0; l < st->nL; l++) {
     LayerW& L = st->layers[l];
-    float* kc = st->kc + (size_t)l * st->layer_stride;
-    float* vc = st->vc + (size_t)l * st->layer_stride;
+    char* kc = st->kc + (size_t)l * st->layer_stride * eb;
+    char* vc = st->vc + (size_t)l * st->layer_stride * eb;
     // decode-sized steps use the fused decode matvec (RMSNorm prologue,
     // RoPE + KV epilogue, programmatic dependent launches); other steps and
     // matrix formats it does not cover run the separate kernels
@@ -481,6 +501,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       f.q_out = st->q;
       f.kc = kc;
       f.vc = vc;
+      f.kv_type = st->kv_type;
       f.slot_stride = st->slot_stride;
       f.kvh_stride = st->kvh_stride;
       f.q_dim = st->qDim;
@@ -491,12 +512,12 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
       TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
       TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1,
-                     rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->slot_stride, st->kvh_stride, st->nH,
-                             st->nKV, st->hd, T, s));
+                     rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->kv_type, st->slot_stride,
+                             st->kvh_stride, st->nH, st->nKV, st->hd, T, s));
     }
-    TN_STEP_LAUNCH(TN_PROF_ATTENTION, 2,
-                   attention(st->q, st->qDim, kc, vc, st->slot_stride, st->kvh_stride, rows, T, st->nH, st->nKV,
-                             st->hd, ns, st->att, st->qDim, s));
+    TN_STEP_LAUNCH(TN_PROF_ATTENTION, 1,
+                   attention(st->q, st->qDim, kc, vc, st->kv_type, st->slot_stride, st->kvh_stride, rows, T, st->nH,
+                             st->nKV, st->hd, ap, st->att, st->qDim, st->attn_ws, st->attn_cnt, s));
     if (fuse && matvec_dec_ok(L.o, T))
       TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else

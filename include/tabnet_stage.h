@@ -52,6 +52,7 @@ enum { TN_HOP_LAST = 0, TN_HOP_ALL = 1 };
 #define TN_FLAG_NO_GRAPHS (1u << 0) /* never capture decode steps in CUDA graphs */
 #define TN_FLAG_PROFILE (1u << 1)   /* time every kernel launch with CUDA events (tn_stage_profile) */
 #define TN_FLAG_NO_FUSED_DECODE (1u << 2) /* decode steps use the separate norm / matvec / RoPE kernels */
+#define TN_FLAG_KV_F16 (1u << 3)          /* KV cache of fp16 rows (half the bytes; the reference keeps f32) */
 
 /* One layer's packed buffer, tensors in web/inference-worker.js:142-159 order:
  * attn_norm(f16) wq wk wv wo ffn_norm(f16) w_gate w_up w_down. */
@@ -208,14 +209,24 @@ void tn_matrix_free(tn_matrix* m);
  * max_ctx are clamped.  Math of
  * web/inference-worker.js:556-564; d_q, d_out: [n_rows][n_heads*head_dim].
  * d_scratch (device, tn_attention_scratch_bytes() bytes, 256-byte aligned)
- * holds only the row table, 16 bytes a row: the split-K partials merge on
- * chip.  Any row count that fits the caller's buffers is accepted. */
+ * holds the row table (16 bytes a row) and, when few rows leave SMs idle and
+ * each row's positions are split over several CTAs, the splits' arrival
+ * counters and partial results (merged on the device in split order, so the
+ * output is deterministic).  Any row count that fits the caller's buffers is
+ * accepted. */
 uint64_t tn_attention_scratch_bytes(int32_t n_rows, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                                     int32_t max_ctx);
 int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
                  int32_t max_ctx, const float* d_q, const float* d_k, const float* d_v,
                  const int32_t* d_slot, const int32_t* d_len, float* d_out, void* d_scratch,
                  uint64_t scratch_bytes, void* stream);
+/* tn_attention over an fp16 KV cache (IEEE binary16 bits, same layout): the
+ * cache format of stages created with TN_FLAG_KV_F16.  Scores, softmax and the
+ * weighted sum are computed in f32 from the fp16 rows. */
+int tn_attention_f16(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                     int32_t max_ctx, const float* d_q, const uint16_t* d_k, const uint16_t* d_v,
+                     const int32_t* d_slot, const int32_t* d_len, float* d_out, void* d_scratch,
+                     uint64_t scratch_bytes, void* stream);
 
 /* tn_attention without a scratch argument, for callers that cannot allocate
  * device memory.  This entry point has no counterpart in the reference.
@@ -226,12 +237,13 @@ int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_
  * from JavaScript), a C binding layer that has no allocator of its own, or a
  * serving loop that must never pay the device-wide synchronisation that
  * cudaMalloc/cudaFree can imply.  This variant takes the same inputs and
- * output as tn_attention but keeps its row table (16 bytes a row) in a
- * fixed array compiled into the library: TN_ATTENTION_STATIC_SCRATCH_BYTES
- * (1 MiB, 65536 rows) of device memory, held on every GPU that loads the
- * library until the process exits.  Calls whose tn_attention_scratch_bytes()
- * exceeds that size fail with TN_ECAPACITY and launch nothing; nothing here
- * allocates.
+ * output as tn_attention but keeps its scratch (row table, split counters and
+ * partials) in a fixed array compiled into the library:
+ * TN_ATTENTION_STATIC_SCRATCH_BYTES (1 MiB) of device memory, held on every
+ * GPU that loads the library until the process exits.  The number of splits
+ * per row is reduced until the partials fit; calls whose row table alone
+ * exceeds the array (more than 65536 rows) fail with TN_ECAPACITY and launch
+ * nothing; nothing here allocates.
  *
  * It runs on the calling thread's current device.  Its first call on a device
  * looks up that device's address of the array (once per device), so make that

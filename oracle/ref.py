@@ -66,6 +66,7 @@ def load() -> C.CDLL:
         lib.ref_kv_len.argtypes = [C.c_void_p, C.c_uint64]
         lib.ref_kv_row.argtypes = [C.c_void_p, C.c_uint64, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         lib.ref_free.argtypes = [C.c_void_p]
+        lib.ref_set_kv_f16.argtypes = [C.c_void_p, C.c_int]
         _lib = lib
     return _lib
 
@@ -150,7 +151,7 @@ class RefStage:
     """initStage / forward / freeStage of the reference CPU path."""
 
     def __init__(self, dims: dict, lo: int, hi: int, is_first: bool, is_last: bool, weights: dict,
-                 n_threads: int | None = None):
+                 n_threads: int | None = None, kv_f16: bool = False):
         lib = load()
         self.H = int(dims["hidden_dim"])
         self.vocab = int(dims["vocab"])
@@ -187,6 +188,10 @@ class RefStage:
         self.h = lib.ref_init(C.byref(s))
         if not self.h:
             raise ValueError("ref_init failed")
+        # not part of the reference: K / V rows stored as binary16, the opt-in
+        # cache format of the GPU stage (TN_FLAG_KV_F16)
+        if kv_f16:
+            lib.ref_set_kv_f16(self.h, 1)
 
     def forward(self, seq_id: int, token_pos: int, token_ids=None, hidden=None, temperature: float = 0.0,
                 top_p: float = 0.95, u: float = 0.0) -> dict:

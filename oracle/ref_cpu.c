@@ -322,7 +322,30 @@ struct ref_stage {
   float* final_norm;    /* [H] */
   ref_seq* seqs;
   int n_seqs, cap_seqs;
+  int kv_f16; /* not in the reference: KV rows rounded to binary16 when pushed */
 };
+
+/* x rounded to the nearest binary16 value (ties to even), as a float: the
+   stored value of an fp16 KV cache.  Overflow gives infinity. */
+static float round_f16(float x) {
+  uint32_t u;
+  memcpy(&u, &x, 4);
+  const uint32_t sign = u & 0x80000000u, a = u & 0x7fffffffu;
+  if (a >= 0x7f800000u) return x; /* inf, nan */
+  if (a >= 0x38800000u) {         /* binary16 normal range: keep 10 mantissa bits */
+    uint32_t r = a + 0xfffu + ((a >> 13) & 1u);
+    r &= ~0x1fffu;
+    if (r >= 0x47800000u) r = 0x7f800000u;
+    r |= sign;
+    float y;
+    memcpy(&y, &r, 4);
+    return y;
+  }
+  /* subnormal range: multiples of 2^-24 (x * 2^24 is exact) */
+  return rintf(x * 16777216.0f) * (1.0f / 16777216.0f);
+}
+
+void ref_set_kv_f16(ref_stage* st, int on) { st->kv_f16 = on != 0; }
 
 static ref_seq* find_seq(ref_stage* st, uint64_t id, int create) {
   for (int i = 0; i < st->n_seqs; i++)
@@ -428,6 +451,11 @@ static int run_layers(ref_stage* st, ref_seq* kv, int pos, float* h) {
     rc |= ref_matvec_packed(b + Ll.off[3], quant, kvDim, H, xn, v, nt);
     ref_rope(q, nH, hd, pos, sp->rope_theta);
     ref_rope(k, nKV, hd, pos, sp->rope_theta);
+    if (st->kv_f16)
+      for (int i = 0; i < kvDim; i++) {
+        k[i] = round_f16(k[i]);
+        v[i] = round_f16(v[i]);
+      }
     memcpy(kv->K[li] + (size_t)kv->len * kvDim, k, sizeof(float) * (size_t)kvDim); /* :554 push */
     memcpy(kv->V[li] + (size_t)kv->len * kvDim, v, sizeof(float) * (size_t)kvDim);
     const int S = kv->len + 1;

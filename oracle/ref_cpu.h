@@ -103,6 +103,9 @@ int ref_forward(ref_stage* st, uint64_t seq_id, int token_pos, const int32_t* to
 int ref_kv_len(ref_stage* st, uint64_t seq_id);
 /* copy of the cached K/V row (layer li, row s) */
 int ref_kv_row(ref_stage* st, uint64_t seq_id, int li, int s, float* k_out, float* v_out);
+/* Not in the reference: store K / V rows rounded to binary16 (ties to even),
+   the opt-in fp16 KV cache of the GPU stage. */
+void ref_set_kv_f16(ref_stage* st, int on);
 void ref_free(ref_stage* st);
 
 #ifdef __cplusplus

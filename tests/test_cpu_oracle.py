@@ -122,3 +122,28 @@ def test_tiny_greedy_fixture_matches_oracle(ref, pkg):
     for s in range(8):
         toks.append(st.forward(1, 32 + s, token_ids=[toks[-1]])["token_id"])
     assert toks == g["tokens"][:9]
+
+
+def test_oracle_fp16_kv_rows_are_rounded_f32_rows(ref, pkg):
+    """The oracle's fp16-cache mode (the GPU stage's opt-in TN_FLAG_KV_F16
+    format; the reference keeps f32) stores each K / V value rounded to the
+    nearest binary16, ties to even -- numpy's float16 conversion.  Layer 0 of
+    position 0 sees identical inputs in both modes, so its rows compare
+    exactly; the sampled token of a short prompt stays the same."""
+    m = pkg.pack.MODELS["tiny"]
+    w = pkg.pack.synth_weights(m, 0, m.n_layers, True, True)
+    kv_dim = m.n_kv_heads * (m.hidden_dim // m.n_heads)
+    full = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
+    half = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w, kv_f16=True)
+    prompt = pkg.pack.synth_prompt(m, 5)
+    a = full.forward(1, 0, token_ids=prompt)
+    b = half.forward(1, 0, token_ids=prompt)
+    for s in range(len(prompt)):
+        k32, v32 = full.kv_row(1, 0, s, kv_dim)
+        k16, v16 = half.kv_row(1, 0, s, kv_dim)
+        if s == 0:
+            assert np.array_equal(k16, k32.astype(np.float16).astype(np.float32))
+            assert np.array_equal(v16, v32.astype(np.float16).astype(np.float32))
+        assert np.array_equal(k16, k16.astype(np.float16).astype(np.float32))  # every row holds fp16 values
+    assert b["token_id"] == a["token_id"]
+    assert float(np.max(np.abs(b["logits"] - a["logits"])) / np.max(np.abs(a["logits"]))) < 1e-2

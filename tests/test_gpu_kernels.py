@@ -150,8 +150,25 @@ def test_matvec_back_to_back_same_matrix(pkg, ref, torch_cuda):
     assert total.value == 0
 
 
-@pytest.mark.parametrize("hd,nH,nKV", [(128, 32, 8), (128, 64, 8), (32, 8, 2)])
-def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV):
+def _kv_cache(torch, K, V, kv):
+    """Device copies of the cache in format kv, and the values the oracle sees
+    (an fp16 cache holds the f32 values rounded to nearest even)."""
+    if kv == "f16":
+        K, V = K.astype(np.float16), V.astype(np.float16)
+        return torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda(), K.astype(np.float32), V.astype(np.float32)
+    return torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda(), K, V
+
+
+def _attn_call(pkg, lib, kv, *args):
+    fn = lib.tn_attention_f16 if kv == "f16" else lib.tn_attention
+    pkg._lib.check(fn(*args))
+
+
+@pytest.mark.parametrize("kv", ["f32", "f16"])
+@pytest.mark.parametrize("hd,nH,nKV", [(128, 32, 8), (128, 64, 8), (32, 8, 2), (64, 64, 4)])
+def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV, kv):
+    """Rows of 1 .. 2100 positions; an fp16 cache is compared with the oracle
+    on the same rounded values (only the storage format differs)."""
     torch = torch_cuda
     lib = pkg._lib.load()
     max_ctx, n_slots = 2100, 3
@@ -161,15 +178,15 @@ def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV):
     lens = [1, 7, 33, 2048, 517, 2100]
     slots = [0, 1, 2, 0, 1, 2]
     q = rng.standard_normal((len(lens), nH * hd)).astype(np.float32)
-    dK, dV, dq = (torch.from_numpy(a).cuda() for a in (K, V, q))
+    dK, dV, K, V = _kv_cache(torch, K, V, kv)
+    dq = torch.from_numpy(q).cuda()
     dslot = torch.tensor(slots, dtype=torch.int32, device="cuda")
     dlen = torch.tensor(lens, dtype=torch.int32, device="cuda")
     out = torch.zeros((len(lens), nH * hd), dtype=torch.float32, device="cuda")
     nbytes = lib.tn_attention_scratch_bytes(len(lens), nH, nKV, hd, max_ctx)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
-    pkg._lib.check(lib.tn_attention(len(lens), n_slots, nH, nKV, hd, max_ctx, dq.data_ptr(), dK.data_ptr(),
-                                    dV.data_ptr(), dslot.data_ptr(), dlen.data_ptr(), out.data_ptr(),
-                                    scratch.data_ptr(), nbytes, None))
+    _attn_call(pkg, lib, kv, len(lens), n_slots, nH, nKV, hd, max_ctx, dq.data_ptr(), dK.data_ptr(), dV.data_ptr(),
+               dslot.data_ptr(), dlen.data_ptr(), out.data_ptr(), scratch.data_ptr(), nbytes, None)
     torch.cuda.synchronize()
     got = out.cpu().numpy()
     for r, (L, s) in enumerate(zip(lens, slots)):
@@ -180,11 +197,17 @@ def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV):
         assert _maxrel(got[r], want) < ATTN_TOL, (r, L, _maxrel(got[r], want))
 
 
-@pytest.mark.parametrize("L,n_rows,n_slots", [(512, 1, 1), (2048, 8, 8), (2048, 64, 16), (8192, 8, 4),
-                                              (8192, 64, 8), (32768, 1, 1), (32768, 8, 2), (32768, 64, 8)])
-def test_attention_context_sweep(pkg, ref, torch_cuda, L, n_rows, n_slots):
+@pytest.mark.parametrize("L,n_rows,n_slots,kv", [
+    (512, 1, 1, "f32"), (1024, 1, 1, "f32"), (2048, 8, 8, "f32"), (2048, 64, 16, "f32"), (8192, 1, 1, "f32"),
+    (8192, 8, 4, "f32"), (8192, 64, 8, "f32"), (32768, 1, 1, "f32"), (32768, 8, 2, "f32"), (32768, 64, 8, "f32"),
+    (1024, 1, 1, "f16"), (8192, 8, 4, "f16"), (32768, 1, 1, "f16"), (32768, 8, 2, "f16"),
+])
+def test_attention_context_sweep(pkg, ref, torch_cuda, L, n_rows, n_slots, kv):
     """The GQA decode-attention sweep (32 query / 8 KV heads x 128, contexts
-    512 .. 32768, 1 .. 64 concurrent rows) against the oracle."""
+    512 .. 32768, 1 .. 64 concurrent rows, f32 and fp16 caches) against the
+    oracle.  Few rows split every row's positions over many CTAs; two
+    launches back to back give identical bits (the merge runs in split order
+    and the last CTA resets the arrival counters)."""
     torch = torch_cuda
     lib = pkg._lib.load()
     hd, nH, nKV = 128, 32, 8
@@ -194,18 +217,20 @@ def test_attention_context_sweep(pkg, ref, torch_cuda, L, n_rows, n_slots):
     lens = [L - (r % 3) for r in range(n_rows)]
     slots = [r % n_slots for r in range(n_rows)]
     q = rng.standard_normal((n_rows, nH * hd), dtype=np.float32)
-    dK, dV, dq = (torch.from_numpy(a).cuda() for a in (K, V, q))
+    dK, dV, K, V = _kv_cache(torch, K, V, kv)
+    dq = torch.from_numpy(q).cuda()
     dslot = torch.tensor(slots, dtype=torch.int32, device="cuda")
     dlen = torch.tensor(lens, dtype=torch.int32, device="cuda")
-    out = torch.zeros((n_rows, nH * hd), dtype=torch.float32, device="cuda")
+    outs = [torch.zeros((n_rows, nH * hd), dtype=torch.float32, device="cuda") for _ in range(2)]
     nbytes = lib.tn_attention_scratch_bytes(n_rows, nH, nKV, hd, L)
     scratch = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
-    pkg._lib.check(lib.tn_attention(n_rows, n_slots, nH, nKV, hd, L, dq.data_ptr(), dK.data_ptr(), dV.data_ptr(),
-                                    dslot.data_ptr(), dlen.data_ptr(), out.data_ptr(), scratch.data_ptr(), nbytes,
-                                    None))
+    for out in outs:
+        _attn_call(pkg, lib, kv, n_rows, n_slots, nH, nKV, hd, L, dq.data_ptr(), dK.data_ptr(), dV.data_ptr(),
+                   dslot.data_ptr(), dlen.data_ptr(), out.data_ptr(), scratch.data_ptr(), nbytes, None)
     torch.cuda.synchronize()
-    got = out.cpu().numpy()
+    got = outs[0].cpu().numpy()
     assert np.isfinite(got).all()
+    assert np.array_equal(got, outs[1].cpu().numpy())
     step = max(1, n_rows // 4) if L >= 8192 else 1  # long contexts: the oracle checks a spread of rows
     for r in sorted(set(range(0, n_rows, step)) | {n_rows - 1}):
         s, n = slots[r], lens[r]

@@ -66,6 +66,36 @@ def test_tiny_single_stage_greedy_64(pkg, ref, tiny, fused):
     pkg.freeStage(ctx)
 
 
+@pytest.mark.parametrize("fused", [True, False])
+def test_tiny_kv_f16_greedy_vs_oracle(pkg, ref, tiny, fused):
+    """The opt-in fp16 KV cache (TN_FLAG_KV_F16; the reference keeps f32
+    rows) against the oracle storing the same rounded rows: greedy tokens
+    identical and per-step logits within the f32 tolerance over 32 steps, on
+    the fused RoPE + KV-append epilogue and on the separate kernels.  The
+    cache takes half the bytes of the f32 one."""
+    m, w = tiny
+    ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, fused_decode=fused, kv_dtype="f16")
+    ref32, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    assert ctx.info()["kv_bytes"] * 2 == ref32.info()["kv_bytes"]
+    pkg.freeStage(ref32)
+    oracle = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w, kv_f16=True)
+    prompt = pkg.pack.synth_prompt(m, 24, seed=77)
+    got = pkg.forward(ctx, {"seq_id": "h", "token_pos": 0, "token_ids": prompt, "temperature": 0})["token_id"]
+    want = oracle.forward(1, 0, token_ids=prompt)
+    assert got == want["token_id"]
+    assert maxrel(ctx.peek("logits", 1)[0], want["logits"]) <= LOGIT_TOL
+    tok = got
+    for s in range(32):
+        pos = 24 + s
+        got = pkg.forward(ctx, {"seq_id": "h", "token_pos": pos, "token_ids": [tok], "temperature": 0})
+        want = oracle.forward(1, pos, token_ids=[tok])
+        assert got["token_id"] == want["token_id"], s
+        err = maxrel(ctx.peek("logits", 1)[0], want["logits"])
+        assert err <= LOGIT_TOL, (s, err)
+        tok = got["token_id"]
+    pkg.freeStage(ctx)
+
+
 def test_tiny_two_stages_reference_hops(pkg, ref, tiny):
     """The reference runtime's hop semantics: prefill hops only the last
     position (web/tabnet-node.js:167-169), so stage 1's KV starts at one row."""
