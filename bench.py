@@ -392,98 +392,6 @@ def device_weights(pkg, torch, m, lo, hi, first, last):
     return bufs
 
 
-class Pipeline:
-    """One stage per rank, stepping micro-batches on the tick schedule of
-    planner.pipeline_tick with all P2P ops of a tick batched."""
-
-    def __init__(self, pkg, torch, ctx, rank, world, M, H):
-        self.pkg, self.torch, self.ctx = pkg, torch, ctx
-        self.rank, self.world, self.M, self.H = rank, world, M, H
-        self.lib = pkg._lib.load()
-        self.stream_ptr = self.lib.tn_stage_stream(ctx.handle)
-        self.stream = torch.cuda.ExternalStream(self.stream_ptr)
-        dev = torch.device("cuda", torch.cuda.current_device())
-        self.tok = torch.zeros((M, 1), dtype=torch.int32, device=dev)          # rank 0 inputs / last outputs
-        self.hin = torch.zeros((M, H), dtype=torch.float16, device=dev)        # hidden inputs (fp16 bits)
-        self.hout = torch.zeros((M, H), dtype=torch.float16, device=dev)       # hidden outputs (fp16 bits)
-        self.tok_out = torch.zeros((M, 1), dtype=torch.int32, device=dev)
-        self.seq_ids = [(C.c_uint64 * 1)(ctx.seq_key(mb)) for mb in range(M)]
-        self.pos = [0] * M
-
-    def _step(self, mb):
-        lib, P = self.lib, self.pkg._lib
-        pos = (C.c_int32 * 1)(self.pos[mb])
-        d = P.StepDesc(n_seqs=1, seq_ids=self.seq_ids[mb], token_pos=pos, temperature=0.0, top_p=0.95, rng_seed=0)
-        if self.ctx.is_first:
-            d.d_token_ids = self.tok[mb].data_ptr()
-        else:
-            d.d_hidden_in = self.hin[mb].data_ptr()
-        if self.ctx.is_last:
-            d.d_token_out = (self.tok if self.world == 1 else self.tok_out)[mb].data_ptr()
-        else:
-            d.d_hidden_out = self.hout[mb].data_ptr()
-        P.check(lib.tn_stage_step_async(self.ctx.handle, C.byref(d), self.stream_ptr))
-        self.pos[mb] += 1
-
-    def rounds(self, n_rounds: int):
-        """n_rounds x M steps per rank, including pipeline fill and drain."""
-        torch, W, M, r = self.torch, self.world, self.M, self.rank
-        n = n_rounds * M
-        with torch.cuda.stream(self.stream):
-            if W == 1:
-                for j in range(n):
-                    self._step(j % M)
-                return
-            import torch.distributed as dist
-
-            bufs = {"recv_token": self.tok, "recv_hidden": self.hin, "send_hidden": self.hout,
-                    "send_token": self.tok_out}
-            for tau in range(self.pkg.planner.pipeline_ticks(W, n)):
-                sched, mb = self.pkg.planner.pipeline_tick(r, W, M, n, tau)
-                ops = [dist.P2POp(dist.irecv if kind.startswith("recv") else dist.isend, bufs[kind][b], peer)
-                       for kind, b, peer in sched]
-                if ops:
-                    for w in dist.batch_isend_irecv(ops):
-                        w.wait()
-                if mb is not None:
-                    self._step(mb)
-
-
-def prefill(pkg, torch, ctx, rank, world, prompts, H):
-    """Untimed prompt prefill through the host API; every prompt position hops
-    to the next stage (hop_mode all) so each stage's KV covers the prompt."""
-    M, L = len(prompts), len(prompts[0])
-    reqs = []
-    if rank == 0:
-        reqs = [{"seq_id": mb, "token_pos": 0, "token_ids": prompts[mb], "temperature": 0, "hop_mode": "all"}
-                for mb in range(M)]
-    else:
-        import torch.distributed as dist
-
-        buf = torch.empty((M, L, H), dtype=torch.float16, device="cuda")
-        dist.recv(buf, rank - 1)
-        hid = buf.cpu().numpy().view(np.uint16)
-        reqs = [{"seq_id": mb, "token_pos": 0, "hidden": hid[mb], "temperature": 0, "hop_mode": "all"}
-                for mb in range(M)]
-    out = pkg.forward_batch(ctx, reqs)
-    if ctx.is_last:
-        first_tok = [o["token_id"] for o in out]
-        if world > 1:
-            import torch.distributed as dist
-
-            dist.send(torch.tensor(first_tok, dtype=torch.int32, device="cuda"), 0)
-        return first_tok
-    import torch.distributed as dist
-
-    hs = np.stack([o["hidden"] for o in out]).astype(np.uint16)
-    dist.send(torch.from_numpy(hs.view(np.float16)).cuda(), rank + 1)
-    if rank == 0:
-        t = torch.empty(M, dtype=torch.int32, device="cuda")
-        dist.recv(t, world - 1)
-        return t.cpu().tolist()
-    return None
-
-
 def matvec_bytes(pkg, m, cls: str, T: int = 1) -> int:
     """Algorithmic bytes of one matvec launch: packed weights + f32 x + f32 y
     (read and written again for the residual epilogues)."""
@@ -546,11 +454,11 @@ def run_ours(args):
     t_init = time.perf_counter() - t_init
     prompts = [pkg.pack.synth_prompt(m, args.prompt, seed=100 + mb) for mb in range(M)]
     t_pre = time.perf_counter()
-    first_tok = prefill(pkg, torch, ctx, rank, world, prompts, m.hidden_dim)
+    first_tok = pkg.pipeline.prefill(ctx, rank, world, prompts, m.hidden_dim)
     torch.cuda.synchronize()
     t_pre = time.perf_counter() - t_pre
-    pipe = Pipeline(pkg, torch, ctx, rank, world, M, m.hidden_dim)
-    pipe.pos = [args.prompt] * M
+    pipe = pkg.pipeline.Pipeline(pkg.pipeline.DeviceStage(ctx, M), rank, world, M, m.hidden_dim, deadline_s=900)
+    pipe.pos = [[args.prompt] for _ in range(M)]
     if rank == 0:
         pipe.tok.copy_(torch.tensor(first_tok, dtype=torch.int32).view(M, 1))
 
@@ -583,7 +491,7 @@ def run_ours(args):
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record(pipe.stream)
     torch.cuda.nvtx.range_push("decode_timed")  # (profilers: --nvtx-include decode_timed/)
-    pipe.rounds(args.steps)
+    pipe.rounds(args.steps, wait=False)
     torch.cuda.nvtx.range_pop()
     ev1.record(pipe.stream)
     barrier()
@@ -594,38 +502,26 @@ def run_ours(args):
     value = tokens / (ms / 1e3)
     launches = info["launches_last_step"] * tokens
     # ---- e2e: the host-buffer API (tn_stage_forward) for every micro-batch step
-    e2e_val, h2d, d2h = None, 0, 0
-    if world == 1:
-        toks = pipe.tok.cpu().view(-1).tolist()
-        barrier()
-        t0 = time.perf_counter()
-        for _ in range(args.steps):
-            for mb in range(M):
-                toks[mb] = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [toks[mb]],
-                                             "temperature": 0})["token_id"]
-                pipe.pos[mb] += 1
-        torch.cuda.synchronize()
-        e2e_s = time.perf_counter() - t0
-        e2e_val = tokens / e2e_s
-        h2d, d2h = 4 * M, 4 * M  # token ids in, token ids out, per round
-        pipe.tok.copy_(torch.tensor(toks, dtype=torch.int32).view(M, 1))
-    else:
-        e2e_val, h2d, d2h = pipeline_e2e(pkg, torch, ctx, pipe, args, rank, world, barrier, max_over_ranks)
+    # (same schedule; a step's input frame comes to the host from the receive
+    # slot and its output goes back to the send slot, so the stages still work
+    # on different micro-batches at once)
+    barrier()
+    t0 = time.perf_counter()
+    pipe.rounds_host(ctx, args.steps)
+    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    e2e_val = tokens / e2e_s
+    # per round: token ids in (rank 0) and out (last rank), one fp16 frame into
+    # and one out of the host API at each of the world - 1 stage boundaries
+    h2d = d2h = 4 * M + 2 * m.hidden_dim * M * (world - 1)
     # ---- profiled pass: per-kernel device time (CUDA events around each launch)
     pkg._lib.check(lib.tn_stage_set_profile(ctx.handle, 1))
     ctx.profile(reset=True)
-    toks = pipe.tok.cpu().view(-1).tolist() if rank == 0 else None
     if world == 1:
-        for _ in range(args.steps):
-            for mb in range(M):
-                toks[mb] = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [toks[mb]],
-                                             "temperature": 0})["token_id"]
-                pipe.pos[mb] += 1
+        pipe.rounds_host(ctx, args.steps)
     prof = ctx.profile() if world == 1 else {}
     pkg._lib.check(lib.tn_stage_set_profile(ctx.handle, 0))
     fused = None
     if world == 1 and not args.no_fused:
-        pipe.tok.copy_(torch.tensor(toks, dtype=torch.int32).view(M, 1))
         fused = fused_decode(pkg, torch, ctx, pipe, args)
     peak, peak_kind = measured_peaks()
     mv = [k for k in prof if k.startswith("matvec") and prof[k][1] > 0]
@@ -688,17 +584,17 @@ def fused_decode(pkg, torch, ctx, pipe, args) -> dict:
     per token (the stage batches concurrent sequences), timed like the
     pipeline rounds -- device-resident token ids, CUDA events on the stage
     stream -- and end to end through the host-buffer batch API."""
-    lib, P, M = pipe.lib, pkg._lib, pipe.M
+    lib, P, M = pipe.stage.lib, pkg._lib, pipe.M
     ids = (C.c_uint64 * M)(*[ctx.seq_key(mb) for mb in range(M)])
     tok = pipe.tok.view(-1)
 
     def step():
-        pos = (C.c_int32 * M)(*pipe.pos)
+        pos = (C.c_int32 * M)(*[p[0] for p in pipe.pos])
         d = P.StepDesc(n_seqs=M, seq_ids=ids, token_pos=pos, d_token_ids=tok.data_ptr(),
                        d_token_out=tok.data_ptr(), temperature=0.0, top_p=0.95, rng_seed=0)
-        P.check(lib.tn_stage_step_async(ctx.handle, C.byref(d), pipe.stream_ptr))
+        P.check(lib.tn_stage_step_async(ctx.handle, C.byref(d), pipe.stage.stream_ptr))
         for mb in range(M):
-            pipe.pos[mb] += 1
+            pipe.pos[mb][0] += 1
 
     with torch.cuda.stream(pipe.stream):
         for _ in range(max(3, args.warmup)):
@@ -721,11 +617,11 @@ def fused_decode(pkg, torch, ctx, pipe, args) -> dict:
     toks = tok.cpu().tolist()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        out = pkg.forward_batch(ctx, [{"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [toks[mb]],
+        out = pkg.forward_batch(ctx, [{"seq_id": mb, "token_pos": pipe.pos[mb][0], "token_ids": [toks[mb]],
                                        "temperature": 0} for mb in range(M)])
         toks = [o["token_id"] for o in out]
         for mb in range(M):
-            pipe.pos[mb] += 1
+            pipe.pos[mb][0] += 1
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     n_tok = args.steps * M
@@ -736,50 +632,6 @@ def fused_decode(pkg, torch, ctx, pipe, args) -> dict:
                     "d2h_bytes_per_step": 4 * M},
             "schedule": f"all {M} sequences' next tokens as one {M}-row step (matvecs in groups of up to "
                         "4 token columns); value above is the micro-batch schedule"}
-
-
-def pipeline_e2e(pkg, torch, ctx, pipe, args, rank, world, barrier, max_over_ranks):
-    """e2e for N>1: every stage step goes through the host-buffer API
-    (tn_stage_forward), on the tick schedule of the timed rounds: a step's
-    input frame comes to the host from the NCCL receive buffer and its output
-    frame goes back to the device for the send, so the stages work on
-    different micro-batches at once."""
-    import torch.distributed as dist
-
-    M, H, W = pipe.M, pipe.H, world
-    n = args.steps * M
-    dev = pipe.tok.device
-    hin = torch.zeros((M, H), dtype=torch.float16, device=dev)
-    hout = torch.zeros((M, H), dtype=torch.float16, device=dev)
-    tok_out = torch.zeros((M, 1), dtype=torch.int32, device=dev)
-    bufs = {"recv_token": pipe.tok, "recv_hidden": hin, "send_hidden": hout, "send_token": tok_out}
-    barrier()
-    t0 = time.perf_counter()
-    for tau in range(pkg.planner.pipeline_ticks(W, n)):
-        sched, mb = pkg.planner.pipeline_tick(rank, W, M, n, tau)
-        ops = [dist.P2POp(dist.irecv if kind.startswith("recv") else dist.isend, bufs[kind][b], peer)
-               for kind, b, peer in sched]
-        if ops:
-            for w in dist.batch_isend_irecv(ops):
-                w.wait()
-        if mb is None:
-            continue
-        if rank == 0:
-            out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb], "token_ids": [int(pipe.tok[mb, 0].item())]})
-            hout[mb].copy_(torch.from_numpy(out["hidden"].view(np.float16)))
-        else:
-            out = pkg.forward(ctx, {"seq_id": mb, "token_pos": pipe.pos[mb],
-                                    "hidden": hin[mb].cpu().numpy().view(np.uint16), "temperature": 0})
-            if ctx.is_last:
-                tok_out[mb, 0] = out["token_id"]
-            else:
-                hout[mb].copy_(torch.from_numpy(out["hidden"].view(np.float16)))
-        pipe.pos[mb] += 1
-    torch.cuda.synchronize()
-    s = max_over_ranks(time.perf_counter() - t0)
-    # per round: token ids in (rank 0) and out (last rank), one fp16 frame into
-    # and one out of the host API at each of the W - 1 stage boundaries
-    return n / s, 4 * M + 2 * H * M * (W - 1), 4 * M + 2 * H * M * (W - 1)
 
 
 def main(argv=None):

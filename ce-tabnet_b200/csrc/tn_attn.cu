@@ -132,18 +132,24 @@ __device__ __forceinline__ float attn_reduce_scatter(float (&v)[N], int lane) {
   return r;
 }
 
+// two resident CTAs per SM (twice the loads in flight) where the registers
+// allow it without spilling
+__host__ __device__ constexpr int attn_min_blocks(int HD, int G) { return (HD == 128 && G <= 2) || G == 16 ? 1 : 2; }
+
 template <int HD, int G, typename KT>
-__global__ void __launch_bounds__(ATT_THREADS) k_attn(const AttnArgs a) {
+__global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G)) k_attn(const AttnArgs a) {
   constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD;
   using Vec = KvVec<KT, DPL>;
   using Raw = typename Vec::Raw;
-  // prefetch the next step's K / V rows when they fit in 16 registers each
-  constexpr bool PF = PS * (((int)sizeof(Raw) + 3) / 4) <= 16;
+  // prefetch the next step's K / V rows when they fit in 4 registers each
+  // (else the second resident CTA keeps the loads in flight)
+  constexpr bool PF = PS * (((int)sizeof(Raw) + 3) / 4) <= 4;
   constexpr unsigned FULL = 0xffffffffu;
   __shared__ float s_m[ATT_WARPS][G], s_l[ATT_WARPS][G];
   __shared__ __align__(16) float s_o[ATT_WARPS][GH];
   __shared__ float s_w[ATT_WARPS][G];  // merge weights exp(m - M) of the warps
   __shared__ float s_M[G], s_L[G];
+  __shared__ __align__(16) float s_q[GH];  // this row's q for the G heads of the KV head
   __shared__ float s_part[2][ATT_MAX_SPLITS][G];  // the splits' maxima and sums (last arriver)
   __shared__ int s_last;
   // grid.x = (row, KV head, split), splits innermost
@@ -160,14 +166,26 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const AttnArgs a) {
   const KT* kb = reinterpret_cast<const KT*>(a.kc) + ri.slot * a.slot_stride + kvh * a.kvh_stride + lane * DPL;
   const KT* vb = reinterpret_cast<const KT*>(a.vc) + ri.slot * a.slot_stride + kvh * a.kvh_stride + lane * DPL;
 
-  float qr[G][DPL], acc[G][DPL];
+  for (int e = tid; e < GH; e += ATT_THREADS) s_q[e] = a.q[(size_t)t * a.ldq + kvh * GH + e];
+  float acc[G][DPL];
 #pragma unroll
   for (int h = 0; h < G; h++)
 #pragma unroll
-    for (int d = 0; d < DPL; d++) {
-      qr[h][d] = a.q[(size_t)t * a.ldq + (kvh * G + h) * HD + lane * DPL + d];
-      acc[h][d] = 0.f;
+    for (int d = 0; d < DPL; d++) acc[h][d] = 0.f;
+  // this lane's DPL dimensions of head h's q
+  auto q_of = [&](int h, float (&qh)[DPL]) {
+    const float* src = s_q + h * HD + lane * DPL;
+    if constexpr (DPL == 4) {
+      const float4 v4 = *reinterpret_cast<const float4*>(src);
+      qh[0] = v4.x;
+      qh[DPL > 1 ? 1 : 0] = v4.y;
+      qh[DPL > 2 ? 2 : 0] = v4.z;
+      qh[DPL > 3 ? 3 : 0] = v4.w;
+    } else {
+#pragma unroll
+      for (int d = 0; d < DPL; d++) qh[d] = src[d];
     }
+  };
   // this lane's (head, position) after the reduce-scatter; its head's running
   // max / sum live in every lane of that head
   const int my_p = lane / G;
@@ -182,17 +200,21 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const AttnArgs a) {
     }
   };
   if (PF && wlo < whi) load_step(wlo, kn, vn);
+  __syncthreads();  // s_q
   for (int p0 = wlo; p0 < whi; p0 += PS) {
-    float kr[PS][DPL], vr[PS][DPL];
+    // this step's rows: K as floats for the scores, V kept raw until the
+    // weighted sum converts it a position at a time
+    float kr[PS][DPL];
+    Raw vw[PS];
     if constexpr (PF) {
 #pragma unroll
       for (int i = 0; i < PS; i++) {
         Vec::cvt(kn[i % (PF ? PS : 1)], kr[i]);
-        Vec::cvt(vn[i % (PF ? PS : 1)], vr[i]);
+        vw[i] = vn[i % (PF ? PS : 1)];
       }
       if (p0 + PS < whi) load_step(p0 + PS, kn, vn);
     } else {
-      Raw kw[PS], vw[PS];
+      Raw kw[PS];
 #pragma unroll
       for (int i = 0; i < PS; i++) {
         const int p = min(p0 + i, whi - 1);
@@ -200,21 +222,21 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const AttnArgs a) {
         vw[i] = Vec::load(vb + (size_t)p * HD);
       }
 #pragma unroll
-      for (int i = 0; i < PS; i++) {
-        Vec::cvt(kw[i], kr[i]);
-        Vec::cvt(vw[i], vr[i]);
-      }
+      for (int i = 0; i < PS; i++) Vec::cvt(kw[i], kr[i]);
     }
     float v[32];
 #pragma unroll
-    for (int i = 0; i < PS; i++)
+    for (int h = 0; h < G; h++) {
+      float qh[DPL];
+      q_of(h, qh);
 #pragma unroll
-      for (int h = 0; h < G; h++) {
+      for (int i = 0; i < PS; i++) {
         float s = 0.f;
 #pragma unroll
-        for (int d = 0; d < DPL; d++) s = fmaf(qr[h][d], kr[i][d], s);
+        for (int d = 0; d < DPL; d++) s = fmaf(qh[d], kr[i][d], s);
         v[i * G + h] = s;
       }
+    }
     const float sc = attn_reduce_scatter<32>(v, lane) * a.scale;
     const float s = p0 + my_p < whi ? sc : -INFINITY;
     float mx = s;
@@ -235,13 +257,16 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const AttnArgs a) {
       for (int d = 0; d < DPL; d++) acc[h][d] *= al;
     }
 #pragma unroll
-    for (int i = 0; i < PS; i++)
+    for (int i = 0; i < PS; i++) {
+      float vr[DPL];
+      Vec::cvt(vw[i], vr);
 #pragma unroll
       for (int h = 0; h < G; h++) {
         const float w = __shfl_sync(FULL, p, i * G + h);
 #pragma unroll
-        for (int d = 0; d < DPL; d++) acc[h][d] = fmaf(w, vr[i][d], acc[h][d]);
+        for (int d = 0; d < DPL; d++) acc[h][d] = fmaf(w, vr[d], acc[h][d]);
       }
+    }
   }
   // merge the warps: the CTA's partial is the output relative to its
   // per-head max M, with the sum L
@@ -307,18 +332,32 @@ __global__ void __launch_bounds__(ATT_THREADS) k_attn(const AttnArgs a) {
     s_L[tid] = Lsum;
   }
   __syncthreads();
-  for (int e = tid; e < GH; e += ATT_THREADS) {
-    const int h = e / HD;
-    float o = 0.f;
-    for (int c0 = 0; c0 < S; c0 += 8) {
-      float pv[8];
+  // this thread's EPT output elements, CB splits at a time: 32 loads in flight
+  constexpr int EPT = (GH + ATT_THREADS - 1) / ATT_THREADS, CB = 32 / EPT > 0 ? 32 / EPT : 1;
+  float o[EPT];
 #pragma unroll
-      for (int j = 0; j < 8; j++) pv[j] = c0 + j < S ? __ldcg(w0 + (size_t)(c0 + j) * a.pstride + e) : 0.f;
+  for (int i = 0; i < EPT; i++) o[i] = 0.f;
+  for (int c0 = 0; c0 < S; c0 += CB) {
+    float pv[CB][EPT];
 #pragma unroll
-      for (int j = 0; j < 8; j++)
-        if (c0 + j < S) o = fmaf(pv[j], s_part[0][c0 + j][h], o);
-    }
-    a.out[(size_t)t * a.ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
+    for (int j = 0; j < CB; j++)
+#pragma unroll
+      for (int i = 0; i < EPT; i++) {
+        const int e = tid + i * ATT_THREADS;
+        pv[j][i] = c0 + j < S && e < GH ? __ldcg(w0 + (size_t)(c0 + j) * a.pstride + e) : 0.f;
+      }
+#pragma unroll
+    for (int j = 0; j < CB; j++)
+#pragma unroll
+      for (int i = 0; i < EPT; i++) {
+        const int e = tid + i * ATT_THREADS;
+        if (c0 + j < S && e < GH) o[i] = fmaf(pv[j][i], s_part[0][c0 + j][e / HD], o[i]);
+      }
+  }
+#pragma unroll
+  for (int i = 0; i < EPT; i++) {
+    const int e = tid + i * ATT_THREADS, h = e / HD;
+    if (e < GH) a.out[(size_t)t * a.ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o[i] / s_L[h] : 0.f;
   }
   if (tid == 0) a.cnt[(size_t)t * a.nkv + kvh] = 0;  // ready for the next launch
 }
@@ -388,11 +427,12 @@ AttnPlan attn_plan(int T, int nH, int nKV, int hd, int max_ctx, int kv_type, siz
   AttnPlan p;
   if (T <= 0 || nKV <= 0 || nH % nKV != 0) return p;
   const int G = nH / nKV, PS = 32 / std::max(1, std::min(G, 32));
-  // splits so that the grid covers every SM's resident CTAs once, each split
-  // at least one warp step per warp of the longest row
+  // splits so that the grid fills every SM's resident CTA slots in one wave
+  // (never a second, mostly idle one), each split at least one warp step per
+  // warp of the longest row
   const int64_t rows_kv = (int64_t)T * nKV;
   const int64_t target = (int64_t)attn_occupancy(hd, G, kv_type) * num_sms();
-  int S = (int)std::max<int64_t>(1, (target + rows_kv - 1) / rows_kv);
+  int S = (int)std::max<int64_t>(1, target / rows_kv);
   S = std::min(S, std::max(1, (max_ctx + ATT_WARPS * PS - 1) / (ATT_WARPS * PS)));
   S = std::min(S, ATT_MAX_SPLITS);
   const size_t per = (size_t)rows_kv * attn_pstride(G, hd);
