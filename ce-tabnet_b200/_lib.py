@@ -103,6 +103,9 @@ SIGNATURES = [
     ("tn_last_error", C.c_char_p, []),
     ("tn_stage_step_async", C.c_int, [C.c_void_p, C.POINTER(StepDesc), C.c_void_p]),
     ("tn_stage_stream", C.c_void_p, [C.c_void_p]),
+    ("tn_stage_check", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("tn_stage_test_raise_kernel_error", C.c_int, [C.c_void_p]),
+    ("tn_test_bounded_wait", C.c_int, [C.c_uint64]),
     ("tn_stage_get_info", C.c_int, [C.c_void_p, C.POINTER(StageInfo)]),
     ("tn_stage_peek", C.c_int, [C.c_void_p, C.c_int32, C.c_void_p, C.c_uint64]),
     ("tn_stage_profile", C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64), C.c_int32]),

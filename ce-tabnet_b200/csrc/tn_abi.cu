@@ -4,6 +4,7 @@
 #include <vector>
 
 #include "tn_kernels.cuh"
+#include "tn_ptx.cuh"
 
 namespace tn {
 
@@ -35,9 +36,46 @@ __global__ void k_rows_from_slots(const int32_t* __restrict__ slot, const int32_
   rows[r] = RowInfo{s, 0, 0, l > max_ctx ? max_ctx : l};
 }
 
+// The kernels' bounded mbarrier wait (mbar_wait) on a barrier that no thread
+// arrives at, with a limit of `limit` cycles: the wait gives up, the CTA's
+// abort flag is raised, and the status says so -- the path a real kernel takes
+// when its copy pipeline stalls, made to run out on purpose without a fault.
+static __device__ int g_wait_probe_status;
+__global__ void k_wait_probe(long long limit) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ volatile int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  const bool ok = mbar_wait(&bar, 0, &abort_flag, limit);
+  __syncthreads();
+  if (threadIdx.x == 0) g_wait_probe_status = ok && !abort_flag ? 0 : 1;
+}
+
 }  // namespace tn
 
 using namespace tn;
+
+extern "C" int tn_test_bounded_wait(uint64_t limit_cycles) {
+  clear_error();
+  TN_REQUIRE(limit_cycles > 0 && limit_cycles <= (uint64_t)kWaitLimitCycles, TN_EINVAL,
+             "tn_test_bounded_wait: limit of %llu cycles", (unsigned long long)limit_cycles);
+  int st = -1;
+  TN_CHECK_CUDA(cudaMemcpyToSymbol(g_wait_probe_status, &st, sizeof(int)));
+  k_wait_probe<<<1, 64>>>((long long)limit_cycles);
+  TN_CHECK_LAUNCH();
+  TN_CHECK_CUDA(cudaDeviceSynchronize());
+  TN_CHECK_CUDA(cudaMemcpyFromSymbol(&st, g_wait_probe_status, sizeof(int)));
+  TN_REQUIRE(st == 0 || st == 1, TN_ECUDA, "tn_test_bounded_wait: status %d", st);
+  if (st) {
+    set_error("bounded wait gave up after %llu cycles", (unsigned long long)limit_cycles);
+    return TN_ETIMEOUT;
+  }
+  return TN_OK;
+}
 
 struct tn_matrix {
   Matrix m;

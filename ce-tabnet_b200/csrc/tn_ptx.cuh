@@ -76,14 +76,17 @@ __device__ __forceinline__ bool mbar_wait_fast(uint64_t* bar, uint32_t parity, v
     }
   }
 }
-// Bounded wait: gives up after ~2 s (or when another thread of the CTA gave
-// up), raising the CTA's abort flag; callers then stop and report an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+// Bounded wait: gives up after `limit` SM cycles (default ~2 s) or when
+// another thread of the CTA gave up, raising the CTA's abort flag; callers
+// then stop and report an error.
+constexpr long long kWaitLimitCycles = 4000000000ll;
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          long long limit = kWaitLimitCycles) {
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - t0 > 4000000000ll) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       return false;
     }

@@ -90,7 +90,7 @@ struct tn_stage {
   // split-attention partials and arrival counters (zero between launches)
   float* attn_ws = nullptr;
   int* attn_cnt = nullptr;
-  size_t attn_ws_floats = 0;
+  size_t attn_ws_floats = 0, attn_cnt_ints = 0;
   size_t kvh_stride = 0, layer_stride = 0, slot_stride = 0;
   // activations
   float *h = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *act = nullptr,
@@ -395,6 +395,7 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
       cnti = std::max(cnti, p.cnt_ints);
     }
     st->attn_ws_floats = wsf;
+    st->attn_cnt_ints = cnti;
     if (wsf && (rc = dalloc(st, &st->attn_ws, wsf))) return rc;
     if (cnti && (rc = dalloc(st, &st->attn_cnt, cnti))) return rc;
   }
@@ -468,6 +469,30 @@ static void prof_collect(tn_stage* st) {
     prof_end(st, s, pi_);                    \
     st->step_launches += (nk);               \
   } while (0)
+
+// After the stage's work on s has finished: TN_ETIMEOUT if a kernel's
+// bounded wait gave up since the last check (its step's outputs are invalid),
+// with the split-K arrival counters and workspaces zeroed so that the next
+// step starts clean; TN_OK otherwise.
+static int recover_kernel_error(tn_stage* st, cudaStream_t s) {
+  int kerr = 0;
+  TN_CHECK_CUDA(cudaMemcpy(&kerr, st->kerr, sizeof(int), cudaMemcpyDeviceToHost));
+  if (!kerr) return TN_OK;
+  TN_CHECK_CUDA(cudaMemset(st->kerr, 0, sizeof(int)));
+  // a launch that gave up may have left split-K arrival counts behind
+  for (LayerW& L : st->layers) {
+    matrix_reset_counters(L.qkv, s);
+    matrix_reset_counters(L.o, s);
+    matrix_reset_counters(L.gu, s);
+    matrix_reset_counters(L.down, s);
+  }
+  matrix_reset_counters(st->lm_head, s);
+  if (st->gemm_ws) TN_CHECK_CUDA(cudaMemsetAsync(st->gemm_ws, 0, st->gemm_ws_bytes, s));
+  if (st->attn_cnt) TN_CHECK_CUDA(cudaMemsetAsync(st->attn_cnt, 0, st->attn_cnt_ints * sizeof(int), s));
+  TN_CHECK_CUDA(cudaStreamSynchronize(s));
+  set_error("a kernel's bounded wait on its copy pipeline gave up; the step's outputs are invalid");
+  return TN_ETIMEOUT;
+}
 
 // the layer stack for T rows already described by the control block
 static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t s) {
@@ -765,25 +790,7 @@ static int forward_impl(tn_stage* st, const tn_fwd_req* reqs, int n, tn_fwd_out*
     }
   }
   TN_CHECK_CUDA(cudaStreamSynchronize(s));
-  {
-    int kerr = 0;
-    TN_CHECK_CUDA(cudaMemcpy(&kerr, st->kerr, sizeof(int), cudaMemcpyDeviceToHost));
-    if (kerr) {
-      TN_CHECK_CUDA(cudaMemset(st->kerr, 0, sizeof(int)));
-      // a launch that gave up may have left split-K arrival counts behind
-      for (LayerW& L : st->layers) {
-        matrix_reset_counters(L.qkv, s);
-        matrix_reset_counters(L.o, s);
-        matrix_reset_counters(L.gu, s);
-        matrix_reset_counters(L.down, s);
-      }
-      matrix_reset_counters(st->lm_head, s);
-      if (st->gemm_ws) TN_CHECK_CUDA(cudaMemsetAsync(st->gemm_ws, 0, st->gemm_ws_bytes, s));
-      TN_CHECK_CUDA(cudaStreamSynchronize(s));
-      set_error("a kernel's bounded wait on its copy pipeline gave up; the step's outputs are invalid");
-      return TN_ETIMEOUT;
-    }
-  }
+  if ((rc = recover_kernel_error(st, s))) return rc;
   for (int i = 0; i < n; i++) {
     st->kv_len[slot[i]] += reqs[i].n_tokens;
     if (st->last) outs[i].n_hidden_tokens = 0;
@@ -889,6 +896,25 @@ extern "C" int tn_stage_step_async(tn_stage* st, const tn_step_desc* step, void*
 }
 
 extern "C" void* tn_stage_stream(tn_stage* st) { return st ? (void*)st->stream : nullptr; }
+
+extern "C" int tn_stage_check(tn_stage* st, void* stream) {
+  clear_error();
+  TN_REQUIRE(st, TN_EINVAL, "null stage");
+  std::lock_guard<std::mutex> lk(st->mu);
+  TN_ENTER_DEVICE(st->device);
+  const cudaStream_t s = stream ? (cudaStream_t)stream : st->stream;
+  TN_CHECK_CUDA(cudaStreamSynchronize(s));
+  return recover_kernel_error(st, s);
+}
+
+extern "C" int tn_stage_test_raise_kernel_error(tn_stage* st) {
+  clear_error();
+  TN_REQUIRE(st, TN_EINVAL, "null stage");
+  std::lock_guard<std::mutex> lk(st->mu);
+  TN_ENTER_DEVICE(st->device);
+  TN_CHECK_CUDA(cudaMemsetAsync(st->kerr, 1, sizeof(int), st->stream));
+  return TN_OK;
+}
 
 extern "C" int tn_stage_free_seq(tn_stage* st, uint64_t seq_id) {
   clear_error();

@@ -91,6 +91,11 @@ class DeviceStage:
             d.d_hidden_out = hid_out.data_ptr()
         _lib.check(self.lib.tn_stage_step_async(self.ctx.handle, C.byref(d), self.stream_ptr))
 
+    def check(self) -> None:
+        """Raise TnError(TN_ETIMEOUT) if a kernel's bounded wait gave up in a
+        step since the last check (tn_stage_check; the stage recovers)."""
+        _lib.check(self.lib.tn_stage_check(self.ctx.handle, self.stream_ptr))
+
 
 class Pipeline:
     """One rank of the decode pipeline.
@@ -211,6 +216,12 @@ class Pipeline:
             if time.monotonic() > t_end:
                 self._fail(-1, None, True)
             time.sleep(0.0002)
+        check = getattr(self.stage, "check", None)
+        if check is not None:
+            try:
+                check()
+            except _lib.TnError as e:  # a device-side bounded wait gave up in one of the steps
+                raise PipelineError(e.code, f"rank {self.rank}: {e}", self.rank, -1) from e
 
     # ----------------------------------------------------------- host API
     def rounds_host(self, ctx, n_rounds: int) -> None:

@@ -150,6 +150,19 @@ typedef struct {
   uint64_t rng_seed;
 } tn_step_desc;
 int tn_stage_step_async(tn_stage* st, const tn_step_desc* step, void* stream);
+/* Waits for the stage's work on `stream` (NULL: the stage stream) and reports
+ * what tn_stage_step_async cannot: TN_ETIMEOUT if a kernel's bounded wait on
+ * its copy pipeline gave up since the last check or forward call (the outputs
+ * of the steps since then are invalid; the stage's split-K counters are reset
+ * so later steps run clean), else TN_OK.  The synchronous forward calls do this
+ * check themselves.  No counterpart in the reference, whose steps are
+ * synchronous. */
+int tn_stage_check(tn_stage* st, void* stream);
+/* Test hook: marks the stage as if a kernel's bounded wait had given up (the
+ * next tn_stage_check or forward returns TN_ETIMEOUT and recovers).  Failure
+ * handling is tested this way and with tn_test_bounded_wait, without faulting
+ * a GPU. */
+int tn_stage_test_raise_kernel_error(tn_stage* st);
 /* the stage's own stream (cudaStream_t) */
 void* tn_stage_stream(tn_stage* st);
 
@@ -259,6 +272,13 @@ int tn_attention_static(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_
                         int32_t head_dim, int32_t max_ctx, const float* d_q, const float* d_k,
                         const float* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
                         void* stream);
+
+/* Test hook: one CTA runs the kernels' bounded mbarrier wait on a barrier
+ * that nothing arrives at, with a limit of limit_cycles SM cycles (at most the
+ * kernels' own ~2 s).  Returns TN_ETIMEOUT when the wait gave up -- always,
+ * by construction -- and leaves the device usable; synchronises the device.
+ * No counterpart in the reference. */
+int tn_test_bounded_wait(uint64_t limit_cycles);
 
 /* Activation hop codec, bit-exact with f32ToF16 / f16ToF32
  * (web/inference-worker.js:68-88): round half up, subnormal mantissa masked. */
