@@ -8,7 +8,9 @@
 //
 // Work split.  CTA (split, KV head, row) streams its share of the row's
 // positions; the split count S is chosen so that the grid fills every SM
-// (one decoding row of an 8-KV-head model is 8 x S CTAs).  Within a CTA each
+// (one decoding row of an 8-KV-head model is 8 x S CTAs), and a row shorter
+// than S splits of two warp steps per warp uses fewer (the grid is fixed for
+// a captured step; the row lengths are not).  Within a CTA each
 // of the 8 warps takes a contiguous part of that share.  A lane holds HD/32
 // dimensions of q for the G query heads of the KV head; a warp step covers
 // PS = 32/G positions: the PS x G partial dot products of a lane are
@@ -19,20 +21,28 @@
 // otherwise it writes its partial (unnormalised output, running max and sum
 // per head) to a workspace, and the CTA that arrives last at the (row, KV
 // head) -- a release / acquire counter -- merges the S partials in split
-// order (deterministic) and resets the counter for the next launch.
+// order (deterministic) and resets the counter for the next launch.  Up to
+// 8 splits, and any split count over caches of at most 4096 positions, run as
+// one thread-block cluster per (row, KV head) and merge through distributed
+// shared memory instead (no global round trip: the decode chain's short rows
+// are latency-bound), also in split order.
 #include <atomic>
 #include <cfloat>
 
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 
 #include "tn_kernels.cuh"
 #include "tn_ptx.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tn {
 
 constexpr int ATT_WARPS = 8;
 constexpr int ATT_THREADS = ATT_WARPS * 32;
 constexpr int ATT_MAX_SPLITS = 32;
+constexpr int kAttnClusterCtx = 4096;  // caches up to this long merge splits within a cluster
 
 struct AttnArgs {
   const float* q;
@@ -132,18 +142,29 @@ __device__ __forceinline__ float attn_reduce_scatter(float (&v)[N], int lane) {
   return r;
 }
 
-// two resident CTAs per SM (twice the loads in flight) where the registers
-// allow it without spilling
-__host__ __device__ constexpr int attn_min_blocks(int HD, int G) { return (HD == 128 && G <= 2) || G == 16 ? 1 : 2; }
+// Two resident CTAs per SM (twice the loads in flight) where the registers
+// allow it without spilling next to the next step's prefetched rows; the
+// others keep the prefetch at one CTA per SM (a decoding row's grid has fewer
+// CTAs than SMs anyway).
+__host__ __device__ constexpr int attn_min_blocks(int HD, int G, bool half) {
+  return G == 16 || (HD == 128 && G != 4) ? 1 : 2;
+}
+// registers of prefetched K (or V) rows a variant may hold: 16, except fp16
+// rows at 4 query heads x 128 dimensions, which measured faster at two CTAs per
+// SM without the prefetch (5.06 vs 4.54 TB/s over 64 rows of 32768 positions)
+__host__ __device__ constexpr int attn_prefetch_regs(int HD, int G, bool half) {
+  return HD == 128 && G == 4 && half ? 0 : 16;
+}
 
-template <int HD, int G, typename KT>
-__global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G)) k_attn(const AttnArgs a) {
+// CL: the S splits of a (row, KV head) are one thread-block cluster and merge
+// through distributed shared memory (S <= 8); else through the workspace
+template <int HD, int G, typename KT, bool CL>
+__global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G, sizeof(KT) == 2)) k_attn(const AttnArgs a) {
   constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD;
   using Vec = KvVec<KT, DPL>;
   using Raw = typename Vec::Raw;
-  // prefetch the next step's K / V rows when they fit in 4 registers each
-  // (else the second resident CTA keeps the loads in flight)
-  constexpr bool PF = PS * (((int)sizeof(Raw) + 3) / 4) <= 4;
+  // prefetch the next step's K / V rows when they fit the variant's budget
+  constexpr bool PF = PS * (((int)sizeof(Raw) + 3) / 4) <= attn_prefetch_regs(HD, G, sizeof(KT) == 2);
   constexpr unsigned FULL = 0xffffffffu;
   __shared__ float s_m[ATT_WARPS][G], s_l[ATT_WARPS][G];
   __shared__ __align__(16) float s_o[ATT_WARPS][GH];
@@ -152,14 +173,19 @@ __global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G)) k_attn(co
   __shared__ __align__(16) float s_q[GH];  // this row's q for the G heads of the KV head
   __shared__ float s_part[2][ATT_MAX_SPLITS][G];  // the splits' maxima and sums (last arriver)
   __shared__ int s_last;
-  // grid.x = (row, KV head, split), splits innermost
-  const int S = a.S;
-  const int split = (int)(blockIdx.x % S), kvh = (int)((blockIdx.x / S) % a.nkv), t = (int)(blockIdx.x / (S * a.nkv));
+  // grid.x = (row, KV head, split), a.S splits innermost
+  const int split = (int)(blockIdx.x % a.S), kvh = (int)((blockIdx.x / a.S) % a.nkv);
+  const int t = (int)(blockIdx.x / (a.S * a.nkv));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   pdl_launch_dependents();
   pdl_wait();  // q and the cache rows of this step come from the previous kernels
   const RowInfo ri = a.rows[t];
   const int L = ri.len;
+  // this row's splits: at most S, and at least two warp steps per warp each
+  // (a short row takes few splits and a cheap merge; the rest exit here)
+  constexpr int MINP = 2 * ATT_WARPS * PS;
+  const int S = CL ? a.S : min(a.S, max(1, (L + MINP - 1) / MINP));  // (a cluster's CTAs all take part)
+  if (split >= S) return;
   const int lo = (int)((int64_t)L * split / S), hi = (int)((int64_t)L * (split + 1) / S);
   const int wlo = lo + (int)((int64_t)(hi - lo) * warp / ATT_WARPS);
   const int whi = lo + (int)((int64_t)(hi - lo) * (warp + 1) / ATT_WARPS);
@@ -292,16 +318,39 @@ __global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G)) k_attn(co
     s_L[tid] = Lsum;
   }
   __syncthreads();
-  const size_t pbase = ((size_t)t * a.nkv + kvh) * S;  // this (row, KV head)'s first partial
+  const size_t pbase = ((size_t)t * a.nkv + kvh) * a.S;  // this (row, KV head)'s first partial
   float* const wp = a.ws + (pbase + split) * a.pstride;
   for (int e = tid; e < GH; e += ATT_THREADS) {
     const int h = e / HD;
     float o = 0.f;
     for (int w = 0; w < ATT_WARPS; w++) o = fmaf(s_o[w][e], s_w[w][h], o);
     if (S == 1) a.out[(size_t)t * a.ldo + (kvh * G + h) * HD + e % HD] = s_L[h] > 0.f ? o / s_L[h] : 0.f;
+    else if (CL) s_o[0][e] = o;  // (element e is read and rewritten by this thread only)
     else wp[e] = o;
   }
   if (S == 1) return;
+  if constexpr (CL) {
+    // after the barrier, split r finalises outputs [r GH / S, (r + 1) GH / S)
+    // from every split's partial, read from the others' shared memory in
+    // split order; the second barrier keeps the partials alive until then
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    for (int e = GH * split / S + tid; e < GH * (split + 1) / S; e += ATT_THREADS) {
+      const int h = e / HD;
+      float M = -INFINITY;
+      for (int c = 0; c < S; c++) M = fmaxf(M, *cluster.map_shared_rank(&s_M[h], c));
+      float Lsum = 0.f, o = 0.f;
+      for (int c = 0; c < S; c++) {
+        const float mc = *cluster.map_shared_rank(&s_M[h], c);
+        const float f = mc == -INFINITY ? 0.f : expf(mc - M);
+        Lsum += *cluster.map_shared_rank(&s_L[h], c) * f;
+        o = fmaf(*cluster.map_shared_rank(&s_o[0][e], c), f, o);
+      }
+      a.out[(size_t)t * a.ldo + (kvh * G + h) * HD + e % HD] = Lsum > 0.f ? o / Lsum : 0.f;
+    }
+    cluster.sync();
+    return;
+  }
   if (tid < G) {
     wp[GH + tid] = s_M[tid];
     wp[GH + G + tid] = s_L[tid];
@@ -371,11 +420,13 @@ struct AttnKernel {
 
 template <int HD, int G, typename KT>
 static cudaError_t attn_launch_t(const AttnArgs& a, dim3 grid, cudaStream_t s) {
-  return launch_pdl(k_attn<HD, G, KT>, grid, dim3(ATT_THREADS), 0, s, a);
+  if (a.ws == nullptr && a.S > 1)  // cluster merge
+    return launch_pdl_cluster(k_attn<HD, G, KT, true>, grid, dim3(ATT_THREADS), 0, a.S, s, a);
+  return launch_pdl(k_attn<HD, G, KT, false>, grid, dim3(ATT_THREADS), 0, s, a);
 }
 template <int HD, int G, typename KT>
 static AttnKernel attn_k() {
-  return AttnKernel{(const void*)k_attn<HD, G, KT>, attn_launch_t<HD, G, KT>};
+  return AttnKernel{(const void*)k_attn<HD, G, KT, false>, attn_launch_t<HD, G, KT>};
 }
 template <int HD, typename KT>
 static bool attn_kernel_hd(int G, AttnKernel* k) {
@@ -435,11 +486,22 @@ AttnPlan attn_plan(int T, int nH, int nKV, int hd, int max_ctx, int kv_type, siz
   int S = (int)std::max<int64_t>(1, target / rows_kv);
   S = std::min(S, std::max(1, (max_ctx + ATT_WARPS * PS - 1) / (ATT_WARPS * PS)));
   S = std::min(S, ATT_MAX_SPLITS);
+  // Up to 8 splits, and any split count over caches of <= kAttnClusterCtx
+  // positions, merge within a cluster: no global round trip, which the decode
+  // chain's short rows feel most.  More splits over longer caches go through
+  // the workspace.
+  if (S <= 8 || max_ctx <= kAttnClusterCtx) {
+    p.splits = std::min(S, 8);
+    p.cluster = p.splits > 1;
+    return p;
+  }
   const size_t per = (size_t)rows_kv * attn_pstride(G, hd);
-  while (S > 1 && per * S > ws_cap_floats) S--;
+  while (S > 8 && per * S > ws_cap_floats) S--;
+  if (per * S > ws_cap_floats) S = 8;  // no room: the cluster merge
   p.splits = S;
-  p.ws_floats = S > 1 ? per * S : 0;
-  p.cnt_ints = S > 1 ? (size_t)rows_kv : 0;
+  p.cluster = S <= 8;
+  p.ws_floats = p.cluster ? 0 : per * S;
+  p.cnt_ints = p.cluster ? 0 : (size_t)rows_kv;
   return p;
 }
 
@@ -449,7 +511,12 @@ int attention(const float* q, int ldq, const void* kc, const void* vc, int kv_ty
   if (T <= 0) return TN_OK;
   TN_REQUIRE(nKV > 0 && nH % nKV == 0, TN_EUNSUPPORTED, "attention: n_heads %% n_kv_heads != 0");
   TN_REQUIRE(plan.splits >= 1 && plan.splits <= ATT_MAX_SPLITS, TN_EINVAL, "attention: %d splits", plan.splits);
-  TN_REQUIRE(plan.splits == 1 || (ws && cnt), TN_EINVAL, "attention: split workspace missing");
+  TN_REQUIRE(plan.splits == 1 || plan.cluster || (ws && cnt), TN_EINVAL, "attention: split workspace missing");
+  TN_REQUIRE(!plan.cluster || plan.splits <= 8, TN_EINVAL, "attention: cluster of %d splits", plan.splits);
+  if (plan.cluster || plan.splits == 1) {
+    ws = nullptr;  // (selects the cluster merge)
+    cnt = nullptr;
+  }
   const int G = nH / nKV;
   AttnKernel k;
   if (!attn_kernel(hd, G, kv_type, &k)) {

@@ -208,10 +208,11 @@ int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs,
 
 // One-query GQA attention (web/inference-worker.js:556-564) for T rows, one
 // kernel (tn_attn.cu): CTA (split, KV head, row) over its share of the row's
-// positions; with several splits the last CTA of a (row, KV head) to finish
-// merges the partials from a workspace in split order.
+// positions; several splits merge in split order, within a thread-block
+// cluster (up to 8) or through a workspace (the last CTA of a (row, KV head)).
 struct AttnPlan {
   int splits = 1;
+  bool cluster = false;  // the splits merge within a thread-block cluster
   size_t ws_floats = 0;  // partials of the split rows
   size_t cnt_ints = 0;   // arrival counters, zero between launches
 };
