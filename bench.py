@@ -441,7 +441,7 @@ def run_ours(args):
     lo, hi = st["layers"]
     # decode positions: pipeline warm-up + timed + e2e + profiled rounds, then
     # the fused pass (warm-up + timed + e2e)
-    n_decode = 2 * args.warmup + 6 * args.steps + 4
+    n_decode = 2 * max(3, args.warmup) + 6 * args.steps + 12
     t_init = time.perf_counter()
     w = device_weights(pkg, torch, m, lo, hi, st["is_first"], st["is_last"])
     ctx = pkg.initStage({"arch": "llama", "dims": m.dims(), "layers": [lo, hi], "is_first": st["is_first"],
@@ -489,11 +489,13 @@ def run_ours(args):
     barrier()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    ev0.record(pipe.stream)
+    # K rounds in the pipeline's steady state: with several stages the call
+    # runs one round before and one after them (the fill and the drain), and
+    # each rank's events bracket its own K x M steps
+    lead = 1 if world > 1 else 0
     torch.cuda.nvtx.range_push("decode_timed")  # (profilers: --nvtx-include decode_timed/)
-    pipe.rounds(args.steps, wait=False)
+    pipe.rounds(lead + args.steps + lead, wait=False, marks={lead * M: ev0, (lead + args.steps) * M: ev1})
     torch.cuda.nvtx.range_pop()
-    ev1.record(pipe.stream)
     barrier()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     clk = clocks.stop()
@@ -506,9 +508,9 @@ def run_ours(args):
     # slot and its output goes back to the send slot, so the stages still work
     # on different micro-batches at once)
     barrier()
-    t0 = time.perf_counter()
-    pipe.rounds_host(ctx, args.steps)
-    e2e_s = max_over_ranks(time.perf_counter() - t0)
+    tm = {lead * M: None, (lead + args.steps) * M: None}
+    pipe.rounds_host(ctx, lead + args.steps + lead, marks=tm)
+    e2e_s = max_over_ranks(tm[(lead + args.steps) * M] - tm[lead * M])
     e2e_val = tokens / e2e_s
     # per round: token ids in (rank 0) and out (last rank), one fp16 frame into
     # and one out of the host API at each of the world - 1 stage boundaries

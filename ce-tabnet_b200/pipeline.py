@@ -164,10 +164,13 @@ class Pipeline:
             pass
 
     # ------------------------------------------------------------ schedule
-    def rounds(self, n_rounds: int, wait: bool = True) -> None:
+    def rounds(self, n_rounds: int, wait: bool = True, marks: dict | None = None) -> None:
         """n_rounds x M micro-batch steps on this rank, fill and drain
         included.  wait: return when this rank's work is complete (or raise
-        PipelineError at the deadline); else return once it is enqueued."""
+        PipelineError at the deadline); else return once it is enqueued.
+        marks: {j: CUDA event} recorded on the stage stream just before this
+        rank's j-th step of the call (j = n_rounds x M: after its last), so a
+        caller can time whole rounds in the pipeline's steady state."""
         import torch.distributed as dist
 
         torch, W, M, r = self.torch, self.world, self.M, self.rank
@@ -176,11 +179,18 @@ class Pipeline:
         gloo = self.device.type != "cuda"
         bufs = {"recv_token": self.tok, "recv_hidden": self.hin, "send_hidden": self.hout,
                 "send_token": self.tok_out}
+        def mark(j):
+            if marks and j in marks:
+                marks[j].record(self.stream if self.stream is not None else torch.cuda.current_stream())
+
         with self._stream_ctx():
             if W == 1:
                 for j in range(n):
+                    mark(j)
                     self._step(j % M)
+                mark(n)
             else:
+                j_local = 0
                 for tau in range(planner.pipeline_ticks(W, n)):
                     sched, mb = planner.pipeline_tick(r, W, M, n, tau)
                     ops = [dist.P2POp(dist.irecv if kind.startswith("recv") else dist.isend, bufs[kind][b], peer,
@@ -202,7 +212,10 @@ class Pipeline:
                         except Exception as e:  # a lost peer or a transport timeout
                             self._fail(tau, e, False)
                     if mb is not None:
+                        mark(j_local)
                         self._step(mb)
+                        j_local += 1
+                mark(n)
         if wait:
             self._drain(t_end)
 
@@ -224,11 +237,13 @@ class Pipeline:
                 raise PipelineError(e.code, f"rank {self.rank}: {e}", self.rank, -1) from e
 
     # ----------------------------------------------------------- host API
-    def rounds_host(self, ctx, n_rounds: int) -> None:
+    def rounds_host(self, ctx, n_rounds: int, marks: dict | None = None) -> None:
         """The same schedule with every stage step through the host-buffer API
         (tn_stage_forward): a step's input frame comes to the host from the
         receive slot and its output frame goes back to the send slot, so the
-        end-to-end path of a caller holding host buffers is timed."""
+        end-to-end path of a caller holding host buffers is timed.  marks:
+        {j: None}, filled with time.perf_counter() just before this rank's
+        j-th step of the call (j = n_rounds x M: after its last)."""
         import torch.distributed as dist
 
         from . import engine
@@ -237,6 +252,12 @@ class Pipeline:
         n = n_rounds * M
         bufs = {"recv_token": self.tok, "recv_hidden": self.hin, "send_hidden": self.hout,
                 "send_token": self.tok_out}
+        j_local = 0
+
+        def mark(j):
+            if marks is not None and j in marks:
+                marks[j] = time.perf_counter()
+
         for tau in range(planner.pipeline_ticks(W, n) if W > 1 else n):
             if W == 1:
                 sched, mb = [], tau % M
@@ -250,6 +271,8 @@ class Pipeline:
                     w.wait()
             if mb is None:
                 continue
+            mark(j_local)
+            j_local += 1
             reqs = []
             for i in range(self.rows):
                 req = {"seq_id": mb * self.rows + i, "token_pos": self.pos[mb][i], "temperature": 0}
@@ -265,6 +288,7 @@ class Pipeline:
                 else:
                     self.hout[mb, i].copy_(torch.from_numpy(out["hidden"].view(np.float16)))
             self.pos[mb] = [x + 1 for x in self.pos[mb]]
+        mark(j_local)
         if self.device.type == "cuda":
             torch.cuda.synchronize()
 
