@@ -135,15 +135,19 @@ __device__ __forceinline__ void mmv_store(const MmvArgs& a, int row, int tt, flo
 // sub-chunk sc): units [0, pool0) in contiguous runs of pool0 / gk units
 // (rounded, at least nsc each, so a (tile, chunk) is split into at most two
 // pieces: part 0 from sub-chunk 0, part 1 from a later one), and on chunks of
-// at least 8 tiles per CTA the last quarter of the tiles, [pool0, NSU), as a
-// pool of whole tiles the chunk's CTAs take in ticket order after their runs
-// -- whole tiles, so the pool adds no cross-CTA pieces -- so that CTAs that
-// got their SM slot late (and start with an empty ring) take fewer of them.
+// at least 2 tiles per CTA a pool of whole tiles [pool0, NSU) (all but one
+// tile per CTA below 8 tiles per CTA, else the last quarter) that the chunk's
+// CTAs take in ticket order after their runs -- whole tiles, so the pool adds
+// no cross-CTA pieces -- so that CTAs that got their SM slot late (and start
+// with an empty ring) take fewer of them (decode bench: 93.8 -> 96.8 tok/s
+// when the smaller matrices got their pool too).
 __host__ __device__ __forceinline__ int mmv_chunk_ctas(int grid, int ks, int kc) { return (grid - kc + ks - 1) / ks; }
 __host__ __device__ __forceinline__ int mmv_pool0(int nsu, int gk, int nsc) {
   const int q = nsu / gk;
-  if (q < 8 * nsc) return nsu;
-  const int p = (gk * (q - q / 4) + nsc - 1) / nsc * nsc;  // a tile boundary
+  if (q < 2 * nsc) return nsu;
+  // at least two tiles per CTA: one static tile each below 8, else the first
+  // three quarters static; the rest is the pool
+  const int p = q < 8 * nsc ? gk * nsc : (gk * (q - q / 4) + nsc - 1) / nsc * nsc;  // a tile boundary
   return p < nsu ? p : nsu;
 }
 // bytes of the per-warp row-sum buffers at the start of dynamic shared memory
