@@ -64,7 +64,9 @@ def parse_args(argv=None):
     p.add_argument("--tokens", default="1,4,16,64,512", help="matvec sweep: token counts")
     p.add_argument("--ctx", default="512,2048,8192,32768", help="attention sweep: cached positions")
     p.add_argument("--seqs", default="1,8,64", help="attention sweep: concurrent rows")
-    p.add_argument("--kv", default="f32,f16", help="attention sweep: KV cache element types")
+    p.add_argument("--kv", default="f32,f16,f8", help="attention sweep: KV cache element types")
+    p.add_argument("--kv-cache", choices=["f32", "f16", "f8"], default="f32",
+                   help="decode: KV cache element type (f32 = the reference's rows; f16 / f8 opt in)")
     p.add_argument("--reps", type=int, default=20, help="kernel sweeps: timed launches per point")
     return p.parse_args(argv)
 
@@ -78,7 +80,7 @@ def workload_config(args, world: int) -> dict:
     return {"workload": f"{args.model} q4_0 decode: {args.microbatches} micro-batches x 1 sequence in flight, "
                         f"{args.prompt}-token prompts, one micro-batch per stage step",
             "model": args.model, "microbatches": args.microbatches, "seqs_per_microbatch": 1,
-            "prompt_len": args.prompt, "stages": world, "parallelism": f"pp{world}",
+            "prompt_len": args.prompt, "stages": world, "parallelism": f"pp{world}", "kv_cache": args.kv_cache,
             "l2": "weights (39 GB at N=1) exceed the 126 MB L2 every step; no flush needed",
             "sampling": "greedy (temperature 0)",
             "weights": "seeded synthetic: Irwin-Hall(4) approximation of N(0, 0.02) per element, quantised "
@@ -251,15 +253,15 @@ def micro_attn(args):
     clocks.start()
     points = []
     for kv, ctx, seqs in [(k, c, n) for k in args.kv.split(",") for c in _ints(args.ctx) for n in _ints(args.seqs)]:
-        eb = 2 if kv == "f16" else 4
+        eb = {"f32": 4, "f16": 2, "f8": 1}[kv]
         slot_bytes = 2 * nKV * ctx * hd * eb
         groups = max(1, int(2 * L2_BYTES // (slot_bytes * seqs)) + 1)
         n_slots = groups * seqs
         gen = torch.Generator(device="cuda").manual_seed(ctx + seqs)
-        dt = torch.float16 if kv == "f16" else torch.float32
+        dt = {"f32": torch.float32, "f16": torch.float16, "f8": torch.float8_e4m3fn}[kv]
         K = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen).to(dt)
         V = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen).to(dt)
-        fn = lib.tn_attention_f16 if kv == "f16" else lib.tn_attention
+        fn = {"f32": lib.tn_attention, "f16": lib.tn_attention_f16, "f8": lib.tn_attention_f8}[kv]
         q = torch.randn((seqs, nH * hd), device="cuda", generator=gen)
         out = torch.empty_like(q)
         lens = torch.full((seqs,), ctx, dtype=torch.int32, device="cuda")
@@ -447,7 +449,7 @@ def run_ours(args):
     ctx = pkg.initStage({"arch": "llama", "dims": m.dims(), "layers": [lo, hi], "is_first": st["is_first"],
                          "is_last": st["is_last"], "weights": w,
                          "opts": {"device": local, "max_ctx": args.prompt + n_decode + 4, "max_seqs": M,
-                                  "max_tokens_per_step": 512}})
+                                  "max_tokens_per_step": 512, "kv_dtype": args.kv_cache}})
     del w
     torch.cuda.synchronize()
     torch.cuda.empty_cache()

@@ -22,6 +22,7 @@ TN_FLAG_NO_GRAPHS = 1
 TN_FLAG_PROFILE = 2
 TN_FLAG_NO_FUSED_DECODE = 4
 TN_FLAG_KV_F16 = 8
+TN_FLAG_KV_F8 = 16
 PROF_CLASSES = ["matvec_qkv", "matvec_o", "matvec_gate_up", "matvec_down", "matvec_lm_head", "attention",
                 "rmsnorm", "rope_kv", "other"]
 TN_TAG_EMBED, TN_TAG_NORM, TN_TAG_LM_HEAD = 1, 2, 3
@@ -121,6 +122,9 @@ SIGNATURES = [
     ("tn_attention", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_uint64, C.c_void_p]),
+    ("tn_attention_f8", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                  C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                  C.c_void_p, C.c_uint64, C.c_void_p]),
     ("tn_attention_f16", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                    C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                    C.c_void_p, C.c_uint64, C.c_void_p]),

@@ -240,9 +240,10 @@ static int attn_check(const char* fn, int32_t n_rows, int32_t n_slots, int32_t n
 extern "C" uint64_t tn_attention_scratch_bytes(int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,
                                                int32_t head_dim, int32_t max_ctx) {
   if (n_rows <= 0 || n_heads <= 0 || n_kv_heads <= 0 || head_dim <= 0 || max_ctx <= 0) return 0;
-  // (enough for either cache element type)
-  return std::max(attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, KV_F32).total,
-                  attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, KV_F16).total);
+  // (enough for every cache element type)
+  return std::max({attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, KV_F32).total,
+                   attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, KV_F16).total,
+                   attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, KV_F8).total});
 }
 
 static int attn_entry(const char* fn, int kv_type, int32_t n_rows, int32_t n_slots, int32_t n_heads,
@@ -267,6 +268,14 @@ extern "C" int tn_attention(int32_t n_rows, int32_t n_slots, int32_t n_heads, in
                             void* d_scratch, uint64_t scratch_bytes, void* stream) {
   return attn_entry("tn_attention", KV_F32, n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v,
                     d_slot, d_len, d_out, d_scratch, scratch_bytes, stream);
+}
+
+extern "C" int tn_attention_f8(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
+                               int32_t head_dim, int32_t max_ctx, const float* d_q, const uint8_t* d_k,
+                               const uint8_t* d_v, const int32_t* d_slot, const int32_t* d_len, float* d_out,
+                               void* d_scratch, uint64_t scratch_bytes, void* stream) {
+  return attn_entry("tn_attention_f8", KV_F8, n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k,
+                    d_v, d_slot, d_len, d_out, d_scratch, scratch_bytes, stream);
 }
 
 extern "C" int tn_attention_f16(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,

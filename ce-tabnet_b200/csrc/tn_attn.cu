@@ -4,7 +4,8 @@
 // softmax over the row's cached positions, weighted sum of V) for T query
 // rows at once, each row over its own sequence slot and length.  The cache
 // holds f32 rows (the reference's format, :554 and :640-653) or, opt-in,
-// fp16 rows (half the bytes; values rounded to nearest even on append).
+// fp16 or fp8 e4m3 rows (half / a quarter of the bytes; values rounded to
+// nearest even on append, e4m3 saturating at +-448).
 //
 // Work split.  CTA (split, KV head, row) streams its share of the row's
 // positions; the split count S is chosen so that the grid fills every SM
@@ -122,6 +123,40 @@ struct KvVec<__half, 1> {
   static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[1]) { o[0] = __half2float(r); }
 };
 
+// fp8 e4m3 rows: 1, 2 or 4 bytes per lane, widened pairwise through fp16 (exact)
+__device__ __forceinline__ float2 f8x2_to_float2(uint32_t b) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)(b & 0xffffu), __NV_E4M3);
+  return __half22float2(__half2(h));
+}
+template <>
+struct KvVec<__nv_fp8_e4m3, 4> {
+  using Raw = uint32_t;
+  static __device__ __forceinline__ Raw load(const __nv_fp8_e4m3* p) { return *reinterpret_cast<const uint32_t*>(p); }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[4]) {
+    const float2 a = f8x2_to_float2(r), b = f8x2_to_float2(r >> 16);
+    o[0] = a.x;
+    o[1] = a.y;
+    o[2] = b.x;
+    o[3] = b.y;
+  }
+};
+template <>
+struct KvVec<__nv_fp8_e4m3, 2> {
+  using Raw = uint16_t;
+  static __device__ __forceinline__ Raw load(const __nv_fp8_e4m3* p) { return *reinterpret_cast<const uint16_t*>(p); }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[2]) {
+    const float2 a = f8x2_to_float2(r);
+    o[0] = a.x;
+    o[1] = a.y;
+  }
+};
+template <>
+struct KvVec<__nv_fp8_e4m3, 1> {
+  using Raw = uint8_t;
+  static __device__ __forceinline__ Raw load(const __nv_fp8_e4m3* p) { return *reinterpret_cast<const uint8_t*>(p); }
+  static __device__ __forceinline__ void cvt(const Raw& r, float (&o)[1]) { o[0] = f8x2_to_float2(r).x; }
+};
+
 // after the loop lane holds the warp sum of v[lane >> (5 - log2 N)]
 template <int N>
 __device__ __forceinline__ float attn_reduce_scatter(float (&v)[N], int lane) {
@@ -159,7 +194,7 @@ __host__ __device__ constexpr int attn_prefetch_regs(int HD, int G, bool half) {
 // CL: the S splits of a (row, KV head) are one thread-block cluster and merge
 // through distributed shared memory (S <= 8); else through the workspace
 template <int HD, int G, typename KT, bool CL>
-__global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G, sizeof(KT) == 2)) k_attn(const AttnArgs a) {
+__global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G, sizeof(KT) < 4)) k_attn(const AttnArgs a) {
   constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD;
   using Vec = KvVec<KT, DPL>;
   using Raw = typename Vec::Raw;
@@ -452,14 +487,16 @@ static bool attn_kernel_kt(int hd, int G, AttnKernel* k) {
   }
 }
 static bool attn_kernel(int hd, int G, int kv_type, AttnKernel* k) {
-  return kv_type == KV_F16 ? attn_kernel_kt<__half>(hd, G, k) : attn_kernel_kt<float>(hd, G, k);
+  if (kv_type == KV_F16) return attn_kernel_kt<__half>(hd, G, k);
+  if (kv_type == KV_F8) return attn_kernel_kt<__nv_fp8_e4m3>(hd, G, k);
+  return attn_kernel_kt<float>(hd, G, k);
 }
 
 // resident CTAs per SM of a variant (looked up once per variant)
 static int attn_occupancy(int hd, int G, int kv_type) {
-  static std::atomic<int> cache[3][5][2];
+  static std::atomic<int> cache[3][5][3];
   const int hi = hd == 32 ? 0 : hd == 64 ? 1 : 2, gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : G == 8 ? 3 : 4;
-  std::atomic<int>& c = cache[hi][gi][kv_type == KV_F16 ? 1 : 0];
+  std::atomic<int>& c = cache[hi][gi][kv_type == KV_F16 ? 1 : (kv_type == KV_F8 ? 2 : 0)];
   int o = c.load(std::memory_order_relaxed);
   if (o > 0) return o;
   AttnKernel k;

@@ -4,6 +4,7 @@
 #include <cuda.h>  // CUtensorMap (the encoder is fetched from the driver at run time)
 
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include "tn_common.cuh"
 
@@ -156,12 +157,16 @@ size_t gemm_counter_offset(int T, int cols);
 int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, float* y, int ldy, int mode,
          void* scratch, size_t scratch_bytes, int* err, cudaStream_t s);
 
-// Element type of a KV cache: f32 (the reference's rows) or, opt-in, fp16
-// (rounded to nearest even when appended).
-enum KvType { KV_F32 = 0, KV_F16 = 1 };
-__host__ __device__ constexpr size_t kv_elem_bytes(int kv_type) { return kv_type == KV_F16 ? 2 : 4; }
+// Element type of a KV cache: f32 (the reference's rows) or, opt-in, fp16 or
+// fp8 e4m3 (rounded to nearest even when appended; e4m3 saturates at +-448
+// and carries no scale).
+enum KvType { KV_F32 = 0, KV_F16 = 1, KV_F8 = 2 };
+__host__ __device__ constexpr size_t kv_elem_bytes(int kv_type) {
+  return kv_type == KV_F16 ? 2 : (kv_type == KV_F8 ? 1 : 4);
+}
 __device__ __forceinline__ void kv_store(void* base, size_t i, int kv_type, float v) {
   if (kv_type == KV_F16) reinterpret_cast<__half*>(base)[i] = __float2half_rn(v);
+  else if (kv_type == KV_F8) reinterpret_cast<__nv_fp8_e4m3*>(base)[i] = __nv_fp8_e4m3(v);
   else reinterpret_cast<float*>(base)[i] = v;
 }
 

@@ -258,7 +258,9 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   st->max_seqs = sp->max_seqs > 0 ? sp->max_seqs : 16;
   st->max_T = sp->max_tokens_per_step > 0 ? sp->max_tokens_per_step : 512;
   st->flags = sp->flags;
-  st->kv_type = (sp->flags & TN_FLAG_KV_F16) ? KV_F16 : KV_F32;
+  st->kv_type = (sp->flags & TN_FLAG_KV_F8) ? KV_F8 : ((sp->flags & TN_FLAG_KV_F16) ? KV_F16 : KV_F32);
+  TN_REQUIRE(!((sp->flags & TN_FLAG_KV_F8) && (sp->flags & TN_FLAG_KV_F16)), TN_EINVAL,
+             "TN_FLAG_KV_F16 and TN_FLAG_KV_F8 exclude each other");
   TN_REQUIRE(st->hd == 32 || st->hd == 64 || st->hd == 128, TN_EUNSUPPORTED,
              "head_dim %d unsupported (32, 64, 128)", st->hd);
   TN_REQUIRE(st->nH % st->nKV == 0 && (st->nH / st->nKV) <= 16 &&

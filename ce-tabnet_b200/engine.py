@@ -103,7 +103,8 @@ def initStage(spec: dict) -> StageCtx:
             layers:[lo, hi], is_first, is_last,
             weights:{layers:[{idx, buf, quant}], embed?, norm?, lm_head?, embedQuant?, lmHeadQuant?, quant?},
             opts?:{max_ctx, max_seqs, max_tokens_per_step, device, hop_mode, no_graphs,
-                   kv_dtype: "f32" (default, the reference's rows) | "f16" (half-size KV cache)}}
+                   kv_dtype: "f32" (default, the reference's rows) | "f16" (half-size KV cache)
+                             | "f8" (e4m3, quarter-size)}}
     """
     lib = _lib.load()
     dims, (lo, hi), w = spec["dims"], spec["layers"], spec["weights"]
@@ -148,10 +149,14 @@ def initStage(spec: dict) -> StageCtx:
     s.max_ctx = int(opts.get("max_ctx", 4096))  # :642
     s.max_seqs = int(opts.get("max_seqs", 16))
     s.max_tokens_per_step = int(opts.get("max_tokens_per_step", 512))
+    kv_dtype = opts.get("kv_dtype", "f32")
+    if kv_dtype not in ("f32", "f16", "f8"):
+        raise ValueError(f"opts.kv_dtype must be 'f32', 'f16' or 'f8', not {kv_dtype!r}")
     s.flags = (_lib.TN_FLAG_NO_GRAPHS if opts.get("no_graphs") else 0) | \
         (_lib.TN_FLAG_PROFILE if opts.get("profile") else 0) | \
         (_lib.TN_FLAG_NO_FUSED_DECODE if opts.get("fused_decode") is False else 0) | \
-        (_lib.TN_FLAG_KV_F16 if opts.get("kv_dtype") == "f16" else 0)
+        (_lib.TN_FLAG_KV_F16 if kv_dtype == "f16" else 0) | \
+        (_lib.TN_FLAG_KV_F8 if kv_dtype == "f8" else 0)
     handle = C.c_void_p()
     _lib.check(lib.tn_stage_init(C.byref(s), C.byref(handle)))
     return StageCtx(handle=handle, dims=dict(dims), layers=(lo, hi), is_first=bool(spec.get("is_first")),

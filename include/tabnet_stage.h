@@ -53,6 +53,7 @@ enum { TN_HOP_LAST = 0, TN_HOP_ALL = 1 };
 #define TN_FLAG_PROFILE (1u << 1)   /* time every kernel launch with CUDA events (tn_stage_profile) */
 #define TN_FLAG_NO_FUSED_DECODE (1u << 2) /* decode steps use the separate norm / matvec / RoPE kernels */
 #define TN_FLAG_KV_F16 (1u << 3)          /* KV cache of fp16 rows (half the bytes; the reference keeps f32) */
+#define TN_FLAG_KV_F8 (1u << 4)           /* KV cache of fp8 e4m3 rows (a quarter; saturates at +-448, no scale) */
 
 /* One layer's packed buffer, tensors in web/inference-worker.js:142-159 order:
  * attn_norm(f16) wq wk wv wo ffn_norm(f16) w_gate w_up w_down. */
@@ -240,6 +241,13 @@ int tn_attention_f16(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n
                      int32_t max_ctx, const float* d_q, const uint16_t* d_k, const uint16_t* d_v,
                      const int32_t* d_slot, const int32_t* d_len, float* d_out, void* d_scratch,
                      uint64_t scratch_bytes, void* stream);
+
+/* tn_attention over an fp8 e4m3 KV cache (one byte a value, same layout): the
+ * cache format of stages created with TN_FLAG_KV_F8.  Computed in f32. */
+int tn_attention_f8(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                    int32_t max_ctx, const float* d_q, const uint8_t* d_k, const uint8_t* d_v,
+                    const int32_t* d_slot, const int32_t* d_len, float* d_out, void* d_scratch,
+                    uint64_t scratch_bytes, void* stream);
 
 /* tn_attention without a scratch argument, for callers that cannot allocate
  * device memory.  This entry point has no counterpart in the reference.

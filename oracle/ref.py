@@ -23,6 +23,7 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "libref_cpu.so"
 QUANT = {"f32": 0, "f16": 1, "q4_0": 2, "q8_0": 3}
+KV_FORMAT = {"f32": 0, "f16": 1, "f8": 2}
 _lib = None
 
 
@@ -66,7 +67,9 @@ def load() -> C.CDLL:
         lib.ref_kv_len.argtypes = [C.c_void_p, C.c_uint64]
         lib.ref_kv_row.argtypes = [C.c_void_p, C.c_uint64, C.c_int, C.c_int, C.c_void_p, C.c_void_p]
         lib.ref_free.argtypes = [C.c_void_p]
-        lib.ref_set_kv_f16.argtypes = [C.c_void_p, C.c_int]
+        lib.ref_set_kv_format.argtypes = [C.c_void_p, C.c_int]
+        lib.ref_round_kv.argtypes = [C.c_int, C.c_float]
+        lib.ref_round_kv.restype = C.c_float
         _lib = lib
     return _lib
 
@@ -151,7 +154,7 @@ class RefStage:
     """initStage / forward / freeStage of the reference CPU path."""
 
     def __init__(self, dims: dict, lo: int, hi: int, is_first: bool, is_last: bool, weights: dict,
-                 n_threads: int | None = None, kv_f16: bool = False):
+                 n_threads: int | None = None, kv_dtype: str = "f32"):
         lib = load()
         self.H = int(dims["hidden_dim"])
         self.vocab = int(dims["vocab"])
@@ -188,10 +191,10 @@ class RefStage:
         self.h = lib.ref_init(C.byref(s))
         if not self.h:
             raise ValueError("ref_init failed")
-        # not part of the reference: K / V rows stored as binary16, the opt-in
-        # cache format of the GPU stage (TN_FLAG_KV_F16)
-        if kv_f16:
-            lib.ref_set_kv_f16(self.h, 1)
+        # not part of the reference: K / V rows stored as binary16 or fp8 e4m3,
+        # the opt-in cache formats of the GPU stage (TN_FLAG_KV_F16 / _F8)
+        if kv_dtype != "f32":
+            lib.ref_set_kv_format(self.h, KV_FORMAT[kv_dtype])
 
     def forward(self, seq_id: int, token_pos: int, token_ids=None, hidden=None, temperature: float = 0.0,
                 top_p: float = 0.95, u: float = 0.0) -> dict:

@@ -322,7 +322,7 @@ struct ref_stage {
   float* final_norm;    /* [H] */
   ref_seq* seqs;
   int n_seqs, cap_seqs;
-  int kv_f16; /* not in the reference: KV rows rounded to binary16 when pushed */
+  int kv_fmt; /* not in the reference: KV rows rounded to binary16 (1) or e4m3 (2) when pushed */
 };
 
 /* x rounded to the nearest binary16 value (ties to even), as a float: the
@@ -345,7 +345,31 @@ static float round_f16(float x) {
   return rintf(x * 16777216.0f) * (1.0f / 16777216.0f);
 }
 
-void ref_set_kv_f16(ref_stage* st, int on) { st->kv_f16 = on != 0; }
+/* x rounded to the nearest fp8 e4m3 value (OCP FP8 E4M3: bias 7, 3 mantissa
+   bits, largest finite 448, no infinities), ties to even, saturating finite:
+   the stored value of an fp8 KV cache.  NaN stays NaN. */
+static float round_e4m3(float x) {
+  if (isnan(x)) return x;
+  const float a = fabsf(x);
+  float r;
+  if (isinf(a)) {
+    r = 448.0f;
+  } else if (a >= 0.015625f) { /* normal: 2^e <= a < 2^(e+1), quantum 2^(e-3) */
+    int E;
+    frexpf(a, &E); /* a = m 2^E, 0.5 <= m < 1, so e = E - 1 */
+    r = ldexpf(rintf(ldexpf(a, 4 - E)), E - 4);
+    if (r > 448.0f) r = 448.0f;
+  } else { /* subnormal: multiples of 2^-9 */
+    r = rintf(a * 512.0f) * (1.0f / 512.0f);
+  }
+  return signbit(x) ? -r : r;
+}
+
+static float round_kv(int fmt, float x) { return fmt == 1 ? round_f16(x) : (fmt == 2 ? round_e4m3(x) : x); }
+
+void ref_set_kv_format(ref_stage* st, int fmt) { st->kv_fmt = (fmt == 1 || fmt == 2) ? fmt : 0; }
+
+float ref_round_kv(int fmt, float x) { return round_kv(fmt, x); }
 
 static ref_seq* find_seq(ref_stage* st, uint64_t id, int create) {
   for (int i = 0; i < st->n_seqs; i++)
@@ -451,10 +475,10 @@ static int run_layers(ref_stage* st, ref_seq* kv, int pos, float* h) {
     rc |= ref_matvec_packed(b + Ll.off[3], quant, kvDim, H, xn, v, nt);
     ref_rope(q, nH, hd, pos, sp->rope_theta);
     ref_rope(k, nKV, hd, pos, sp->rope_theta);
-    if (st->kv_f16)
+    if (st->kv_fmt)
       for (int i = 0; i < kvDim; i++) {
-        k[i] = round_f16(k[i]);
-        v[i] = round_f16(v[i]);
+        k[i] = round_kv(st->kv_fmt, k[i]);
+        v[i] = round_kv(st->kv_fmt, v[i]);
       }
     memcpy(kv->K[li] + (size_t)kv->len * kvDim, k, sizeof(float) * (size_t)kvDim); /* :554 push */
     memcpy(kv->V[li] + (size_t)kv->len * kvDim, v, sizeof(float) * (size_t)kvDim);

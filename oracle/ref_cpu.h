@@ -103,9 +103,12 @@ int ref_forward(ref_stage* st, uint64_t seq_id, int token_pos, const int32_t* to
 int ref_kv_len(ref_stage* st, uint64_t seq_id);
 /* copy of the cached K/V row (layer li, row s) */
 int ref_kv_row(ref_stage* st, uint64_t seq_id, int li, int s, float* k_out, float* v_out);
-/* Not in the reference: store K / V rows rounded to binary16 (ties to even),
-   the opt-in fp16 KV cache of the GPU stage. */
-void ref_set_kv_f16(ref_stage* st, int on);
+/* Not in the reference: store K / V rows rounded (ties to even) to binary16
+   (fmt 1) or to fp8 e4m3 saturating at +-448 (fmt 2), the opt-in fp16 / fp8
+   KV caches of the GPU stage; fmt 0 keeps f32 rows. */
+void ref_set_kv_format(ref_stage* st, int fmt);
+/* the rounding ref_set_kv_format applies, for one value */
+float ref_round_kv(int fmt, float x);
 void ref_free(ref_stage* st);
 
 #ifdef __cplusplus

@@ -134,7 +134,7 @@ def test_oracle_fp16_kv_rows_are_rounded_f32_rows(ref, pkg):
     w = pkg.pack.synth_weights(m, 0, m.n_layers, True, True)
     kv_dim = m.n_kv_heads * (m.hidden_dim // m.n_heads)
     full = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
-    half = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w, kv_f16=True)
+    half = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w, kv_dtype="f16")
     prompt = pkg.pack.synth_prompt(m, 5)
     a = full.forward(1, 0, token_ids=prompt)
     b = half.forward(1, 0, token_ids=prompt)
@@ -147,3 +147,45 @@ def test_oracle_fp16_kv_rows_are_rounded_f32_rows(ref, pkg):
         assert np.array_equal(k16, k16.astype(np.float16).astype(np.float32))  # every row holds fp16 values
     assert b["token_id"] == a["token_id"]
     assert float(np.max(np.abs(b["logits"] - a["logits"])) / np.max(np.abs(a["logits"]))) < 1e-2
+
+
+def test_oracle_e4m3_rounding_matches_torch(ref):
+    """The oracle's fp8 e4m3 rounding (the GPU stage's opt-in TN_FLAG_KV_F8
+    cache format) against torch's float8_e4m3fn conversion: nearest, ties to
+    even, subnormals down to 2^-9, saturating to +-448 (torch is given the
+    clipped value; it does not saturate)."""
+    import torch
+    lib = ref.load()
+    rng = np.random.default_rng(5)
+    x = np.concatenate([rng.standard_normal(4000).astype(np.float32) * s for s in (1e-3, 1e-2, 0.1, 1, 10, 100)])
+    edge = [0.0, -0.0, 2.0 ** -6, 2.0 ** -7, 2.0 ** -9, 2.0 ** -10, 1.5 * 2 ** -10, 2.5 * 2 ** -9, 3.5 * 2 ** -9,
+            1.0625, 1.1875, 447.0, 448.0, 449.0, 463.9, 464.0, 480.0, 1e6, -1e6]
+    x = np.concatenate([x, np.array(edge, np.float32)])
+    got = np.array([lib.ref_round_kv(2, float(v)) for v in x], np.float32)
+    want = torch.from_numpy(np.clip(x, -448, 448)).to(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(got, want)
+    assert lib.ref_round_kv(2, float("inf")) == 448.0 and np.isnan(lib.ref_round_kv(2, float("nan")))
+
+
+def test_oracle_fp8_kv_rows_are_e4m3_values(ref, pkg):
+    """With the fp8-cache mode every stored K / V value is an e4m3 value and
+    layer 0 of position 0 holds exactly the rounded f32 rows."""
+    import torch
+    m = pkg.pack.MODELS["tiny"]
+    w = pkg.pack.synth_weights(m, 0, m.n_layers, True, True)
+    kv_dim = m.n_kv_heads * (m.hidden_dim // m.n_heads)
+    full = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
+    q8 = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w, kv_dtype="f8")
+    prompt = pkg.pack.synth_prompt(m, 5)
+    full.forward(1, 0, token_ids=prompt)
+    q8.forward(1, 0, token_ids=prompt)
+
+    def e4m3(a):
+        return torch.from_numpy(np.clip(a, -448, 448)).to(torch.float8_e4m3fn).float().numpy()
+
+    for s in range(len(prompt)):
+        k32, v32 = full.kv_row(1, 0, s, kv_dim)
+        k8, v8 = q8.kv_row(1, 0, s, kv_dim)
+        if s == 0:
+            assert np.array_equal(k8, e4m3(k32)) and np.array_equal(v8, e4m3(v32))
+        assert np.array_equal(k8, e4m3(k8)) and np.array_equal(v8, e4m3(v8))

@@ -152,7 +152,12 @@ def test_matvec_back_to_back_same_matrix(pkg, ref, torch_cuda):
 
 def _kv_cache(torch, K, V, kv):
     """Device copies of the cache in format kv, and the values the oracle sees
-    (an fp16 cache holds the f32 values rounded to nearest even)."""
+    (an fp16 or fp8 e4m3 cache holds the f32 values rounded to nearest even)."""
+    if kv == "f8":
+        K8 = torch.from_numpy(K).to(torch.float8_e4m3fn)
+        V8 = torch.from_numpy(V).to(torch.float8_e4m3fn)
+        return (K8.view(torch.uint8).cuda(), V8.view(torch.uint8).cuda(), K8.float().numpy(),
+                V8.float().numpy())
     if kv == "f16":
         K, V = K.astype(np.float16), V.astype(np.float16)
         return torch.from_numpy(K).cuda(), torch.from_numpy(V).cuda(), K.astype(np.float32), V.astype(np.float32)
@@ -160,15 +165,15 @@ def _kv_cache(torch, K, V, kv):
 
 
 def _attn_call(pkg, lib, kv, *args):
-    fn = lib.tn_attention_f16 if kv == "f16" else lib.tn_attention
+    fn = {"f32": lib.tn_attention, "f16": lib.tn_attention_f16, "f8": lib.tn_attention_f8}[kv]
     pkg._lib.check(fn(*args))
 
 
-@pytest.mark.parametrize("kv", ["f32", "f16"])
+@pytest.mark.parametrize("kv", ["f32", "f16", "f8"])
 @pytest.mark.parametrize("hd,nH,nKV", [(128, 32, 8), (128, 64, 8), (32, 8, 2), (64, 64, 4)])
 def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV, kv):
-    """Rows of 1 .. 2100 positions; an fp16 cache is compared with the oracle
-    on the same rounded values (only the storage format differs)."""
+    """Rows of 1 .. 2100 positions; an fp16 or fp8 cache is compared with the
+    oracle on the same rounded values (only the storage format differs)."""
     torch = torch_cuda
     lib = pkg._lib.load()
     max_ctx, n_slots = 2100, 3
@@ -201,10 +206,11 @@ def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV, kv):
     (512, 1, 1, "f32"), (1024, 1, 1, "f32"), (2048, 8, 8, "f32"), (2048, 64, 16, "f32"), (8192, 1, 1, "f32"),
     (8192, 8, 4, "f32"), (8192, 64, 8, "f32"), (32768, 1, 1, "f32"), (32768, 8, 2, "f32"), (32768, 64, 8, "f32"),
     (1024, 1, 1, "f16"), (8192, 8, 4, "f16"), (32768, 1, 1, "f16"), (32768, 8, 2, "f16"),
+    (1024, 1, 1, "f8"), (8192, 8, 4, "f8"), (32768, 1, 1, "f8"), (32768, 64, 8, "f8"),
 ])
 def test_attention_context_sweep(pkg, ref, torch_cuda, L, n_rows, n_slots, kv):
     """The GQA decode-attention sweep (32 query / 8 KV heads x 128, contexts
-    512 .. 32768, 1 .. 64 concurrent rows, f32 and fp16 caches) against the
+    512 .. 32768, 1 .. 64 concurrent rows, f32, fp16 and fp8 caches) against the
     oracle.  Few rows split every row's positions over many CTAs; two
     launches back to back give identical bits (the merge runs in split order
     and the last CTA resets the arrival counters)."""
