@@ -65,6 +65,9 @@ def parse_args(argv=None):
     p.add_argument("--ctx", default="512,2048,8192,32768", help="attention sweep: cached positions")
     p.add_argument("--seqs", default="1,8,64", help="attention sweep: concurrent rows")
     p.add_argument("--kv", default="f32,f16,f8", help="attention sweep: KV cache element types")
+    p.add_argument("--heads", default="32,8", help="attention sweep: query heads, KV heads")
+    p.add_argument("--page-tokens", type=int, default=0,
+                   help="attention sweep: paged cache with pages of this many positions (0: contiguous)")
     p.add_argument("--kv-cache", choices=["f32", "f16", "f8"], default="f32",
                    help="decode: KV cache element type (f32 = the reference's rows; f16 / f8 opt in)")
     p.add_argument("--reps", type=int, default=20, help="kernel sweeps: timed launches per point")
@@ -239,7 +242,9 @@ def micro_matvec(args):
 def micro_attn(args):
     """The GQA decode-attention sweep: tn_attention over seqs rows of ctx
     cached positions, each launch on other sequence slots of an arena larger
-    than twice the L2."""
+    than twice the L2 (or, with --page-tokens, on the same rows as pages of a
+    shuffled pool).  Device time per call from a CUDA graph of `reps` calls:
+    each the row-table kernel and the attention kernel."""
     import torch
 
     import __graft_entry__ as g
@@ -247,11 +252,13 @@ def micro_attn(args):
     pkg = g.load_package()
     lib, P = pkg._lib.load(), pkg._lib
     torch.cuda.set_device(0)
-    nH, nKV, hd = 32, 8, 128
+    nH, nKV = _ints(args.heads)
+    hd = 128
     hbm, hbm_kind = measured_peaks()
     clocks = ClockSampler(physical_gpu(0))
     clocks.start()
     points = []
+    stream = torch.cuda.Stream()
     for kv, ctx, seqs in [(k, c, n) for k in args.kv.split(",") for c in _ints(args.ctx) for n in _ints(args.seqs)]:
         eb = {"f32": 4, "f16": 2, "f8": 1}[kv]
         slot_bytes = 2 * nKV * ctx * hd * eb
@@ -259,8 +266,20 @@ def micro_attn(args):
         n_slots = groups * seqs
         gen = torch.Generator(device="cuda").manual_seed(ctx + seqs)
         dt = {"f32": torch.float32, "f16": torch.float16, "f8": torch.float8_e4m3fn}[kv]
-        K = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen).to(dt)
-        V = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen).to(dt)
+        K = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen)
+        V = torch.randn((n_slots, nKV, ctx, hd), device="cuda", generator=gen)
+        if args.page_tokens:
+            # the same rows as pages of a pool: slot s's positions in ctx / pt
+            # pages, handed out in a shuffled order
+            pt = args.page_tokens
+            per = ctx // pt
+            K = K.view(n_slots, nKV, per, pt, hd).transpose(1, 2).reshape(n_slots * per, nKV, pt, hd)
+            V = V.view(n_slots, nKV, per, pt, hd).transpose(1, 2).reshape(n_slots * per, nKV, pt, hd)
+            perm = torch.randperm(n_slots * per, generator=torch.Generator().manual_seed(ctx)).to(torch.int32)
+            K[perm.long().cuda()] = K.clone()
+            V[perm.long().cuda()] = V.clone()
+            tables = [perm.view(n_slots, per)[g0 * seqs:(g0 + 1) * seqs].contiguous().cuda() for g0 in range(groups)]
+        K, V = K.to(dt), V.to(dt)
         fn = {"f32": lib.tn_attention, "f16": lib.tn_attention_f16, "f8": lib.tn_attention_f8}[kv]
         q = torch.randn((seqs, nH * hd), device="cuda", generator=gen)
         out = torch.empty_like(q)
@@ -269,32 +288,51 @@ def micro_attn(args):
         nbytes = lib.tn_attention_scratch_bytes(seqs, nH, nKV, hd, ctx)
         scratch = torch.empty(max(nbytes, 256), dtype=torch.uint8, device="cuda")
 
-        def call(i):
-            P.check(fn(seqs, n_slots, nH, nKV, hd, ctx, q.data_ptr(), K.data_ptr(), V.data_ptr(),
-                       slots[i % groups].data_ptr(), lens.data_ptr(), out.data_ptr(), scratch.data_ptr(), nbytes,
-                       None))
+        if args.page_tokens:
+            code = {"f32": 0, "f16": 1, "f8": 2}[kv]
 
-        for i in range(max(3, args.warmup)):
-            call(i)
-        torch.cuda.synchronize()
+            def call(i):
+                P.check(lib.tn_attention_paged(code, seqs, nH, nKV, hd, pt, per, n_slots * per, q.data_ptr(),
+                                               K.data_ptr(), V.data_ptr(), tables[i % groups].data_ptr(),
+                                               lens.data_ptr(), out.data_ptr(), scratch.data_ptr(), nbytes,
+                                               stream.cuda_stream))
+        else:
+            def call(i):
+                P.check(fn(seqs, n_slots, nH, nKV, hd, ctx, q.data_ptr(), K.data_ptr(), V.data_ptr(),
+                           slots[i % groups].data_ptr(), lens.data_ptr(), out.data_ptr(), scratch.data_ptr(),
+                           nbytes, stream.cuda_stream))
+
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for i in range(args.reps):
-            call(i)
-        e1.record()
-        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            for i in range(max(3, args.warmup)):
+                call(i)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(args.reps):
+                    call(i)
+            for _ in range(3):
+                graph.replay()
+            stream.synchronize()
+            e0.record(stream)
+            graph.replay()
+            e1.record(stream)
+            stream.synchronize()
         us = e0.elapsed_time(e1) / args.reps * 1e3
+        del graph
         byts = seqs * ctx * 2 * nKV * hd * eb + 2 * seqs * nH * hd * 4
         gbs = byts / us / 1e3
-        points.append({"kv": kv, "ctx": ctx, "seqs": seqs, "us": round(us, 2), "GB_s": round(gbs, 1),
+        points.append({"kv": kv, "ctx": ctx, "seqs": seqs, "page_tokens": args.page_tokens, "us": round(us, 2),
+                       "GB_s": round(gbs, 1),
                        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                                     "frac": round(gbs / hbm, 4), "peak_source": hbm_kind},
                        "arena_MB": round(n_slots * slot_bytes / 1e6, 1)})
-        print(f"# attn kv={kv} ctx={ctx} seqs={seqs}: {us:.1f} us, {gbs:.0f} GB/s", file=sys.stderr, flush=True)
+        print(f"# attn kv={kv} heads={nH}/{nKV} ctx={ctx} seqs={seqs} page={args.page_tokens}: {us:.1f} us, "
+              f"{gbs:.0f} GB/s", file=sys.stderr, flush=True)
         del K, V
         torch.cuda.empty_cache()
     clk = clocks.stop()
-    print(json.dumps({"micro": "attn", "metric": "GQA decode attention HBM GB/s (32/8 heads x 128, f32 / fp16 KV)",
+    print(json.dumps({"micro": "attn", "metric": f"GQA decode attention HBM GB/s ({nH}/{nKV} heads x 128)",
                       "unit": "GB/s", "points": points, "clocks": clk, "reps": args.reps,
                       "config": {"l2": "launches rotate over sequence slots of an arena > 2 x L2",
                                  "values": "q f32, K / V N(0,1) stored as the point's kv type"}}), flush=True)

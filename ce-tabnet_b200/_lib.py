@@ -11,7 +11,7 @@ from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libtabnet_stage.so"
 
-TN_ABI_VERSION = 1
+TN_ABI_VERSION = 2
 TN_OK, TN_EINVAL, TN_ENOMEM, TN_ECUDA, TN_EUNSUPPORTED, TN_ECAPACITY, TN_ESTATE, TN_ETIMEOUT = (
     0, -1, -2, -3, -4, -5, -6, -7)
 STATUS_NAMES = {0: "TN_OK", -1: "TN_EINVAL", -2: "TN_ENOMEM", -3: "TN_ECUDA", -4: "TN_EUNSUPPORTED",
@@ -55,6 +55,7 @@ class StageSpec(C.Structure):
         ("device", C.c_int32), ("max_ctx", C.c_int32), ("max_seqs", C.c_int32),
         ("max_tokens_per_step", C.c_int32),
         ("flags", C.c_uint32),
+        ("kv_page_tokens", C.c_int32), ("kv_pages", C.c_int32),
     ]
 
 
@@ -122,6 +123,9 @@ SIGNATURES = [
     ("tn_attention", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                C.c_void_p, C.c_uint64, C.c_void_p]),
+    ("tn_attention_paged", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
+                                     C.c_int32, C.c_int32, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                     C.c_void_p, C.c_void_p, C.c_void_p, C.c_uint64, C.c_void_p]),
     ("tn_attention_f8", C.c_int, [C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_int32,
                                   C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                   C.c_void_p, C.c_uint64, C.c_void_p]),

@@ -36,6 +36,25 @@ __global__ void k_rows_from_slots(const int32_t* __restrict__ slot, const int32_
   rows[r] = RowInfo{s, 0, 0, l > max_ctx ? max_ctx : l};
 }
 
+// the row table of tn_attention_paged's rows (row r reads page-table row r);
+// a row whose used page ids leave [0, n_pages) gets no positions
+__global__ void k_rows_from_pages(const int32_t* __restrict__ pages, const int32_t* __restrict__ len, int n,
+                                  int max_pages, int shift, int n_pages, RowInfo* __restrict__ rows,
+                                  int* __restrict__ cnt, int n_cnt) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  for (int i = r; i < n_cnt; i += gridDim.x * blockDim.x) cnt[i] = 0;
+  if (r >= n) return;
+  const int max_ctx = max_pages << shift;
+  int l = len[r];
+  l = l < 1 ? 0 : (l > max_ctx ? max_ctx : l);
+  const int used = (l + (1 << shift) - 1) >> shift;
+  for (int j = 0; j < used; j++) {
+    const int pg = pages[(size_t)r * max_pages + j];
+    if (pg < 0 || pg >= n_pages) l = 0;
+  }
+  rows[r] = RowInfo{r, 0, 0, l};
+}
+
 // The kernels' bounded mbarrier wait (mbar_wait) on a barrier that no thread
 // arrives at, with a limit of `limit` cycles: the wait gives up, the CTA's
 // abort flag is raised, and the status says so -- the path a real kernel takes
@@ -221,9 +240,11 @@ static int attn_run(int n_rows, int n_slots, int n_heads, int n_kv_heads, int he
   const int work = std::max(n_rows, n_cnt);
   k_rows_from_slots<<<(work + 127) / 128, 128, 0, s>>>(d_slot, d_len, n_rows, n_slots, max_ctx, rows, cnt, n_cnt);
   TN_CHECK_LAUNCH();
-  const size_t kvh_stride = (size_t)max_ctx * head_dim;
-  return attention(d_q, n_heads * head_dim, d_k, d_v, kv_type, kvh_stride * n_kv_heads, kvh_stride, rows, n_rows,
-                   n_heads, n_kv_heads, head_dim, sc.plan, d_out, n_heads * head_dim, ws, cnt, s);
+  KvMap kv;
+  kv.kvh_stride = (size_t)max_ctx * head_dim;
+  kv.slot_stride = kv.kvh_stride * n_kv_heads;
+  return attention(d_q, n_heads * head_dim, d_k, d_v, kv_type, kv, rows, n_rows, n_heads, n_kv_heads, head_dim,
+                   sc.plan, d_out, n_heads * head_dim, ws, cnt, s);
 }
 
 static int attn_check(const char* fn, int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n_kv_heads,
@@ -284,6 +305,51 @@ extern "C" int tn_attention_f16(int32_t n_rows, int32_t n_slots, int32_t n_heads
                                 void* d_scratch, uint64_t scratch_bytes, void* stream) {
   return attn_entry("tn_attention_f16", KV_F16, n_rows, n_slots, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k,
                     d_v, d_slot, d_len, d_out, d_scratch, scratch_bytes, stream);
+}
+
+extern "C" int tn_attention_paged(int32_t kv_type, int32_t n_rows, int32_t n_heads, int32_t n_kv_heads,
+                                  int32_t head_dim, int32_t page_tokens, int32_t max_pages, int32_t n_pages,
+                                  const float* d_q, const void* d_k, const void* d_v, const int32_t* d_pages,
+                                  const int32_t* d_len, float* d_out, void* d_scratch, uint64_t scratch_bytes,
+                                  void* stream) {
+  clear_error();
+  TN_REQUIRE(kv_type == KV_F32 || kv_type == KV_F16 || kv_type == KV_F8, TN_EINVAL,
+             "tn_attention_paged: kv_type %d", kv_type);
+  TN_REQUIRE(page_tokens >= 16 && page_tokens <= 4096 && (page_tokens & (page_tokens - 1)) == 0, TN_EINVAL,
+             "tn_attention_paged: page_tokens %d (a power of two in [16, 4096])", page_tokens);
+  TN_REQUIRE(max_pages > 0 && max_pages + 1 <= kAttnMaxPages && n_pages > 0, TN_EINVAL,
+             "tn_attention_paged: max_pages %d (1 .. %d), n_pages %d", max_pages, kAttnMaxPages - 1, n_pages);
+  const int max_ctx = max_pages * page_tokens;
+  int rc = attn_check("tn_attention_paged", n_rows, 1, n_heads, n_kv_heads, head_dim, max_ctx, d_q, d_k, d_v,
+                      d_pages, d_len, d_out);
+  if (rc) return rc;
+  TN_REQUIRE(d_scratch, TN_EINVAL, "tn_attention_paged: null scratch");
+  TN_REQUIRE((reinterpret_cast<uintptr_t>(d_scratch) & 255) == 0, TN_EINVAL,
+             "tn_attention_paged: scratch must be 256-byte aligned");
+  if (n_rows == 0) return TN_OK;
+  const AttnScratch sc = attn_scratch(n_rows, n_heads, n_kv_heads, head_dim, max_ctx, kv_type, scratch_bytes);
+  TN_REQUIRE(sc.total <= scratch_bytes, TN_EINVAL, "attention: scratch of %llu bytes, %zu needed",
+             (unsigned long long)scratch_bytes, sc.total);
+  int shift = 0;
+  while ((1 << shift) < page_tokens) shift++;
+  char* base = (char*)d_scratch;
+  RowInfo* rows = (RowInfo*)base;
+  int* cnt = sc.plan.splits > 1 ? (int*)(base + sc.cnt_off) : nullptr;
+  float* ws = sc.plan.splits > 1 ? (float*)(base + sc.ws_off) : nullptr;
+  const int n_cnt = cnt ? (int)sc.plan.cnt_ints : 0;
+  const int work = std::max((int)n_rows, n_cnt);
+  const cudaStream_t s = (cudaStream_t)stream;
+  k_rows_from_pages<<<(work + 127) / 128, 128, 0, s>>>(d_pages, d_len, n_rows, max_pages, shift, n_pages, rows, cnt,
+                                                       n_cnt);
+  TN_CHECK_LAUNCH();
+  KvMap kv;
+  kv.kvh_stride = (size_t)page_tokens * head_dim;
+  kv.slot_stride = kv.kvh_stride * n_kv_heads;
+  kv.pages = d_pages;
+  kv.max_pages = max_pages;
+  kv.shift = shift;
+  return attention(d_q, n_heads * head_dim, d_k, d_v, kv_type, kv, rows, n_rows, n_heads, n_kv_heads, head_dim,
+                   sc.plan, d_out, n_heads * head_dim, ws, cnt, s);
 }
 
 // ---- tn_attention_static: attention with its scratch in a fixed device array,

@@ -50,7 +50,7 @@ struct AttnArgs {
   int ldq;
   const void* kc;  // KT elements
   const void* vc;
-  size_t slot_stride, kvh_stride;  // in elements
+  KvMap kv;  // the rows' places in the cache
   const RowInfo* rows;
   int S, nkv;
   float scale;
@@ -192,8 +192,9 @@ __host__ __device__ constexpr int attn_prefetch_regs(int HD, int G, bool half) {
 }
 
 // CL: the S splits of a (row, KV head) are one thread-block cluster and merge
-// through distributed shared memory (S <= 8); else through the workspace
-template <int HD, int G, typename KT, bool CL>
+// through distributed shared memory (S <= 8); else through the workspace.
+// PG: the cache is paged (a.kv.pages), else contiguous per sequence slot.
+template <int HD, int G, typename KT, bool CL, bool PG>
 __global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G, sizeof(KT) < 4)) k_attn(const AttnArgs a) {
   constexpr int DPL = HD / 32, PS = 32 / G, GH = G * HD;
   using Vec = KvVec<KT, DPL>;
@@ -208,6 +209,7 @@ __global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G, sizeof(KT)
   __shared__ __align__(16) float s_q[GH];  // this row's q for the G heads of the KV head
   __shared__ float s_part[2][ATT_MAX_SPLITS][G];  // the splits' maxima and sums (last arriver)
   __shared__ int s_last;
+  __shared__ int s_pg[PG ? kAttnMaxPages : 1];  // (paged cache) the pages of this CTA's positions
   // grid.x = (row, KV head, split), a.S splits innermost
   const int split = (int)(blockIdx.x % a.S), kvh = (int)((blockIdx.x / a.S) % a.nkv);
   const int t = (int)(blockIdx.x / (a.S * a.nkv));
@@ -224,8 +226,20 @@ __global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G, sizeof(KT)
   const int lo = (int)((int64_t)L * split / S), hi = (int)((int64_t)L * (split + 1) / S);
   const int wlo = lo + (int)((int64_t)(hi - lo) * warp / ATT_WARPS);
   const int whi = lo + (int)((int64_t)(hi - lo) * (warp + 1) / ATT_WARPS);
-  const KT* kb = reinterpret_cast<const KT*>(a.kc) + ri.slot * a.slot_stride + kvh * a.kvh_stride + lane * DPL;
-  const KT* vb = reinterpret_cast<const KT*>(a.vc) + ri.slot * a.slot_stride + kvh * a.kvh_stride + lane * DPL;
+  // this lane's dimensions of position p's row at kb / vb + roff(p)
+  const size_t base = (PG ? 0 : (size_t)ri.slot * a.kv.slot_stride) + kvh * a.kv.kvh_stride + lane * DPL;
+  const KT* const kb = reinterpret_cast<const KT*>(a.kc) + base;
+  const KT* const vb = reinterpret_cast<const KT*>(a.vc) + base;
+  const int sh = a.kv.shift, pg0 = lo >> sh;
+  auto roff = [&](int p) -> size_t {
+    if constexpr (PG) return (size_t)s_pg[(p >> sh) - pg0] * a.kv.slot_stride + (size_t)(p & ((1 << sh) - 1)) * HD;
+    else return (size_t)p * HD;
+  };
+  if constexpr (PG) {
+    const int np = hi > lo ? ((hi - 1) >> sh) - pg0 + 1 : 0;  // <= kAttnMaxPages (checked by the host)
+    for (int i = tid; i < np; i += ATT_THREADS) s_pg[i] = a.kv.pages[(size_t)ri.slot * a.kv.max_pages + pg0 + i];
+    __syncthreads();
+  }
 
   for (int e = tid; e < GH; e += ATT_THREADS) s_q[e] = a.q[(size_t)t * a.ldq + kvh * GH + e];
   float acc[G][DPL];
@@ -255,9 +269,9 @@ __global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G, sizeof(KT)
   auto load_step = [&](int p0, Raw (&kd)[PF ? PS : 1], Raw (&vd)[PF ? PS : 1]) {
 #pragma unroll
     for (int i = 0; i < (PF ? PS : 1); i++) {
-      const int p = min(p0 + i, whi - 1);  // past the end: a valid row, masked below
-      kd[i] = Vec::load(kb + (size_t)p * HD);
-      vd[i] = Vec::load(vb + (size_t)p * HD);
+      const size_t o = roff(min(p0 + i, whi - 1));  // past the end: a valid row, masked below
+      kd[i] = Vec::load(kb + o);
+      vd[i] = Vec::load(vb + o);
     }
   };
   if (PF && wlo < whi) load_step(wlo, kn, vn);
@@ -278,9 +292,9 @@ __global__ void __launch_bounds__(ATT_THREADS, attn_min_blocks(HD, G, sizeof(KT)
       Raw kw[PS];
 #pragma unroll
       for (int i = 0; i < PS; i++) {
-        const int p = min(p0 + i, whi - 1);
-        kw[i] = Vec::load(kb + (size_t)p * HD);
-        vw[i] = Vec::load(vb + (size_t)p * HD);
+        const size_t o = roff(min(p0 + i, whi - 1));
+        kw[i] = Vec::load(kb + o);
+        vw[i] = Vec::load(vb + o);
       }
 #pragma unroll
       for (int i = 0; i < PS; i++) Vec::cvt(kw[i], kr[i]);
@@ -453,15 +467,19 @@ struct AttnKernel {
   AttnLaunch launch = nullptr;
 };
 
+template <int HD, int G, typename KT, bool PG>
+static cudaError_t attn_launch_pg(const AttnArgs& a, dim3 grid, cudaStream_t s) {
+  if (a.ws == nullptr && a.S > 1)  // cluster merge
+    return launch_pdl_cluster(k_attn<HD, G, KT, true, PG>, grid, dim3(ATT_THREADS), 0, a.S, s, a);
+  return launch_pdl(k_attn<HD, G, KT, false, PG>, grid, dim3(ATT_THREADS), 0, s, a);
+}
 template <int HD, int G, typename KT>
 static cudaError_t attn_launch_t(const AttnArgs& a, dim3 grid, cudaStream_t s) {
-  if (a.ws == nullptr && a.S > 1)  // cluster merge
-    return launch_pdl_cluster(k_attn<HD, G, KT, true>, grid, dim3(ATT_THREADS), 0, a.S, s, a);
-  return launch_pdl(k_attn<HD, G, KT, false>, grid, dim3(ATT_THREADS), 0, s, a);
+  return a.kv.pages ? attn_launch_pg<HD, G, KT, true>(a, grid, s) : attn_launch_pg<HD, G, KT, false>(a, grid, s);
 }
 template <int HD, int G, typename KT>
 static AttnKernel attn_k() {
-  return AttnKernel{(const void*)k_attn<HD, G, KT, false>, attn_launch_t<HD, G, KT>};
+  return AttnKernel{(const void*)k_attn<HD, G, KT, false, false>, attn_launch_t<HD, G, KT>};
 }
 template <int HD, typename KT>
 static bool attn_kernel_hd(int G, AttnKernel* k) {
@@ -542,9 +560,9 @@ AttnPlan attn_plan(int T, int nH, int nKV, int hd, int max_ctx, int kv_type, siz
   return p;
 }
 
-int attention(const float* q, int ldq, const void* kc, const void* vc, int kv_type, size_t slot_stride,
-              size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, const AttnPlan& plan,
-              float* out, int ldo, float* ws, int* cnt, cudaStream_t s) {
+int attention(const float* q, int ldq, const void* kc, const void* vc, int kv_type, const KvMap& kv,
+              const RowInfo* rows, int T, int nH, int nKV, int hd, const AttnPlan& plan, float* out, int ldo,
+              float* ws, int* cnt, cudaStream_t s) {
   if (T <= 0) return TN_OK;
   TN_REQUIRE(nKV > 0 && nH % nKV == 0, TN_EUNSUPPORTED, "attention: n_heads %% n_kv_heads != 0");
   TN_REQUIRE(plan.splits >= 1 && plan.splits <= ATT_MAX_SPLITS, TN_EINVAL, "attention: %d splits", plan.splits);
@@ -560,7 +578,8 @@ int attention(const float* q, int ldq, const void* kc, const void* vc, int kv_ty
     set_error("attention: %d query heads per KV head with head_dim %d unsupported", G, hd);
     return TN_EUNSUPPORTED;
   }
-  const AttnArgs a{q,   ldq, kc,  vc,         slot_stride, kvh_stride, rows, plan.splits, nKV, (float)(1.0 / sqrt((double)hd)),
+  TN_REQUIRE(!kv.pages || (kv.shift >= 0 && kv.shift < 30), TN_EINVAL, "attention: page shift %d", kv.shift);
+  const AttnArgs a{q,   ldq, kc,  vc,         kv, rows, plan.splits, nKV, (float)(1.0 / sqrt((double)hd)),
                    out, ldo, ws, cnt, attn_pstride(G, hd)};
   const dim3 grid((unsigned)((int64_t)plan.splits * nKV * T));
   TN_CHECK_CUDA(k.launch(a, grid, s));

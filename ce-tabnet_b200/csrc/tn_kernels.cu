@@ -599,8 +599,7 @@ int rope_table(const RowInfo* rows, const double* freq, int half, int T, double2
 // :554 into the cache at the row's KV index.  Rotations in double, unfused.
 __global__ void k_rope_kv(const float* __restrict__ qkv, int ldqkv, const RowInfo* __restrict__ rows,
                           const double2* __restrict__ cs, float* __restrict__ q_out, void* __restrict__ kc,
-                          void* __restrict__ vc, int kv_type, size_t slot_stride, size_t kvh_stride, int nH,
-                          int nKV, int hd) {
+                          void* __restrict__ vc, int kv_type, const KvMap kv, int nH, int nKV, int hd) {
   const int t = blockIdx.x;
   const RowInfo ri = rows[t];
   const int half = hd >> 1, qDim = nH * hd, kvDim = nKV * hd;
@@ -623,22 +622,21 @@ __global__ void k_rope_kv(const float* __restrict__ qkv, int ldqkv, const RowInf
         qo[i] = o0;
         qo[half + i] = o1;
       } else {
-        const size_t ko = ri.slot * slot_stride + head * kvh_stride + (size_t)ri.kv_idx * hd;
+        const size_t ko = kv_row_off(kv, ri.slot, head, ri.kv_idx, hd);
         kv_store(kc, ko + i, kv_type, o0);
         kv_store(kc, ko + half + i, kv_type, o1);
       }
     } else {
       const int d = k - nq - nk, head = d / hd, e = d % hd;
-      kv_store(vc, ri.slot * slot_stride + head * kvh_stride + (size_t)ri.kv_idx * hd + e, kv_type,
-               src[qDim + kvDim + d]);
+      kv_store(vc, kv_row_off(kv, ri.slot, head, ri.kv_idx, hd) + e, kv_type, src[qDim + kvDim + d]);
     }
   }
 }
 
 int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs, float* q_out, void* kc, void* vc,
-            int kv_type, size_t slot_stride, size_t kvh_stride, int nH, int nKV, int hd, int T, cudaStream_t s) {
+            int kv_type, const KvMap& kv, int nH, int nKV, int hd, int T, cudaStream_t s) {
   if (T <= 0) return TN_OK;
-  k_rope_kv<<<T, 256, 0, s>>>(qkv, ldqkv, rows, cs, q_out, kc, vc, kv_type, slot_stride, kvh_stride, nH, nKV, hd);
+  k_rope_kv<<<T, 256, 0, s>>>(qkv, ldqkv, rows, cs, q_out, kc, vc, kv_type, kv, nH, nKV, hd);
   TN_CHECK_LAUNCH();
   return TN_OK;
 }

@@ -175,6 +175,22 @@ struct RowInfo {
   int slot, pos, kv_idx, len;
 };
 
+// Where a sequence's KV rows live, in elements from the cache base pointer
+// (a layer's K or V).  Contiguous: row i of sequence slot s at
+// s * slot_stride + kvh * kvh_stride + i * hd.  Paged: the row is row
+// i & (2^shift - 1) of page pages[s * max_pages + (i >> shift)], a page at
+// page * slot_stride with kvh_stride between its KV heads.
+struct KvMap {
+  size_t slot_stride = 0, kvh_stride = 0;
+  const int* pages = nullptr;  // [slot][max_pages] page ids (paged), else null
+  int max_pages = 0, shift = 0;
+};
+__device__ __forceinline__ size_t kv_row_off(const KvMap& m, int slot, int kvh, int i, int hd) {
+  if (m.pages == nullptr) return (size_t)slot * m.slot_stride + (size_t)kvh * m.kvh_stride + (size_t)i * hd;
+  const int pg = m.pages[(size_t)slot * m.max_pages + (i >> m.shift)];
+  return (size_t)pg * m.slot_stride + (size_t)kvh * m.kvh_stride + (size_t)(i & ((1 << m.shift) - 1)) * hd;
+}
+
 int rmsnorm(const float* h, int ldh, const int* rowsel, const float* w, float* out, int ldo, int H,
             int T, cudaStream_t s);
 
@@ -194,7 +210,7 @@ struct MvFuse {
   void* kc = nullptr;  // kv_type elements
   void* vc = nullptr;
   int kv_type = KV_F32;
-  size_t slot_stride = 0, kvh_stride = 0;
+  KvMap kv;
   int q_dim = 0, kv_dim = 0, hd = 0;
 };
 // the fused decode matvec handles q4_0 / q8_0 matrices; tokens are taken two at a time
@@ -208,8 +224,7 @@ int embed_rows(const Matrix& emb, const int* ids, int T, float* out, int ldo, in
                cudaStream_t s);
 int rope_table(const RowInfo* rows, const double* freq, int half, int T, double2* cs, cudaStream_t s);
 int rope_kv(const float* qkv, int ldqkv, const RowInfo* rows, const double2* cs, float* q_out,
-            void* kc, void* vc, int kv_type, size_t slot_stride, size_t kvh_stride, int nH, int nKV, int hd,
-            int T, cudaStream_t s);
+            void* kc, void* vc, int kv_type, const KvMap& kv, int nH, int nKV, int hd, int T, cudaStream_t s);
 
 // One-query GQA attention (web/inference-worker.js:556-564) for T rows, one
 // kernel (tn_attn.cu): CTA (split, KV head, row) over its share of the row's
@@ -224,10 +239,12 @@ struct AttnPlan {
 // splits for T rows over caches of up to max_ctx positions; a workspace of at
 // most ws_cap_floats floats bounds them
 AttnPlan attn_plan(int T, int nH, int nKV, int hd, int max_ctx, int kv_type, size_t ws_cap_floats = SIZE_MAX);
-// kc / vc: kv_type elements; strides in elements
-int attention(const float* q, int ldq, const void* kc, const void* vc, int kv_type, size_t slot_stride,
-              size_t kvh_stride, const RowInfo* rows, int T, int nH, int nKV, int hd, const AttnPlan& plan,
-              float* out, int ldo, float* ws, int* cnt, cudaStream_t s);
+// kc / vc: kv_type elements.  A paged map may give each CTA at most
+// kAttnMaxPages pages: ceil(max_ctx / page positions) + 1 <= kAttnMaxPages.
+constexpr int kAttnMaxPages = 1024;
+int attention(const float* q, int ldq, const void* kc, const void* vc, int kv_type, const KvMap& kv,
+              const RowInfo* rows, int T, int nH, int nKV, int hd, const AttnPlan& plan, float* out, int ldo,
+              float* ws, int* cnt, cudaStream_t s);
 
 int hop_encode_rows(const float* h, int ldh, const int* rowsel, int T, int H, uint16_t* out,
                     cudaStream_t s);

@@ -118,14 +118,13 @@ __device__ __forceinline__ void mmv_store(const MmvArgs& a, int row, int tt, flo
         dst[i] = o0;
         dst[half + i] = o1;
       } else {
-        const size_t ko = ri.slot * f.slot_stride + head * f.kvh_stride + (size_t)ri.kv_idx * f.hd;
+        const size_t ko = kv_row_off(f.kv, ri.slot, head, ri.kv_idx, f.hd);
         kv_store(f.kc, ko + i, f.kv_type, o0);
         kv_store(f.kc, ko + half + i, f.kv_type, o1);
       }
     } else {
       const int dv = row - f.q_dim - f.kv_dim;
-      kv_store(f.vc, ri.slot * f.slot_stride + (dv / f.hd) * f.kvh_stride + (size_t)ri.kv_idx * f.hd + dv % f.hd,
-               f.kv_type, v);
+      kv_store(f.vc, kv_row_off(f.kv, ri.slot, dv / f.hd, ri.kv_idx, f.hd) + dv % f.hd, f.kv_type, v);
     }
   }
 }

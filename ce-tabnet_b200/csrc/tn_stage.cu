@@ -92,6 +92,14 @@ struct tn_stage {
   int* attn_cnt = nullptr;
   size_t attn_ws_floats = 0, attn_cnt_ints = 0;
   size_t kvh_stride = 0, layer_stride = 0, slot_stride = 0;
+  // paged KV (kv_page_tokens > 0): a pool of n_pages pages laid out
+  // [page][layer][kv_head][page_tokens][head_dim]; a sequence slot holds
+  // seq_pages[slot] of them, listed in its row of the page table
+  int page_tokens = 0, page_shift = 0, n_pages = 0, max_pages = 0;
+  int* d_pages = nullptr;  // [max_seqs][max_pages] page ids
+  int* h_pages = nullptr;  // pinned host copy
+  std::vector<int> free_pages, seq_pages;
+  KvMap kvmap;
   // activations
   float *h = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr, *act = nullptr,
         *logits = nullptr;
@@ -157,6 +165,7 @@ tn_stage::~tn_stage() {
   }
   if (h_in) cudaFreeHost(h_in);
   if (h_out) cudaFreeHost(h_out);
+  if (h_pages) cudaFreeHost(h_pages);
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -258,6 +267,23 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
   st->max_seqs = sp->max_seqs > 0 ? sp->max_seqs : 16;
   st->max_T = sp->max_tokens_per_step > 0 ? sp->max_tokens_per_step : 512;
   st->flags = sp->flags;
+  if (sp->kv_page_tokens) {
+    const int pt = sp->kv_page_tokens;
+    TN_REQUIRE(pt >= 16 && pt <= 4096 && (pt & (pt - 1)) == 0, TN_EINVAL,
+               "kv_page_tokens %d: a power of two in [16, 4096]", pt);
+    st->page_tokens = pt;
+    while ((1 << st->page_shift) < pt) st->page_shift++;
+    st->max_pages = (st->max_ctx + pt - 1) / pt;
+    TN_REQUIRE(st->max_pages + 1 <= kAttnMaxPages, TN_EINVAL,
+               "max_ctx %d needs %d pages of %d positions (at most %d)", st->max_ctx, st->max_pages, pt,
+               kAttnMaxPages - 1);
+    const int64_t dflt = (int64_t)st->max_seqs * st->max_pages;
+    const int64_t np = sp->kv_pages > 0 ? sp->kv_pages : dflt;
+    TN_REQUIRE(np <= (1 << 30), TN_EINVAL, "kv_pages %lld", (long long)np);
+    st->n_pages = (int)np;
+  } else {
+    TN_REQUIRE(sp->kv_pages == 0, TN_EINVAL, "kv_pages without kv_page_tokens");
+  }
   st->kv_type = (sp->flags & TN_FLAG_KV_F8) ? KV_F8 : ((sp->flags & TN_FLAG_KV_F16) ? KV_F16 : KV_F32);
   TN_REQUIRE(!((sp->flags & TN_FLAG_KV_F8) && (sp->flags & TN_FLAG_KV_F16)), TN_EINVAL,
              "TN_FLAG_KV_F16 and TN_FLAG_KV_F8 exclude each other");
@@ -329,19 +355,34 @@ static int init_impl(const tn_stage_spec* sp, tn_stage* st) {
     st->packed_bytes += head_bytes + (uint64_t)st->H * 2;
   }
 
-  // KV arena [slot][layer][kv_head][ctx][head_dim], K and V
-  st->kvh_stride = (size_t)st->max_ctx * st->hd;
+  // KV arena, K and V: [slot][layer][kv_head][max_ctx][head_dim], or the
+  // page pool [page][layer][kv_head][page_tokens][head_dim]
+  const int ctx_rows = st->page_tokens ? st->page_tokens : st->max_ctx;
+  st->kvh_stride = (size_t)ctx_rows * st->hd;
   st->layer_stride = st->kvh_stride * st->nKV;
   st->slot_stride = st->layer_stride * std::max(1, st->nL);
-  const size_t kv_elems = st->slot_stride * st->max_seqs;
+  const size_t kv_elems = st->slot_stride * (st->page_tokens ? st->n_pages : st->max_seqs);
   if (st->nL > 0) {
     const size_t eb = kv_elem_bytes(st->kv_type);
     cudaError_t e1 = cudaMalloc(&st->kc, kv_elems * eb);
     cudaError_t e2 = e1 == cudaSuccess ? cudaMalloc(&st->vc, kv_elems * eb) : e1;
     TN_REQUIRE(e1 == cudaSuccess && e2 == cudaSuccess, TN_ENOMEM,
-               "KV arena of 2 x %zu bytes (max_seqs %d x max_ctx %d): %s", kv_elems * eb,
-               st->max_seqs, st->max_ctx, cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
+               "KV arena of 2 x %zu bytes (%d %s of %d rows): %s", kv_elems * eb,
+               st->page_tokens ? st->n_pages : st->max_seqs, st->page_tokens ? "pages" : "slots", ctx_rows,
+               cudaGetErrorString(e1 != cudaSuccess ? e1 : e2));
     st->kv_bytes = 2 * kv_elems * eb;
+  }
+  st->kvmap.slot_stride = st->slot_stride;
+  st->kvmap.kvh_stride = st->kvh_stride;
+  if (st->page_tokens) {
+    TN_CHECK_CUDA(cudaHostAlloc((void**)&st->h_pages, (size_t)st->max_seqs * st->max_pages * sizeof(int),
+                                cudaHostAllocDefault));
+    if ((rc = dalloc(st, &st->d_pages, (size_t)st->max_seqs * st->max_pages))) return rc;
+    st->kvmap.pages = st->d_pages;
+    st->kvmap.max_pages = st->max_pages;
+    st->kvmap.shift = st->page_shift;
+    for (int i = st->n_pages - 1; i >= 0; i--) st->free_pages.push_back(i);
+    st->seq_pages.assign(st->max_seqs, 0);
   }
 
   // activations for max_T rows
@@ -529,8 +570,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       f.kc = kc;
       f.vc = vc;
       f.kv_type = st->kv_type;
-      f.slot_stride = st->slot_stride;
-      f.kvh_stride = st->kvh_stride;
+      f.kv = st->kvmap;
       f.q_dim = st->qDim;
       f.kv_dim = st->kvDim;
       f.hd = st->hd;
@@ -539,12 +579,12 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
       TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
       TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1,
-                     rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->kv_type, st->slot_stride,
-                             st->kvh_stride, st->nH, st->nKV, st->hd, T, s));
+                     rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->kv_type, st->kvmap, st->nH,
+                             st->nKV, st->hd, T, s));
     }
     TN_STEP_LAUNCH(TN_PROF_ATTENTION, 1,
-                   attention(st->q, st->qDim, kc, vc, st->kv_type, st->slot_stride, st->kvh_stride, rows, T, st->nH,
-                             st->nKV, st->hd, ap, st->att, st->qDim, st->attn_ws, st->attn_cnt, s));
+                   attention(st->q, st->qDim, kc, vc, st->kv_type, st->kvmap, rows, T, st->nH, st->nKV, st->hd, ap,
+                             st->att, st->qDim, st->attn_ws, st->attn_cnt, s));
     if (fuse && matvec_dec_ok(L.o, T))
       TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
@@ -634,13 +674,27 @@ static int upload_ctl(tn_stage* st, int idx, cudaStream_t s) {
   return TN_OK;
 }
 
-// slots for the requests' sequences; new slots are released again on failure
+// a freed sequence slot's pages go back to the pool
+static void release_pages(tn_stage* st, int slot) {
+  if (!st->page_tokens) return;
+  for (int j = st->seq_pages[slot] - 1; j >= 0; j--)
+    st->free_pages.push_back(st->h_pages[(size_t)slot * st->max_pages + j]);
+  st->seq_pages[slot] = 0;
+}
+
+// slots for the requests' sequences and pages for their new rows; new slots
+// and pages are released again on failure
 struct SlotTxn {
   tn_stage* st;
   std::vector<uint64_t> created;
+  std::vector<std::pair<int, int>> taken;  // (slot, page) in order
   bool committed = false;
   ~SlotTxn() {
     if (committed) return;
+    for (auto it = taken.rbegin(); it != taken.rend(); ++it) {
+      st->seq_pages[it->first]--;
+      st->free_pages.push_back(it->second);
+    }
     for (uint64_t id : created) {
       auto it = st->seq_slot.find(id);
       if (it != st->seq_slot.end()) {
@@ -649,6 +703,26 @@ struct SlotTxn {
         st->seq_slot.erase(it);
       }
     }
+  }
+  // pages for rows [0, rows) of the slot's sequence, their page-table
+  // entries copied to the device on s ahead of the step's kernels
+  int grow(int slot, int rows, cudaStream_t s) {
+    if (!st->page_tokens) return TN_OK;
+    const int need = (rows + st->page_tokens - 1) >> st->page_shift, j0 = st->seq_pages[slot];
+    if (need <= j0) return TN_OK;
+    TN_REQUIRE((int)st->free_pages.size() >= need - j0, TN_ECAPACITY,
+               "KV page pool exhausted: %d pages needed, %zu of %d free", need - j0, st->free_pages.size(),
+               st->n_pages);
+    int* row = st->h_pages + (size_t)slot * st->max_pages;
+    for (int j = j0; j < need; j++) {
+      row[j] = st->free_pages.back();
+      st->free_pages.pop_back();
+      st->seq_pages[slot]++;
+      taken.emplace_back(slot, row[j]);
+    }
+    TN_CHECK_CUDA(cudaMemcpyAsync(st->d_pages + (size_t)slot * st->max_pages + j0, row + j0,
+                                  (size_t)(need - j0) * sizeof(int), cudaMemcpyHostToDevice, s));
+    return TN_OK;
   }
   int get(uint64_t id, int* slot) {
     auto it = st->seq_slot.find(id);
@@ -700,12 +774,13 @@ static int forward_impl(tn_stage* st, const tn_fwd_req* reqs, int n, tn_fwd_out*
   }
   SlotTxn txn{st};
   std::vector<int> slot(n);
+  int rc;
   for (int i = 0; i < n; i++) {
-    int rc = txn.get(reqs[i].seq_id, &slot[i]);
-    if (rc) return rc;
+    if ((rc = txn.get(reqs[i].seq_id, &slot[i]))) return rc;
     TN_REQUIRE(st->kv_len[slot[i]] + reqs[i].n_tokens <= st->max_ctx, TN_ECAPACITY,
                "seq %llu: %d cached + %d new rows > max_ctx %d", (unsigned long long)reqs[i].seq_id,
                st->kv_len[slot[i]], reqs[i].n_tokens, st->max_ctx);
+    if ((rc = txn.grow(slot[i], st->kv_len[slot[i]] + reqs[i].n_tokens, st->stream))) return rc;
   }
   // global row list
   struct RowRef {
@@ -727,7 +802,6 @@ static int forward_impl(tn_stage* st, const tn_fwd_req* reqs, int n, tn_fwd_out*
   };
   const bool decode_shape = R == n;  // one row per sequence
   cudaStream_t s = st->stream;
-  int rc;
   for (int r0 = 0; r0 < R; r0 += st->max_T) {
     const int T = std::min(st->max_T, R - r0);
     int ci;
@@ -819,6 +893,7 @@ static int step_async_impl(tn_stage* st, const tn_step_desc* d, cudaStream_t s) 
                (unsigned long long)d->seq_ids[i], st->max_ctx);
     for (int j = 0; j < i; j++)
       TN_REQUIRE(slot[j] != slot[i], TN_EINVAL, "step: seq_id twice in one step");
+    if ((rc = txn.grow(slot[i], st->kv_len[slot[i]] + 1, s))) return rc;
   }
   int ci;
   char* ctl = next_ctl(st, &ci);
@@ -925,6 +1000,7 @@ extern "C" int tn_stage_free_seq(tn_stage* st, uint64_t seq_id) {
   auto it = st->seq_slot.find(seq_id);
   TN_REQUIRE(it != st->seq_slot.end(), TN_EINVAL, "unknown seq_id %llu", (unsigned long long)seq_id);
   st->kv_len[it->second] = 0;
+  release_pages(st, it->second);
   st->free_slots.push_back(it->second);
   st->seq_slot.erase(it);
   return TN_OK;

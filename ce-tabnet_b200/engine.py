@@ -104,7 +104,9 @@ def initStage(spec: dict) -> StageCtx:
             weights:{layers:[{idx, buf, quant}], embed?, norm?, lm_head?, embedQuant?, lmHeadQuant?, quant?},
             opts?:{max_ctx, max_seqs, max_tokens_per_step, device, hop_mode, no_graphs,
                    kv_dtype: "f32" (default, the reference's rows) | "f16" (half-size KV cache)
-                             | "f8" (e4m3, quarter-size)}}
+                             | "f8" (e4m3, quarter-size),
+                   kv_page_tokens: 0 (contiguous max_ctx rows per sequence) | positions per KV page,
+                   kv_pages: pages in the pool (0: max_seqs x max_ctx worth)}}
     """
     lib = _lib.load()
     dims, (lo, hi), w = spec["dims"], spec["layers"], spec["weights"]
@@ -152,6 +154,8 @@ def initStage(spec: dict) -> StageCtx:
     kv_dtype = opts.get("kv_dtype", "f32")
     if kv_dtype not in ("f32", "f16", "f8"):
         raise ValueError(f"opts.kv_dtype must be 'f32', 'f16' or 'f8', not {kv_dtype!r}")
+    s.kv_page_tokens = int(opts.get("kv_page_tokens") or 0)
+    s.kv_pages = int(opts.get("kv_pages") or 0)
     s.flags = (_lib.TN_FLAG_NO_GRAPHS if opts.get("no_graphs") else 0) | \
         (_lib.TN_FLAG_PROFILE if opts.get("profile") else 0) | \
         (_lib.TN_FLAG_NO_FUSED_DECODE if opts.get("fused_decode") is False else 0) | \

@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define TN_ABI_VERSION 1
+#define TN_ABI_VERSION 2
 
 /* ---- status codes ---- */
 #define TN_OK 0
@@ -33,7 +33,7 @@ extern "C" {
 #define TN_ENOMEM (-2)       /* host or device allocation failed */
 #define TN_ECUDA (-3)        /* a CUDA runtime call failed */
 #define TN_EUNSUPPORTED (-4) /* "unsupported quant" (web/inference-worker.js:126,136) */
-#define TN_ECAPACITY (-5)    /* max_ctx / max_seqs / max_tokens_per_step exceeded */
+#define TN_ECAPACITY (-5)    /* max_ctx / max_seqs / max_tokens_per_step / KV pages exceeded */
 #define TN_ESTATE (-6)       /* wrong stage role for the call (e.g. ids to a non-first stage) */
 #define TN_ETIMEOUT (-7)     /* a bounded device wait ran out */
 
@@ -86,6 +86,14 @@ typedef struct {
   int32_t max_seqs;            /* concurrent sequences with KV; 0 -> 16 */
   int32_t max_tokens_per_step; /* rows fused into one step; 0 -> 512 (longer prompts are chunked) */
   uint32_t flags;
+  /* Paged KV (not in the reference, whose KV is one growing array per
+   * sequence): 0 keeps max_ctx contiguous rows per sequence slot; else the
+   * rows live in a pool of kv_pages pages of kv_page_tokens positions (a power
+   * of two in [16, 4096]), a sequence taking pages as it grows and returning
+   * them when freed.  max_ctx still bounds one sequence and max_seqs the
+   * sequences; kv_pages 0 -> max_seqs * ceil(max_ctx / kv_page_tokens). */
+  int32_t kv_page_tokens;
+  int32_t kv_pages;
 } tn_stage_spec;
 
 typedef struct tn_stage tn_stage;
@@ -241,6 +249,19 @@ int tn_attention_f16(int32_t n_rows, int32_t n_slots, int32_t n_heads, int32_t n
                      int32_t max_ctx, const float* d_q, const uint16_t* d_k, const uint16_t* d_v,
                      const int32_t* d_slot, const int32_t* d_len, float* d_out, void* d_scratch,
                      uint64_t scratch_bytes, void* stream);
+
+/* tn_attention over a paged cache, the layout of stages created with
+ * kv_page_tokens > 0, one layer: d_k / d_v are pools of n_pages pages
+ * [page][kv_head][page_tokens][head_dim] of kv_type elements (0 f32, 1 fp16,
+ * 2 fp8 e4m3; 16-byte aligned); row r's positions 0 .. d_len[r] - 1 are
+ * position p % page_tokens of page d_pages[r * max_pages + p / page_tokens].
+ * page_tokens is a power of two in [16, 4096], max_pages <= 1023.  A row whose
+ * used page ids leave [0, n_pages) gives zeros.  Scratch as tn_attention with
+ * max_ctx = max_pages * page_tokens. */
+int tn_attention_paged(int32_t kv_type, int32_t n_rows, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                       int32_t page_tokens, int32_t max_pages, int32_t n_pages, const float* d_q, const void* d_k,
+                       const void* d_v, const int32_t* d_pages, const int32_t* d_len, float* d_out,
+                       void* d_scratch, uint64_t scratch_bytes, void* stream);
 
 /* tn_attention over an fp8 e4m3 KV cache (one byte a value, same layout): the
  * cache format of stages created with TN_FLAG_KV_F8.  Computed in f32. */

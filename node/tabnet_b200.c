@@ -280,6 +280,8 @@ static napi_value js_initStage(napi_env env, napi_callback_info info) {
   s->max_ctx = opts ? (int32_t)num(env, opts, "max_ctx", 4096) : 4096; /* :642 */
   s->max_seqs = opts ? (int32_t)num(env, opts, "max_seqs", 16) : 16;
   s->device = opts ? (int32_t)num(env, opts, "device", 0) : 0;
+  s->kv_page_tokens = opts ? (int32_t)num(env, opts, "kv_page_tokens", 0) : 0; /* 0: contiguous KV */
+  s->kv_pages = opts ? (int32_t)num(env, opts, "kv_pages", 0) : 0;
   NAPI_OK(napi_create_reference(env, spec, 1, &j->keep));
   NAPI_OK(napi_create_promise(env, &j->deferred, &promise));
   napi_create_string_utf8(env, "tabnet_b200.initStage", NAPI_AUTO_LENGTH, &name);

@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol(pkg):
 
 
 def test_abi_version(pkg):
-    assert pkg._lib.load().tn_abi_version() == 1
+    assert pkg._lib.load().tn_abi_version() == 2
 
 
 def test_layout_matches_oracle_and_library(pkg, ref):

@@ -202,6 +202,57 @@ def test_attention_vs_oracle(pkg, ref, torch_cuda, hd, nH, nKV, kv):
         assert _maxrel(got[r], want) < ATTN_TOL, (r, L, _maxrel(got[r], want))
 
 
+@pytest.mark.parametrize("kv,page", [("f32", 16), ("f32", 64), ("f16", 256), ("f8", 64), ("f32", 4096)])
+def test_attention_paged_vs_oracle(pkg, ref, torch_cuda, kv, page):
+    """tn_attention_paged: each row's positions scattered over a shuffled page
+    pool (page boundaries inside warp steps and splits), lengths 1 .. 5000,
+    against the oracle on the rows gathered back in order; a row naming a page
+    outside the pool gives zeros."""
+    torch = torch_cuda
+    lib = pkg._lib.load()
+    hd, nH, nKV = 128, 32, 8
+    lens = [1, page - 1, page, page + 1, 7, 2100, 5000, 3 * page + 5]
+    n = len(lens)
+    max_pages = -(-max(lens) // page)
+    rng = np.random.default_rng(page)
+    need = sum(-(-L // page) for L in lens)
+    n_pages = need + 5
+    perm = rng.permutation(n_pages)
+    table = np.full((n + 1, max_pages), -1, np.int32)
+    k = 0
+    for r, L in enumerate(lens):
+        for j in range(-(-L // page)):
+            table[r, j] = perm[k]
+            k += 1
+    table[n, 0] = n_pages  # the extra row: a page id outside the pool
+    lens = lens + [5]
+    K = rng.standard_normal((n_pages, nKV, page, hd)).astype(np.float32)
+    V = rng.standard_normal((n_pages, nKV, page, hd)).astype(np.float32)
+    dK, dV, K, V = _kv_cache(torch, K, V, kv)
+    q = rng.standard_normal((n + 1, nH * hd)).astype(np.float32)
+    dq = torch.from_numpy(q).cuda()
+    dtab = torch.from_numpy(table).cuda()
+    dlen = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = torch.full((n + 1, nH * hd), 7.0, dtype=torch.float32, device="cuda")
+    nbytes = lib.tn_attention_scratch_bytes(n + 1, nH, nKV, hd, max_pages * page)
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    code = {"f32": 0, "f16": 1, "f8": 2}[kv]
+    pkg._lib.check(lib.tn_attention_paged(code, n + 1, nH, nKV, hd, page, max_pages, n_pages, dq.data_ptr(),
+                                          dK.data_ptr(), dV.data_ptr(), dtab.data_ptr(), dlen.data_ptr(),
+                                          out.data_ptr(), scratch.data_ptr(), nbytes, None))
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for r in range(n):
+        L = lens[r]
+        pos = np.arange(L)
+        pg = table[r, pos // page]
+        Kr = K[pg, :, pos % page, :].reshape(L, nKV * hd)
+        Vr = V[pg, :, pos % page, :].reshape(L, nKV * hd)
+        want = ref.attention(q[r], Kr, Vr, nH, nKV, hd)
+        assert _maxrel(got[r], want) < ATTN_TOL, (r, L, _maxrel(got[r], want))
+    assert not got[n].any()
+
+
 @pytest.mark.parametrize("L,n_rows,n_slots,kv", [
     (512, 1, 1, "f32"), (1024, 1, 1, "f32"), (2048, 8, 8, "f32"), (2048, 64, 16, "f32"), (8192, 1, 1, "f32"),
     (8192, 8, 4, "f32"), (8192, 64, 8, "f32"), (32768, 1, 1, "f32"), (32768, 8, 2, "f32"), (32768, 64, 8, "f32"),

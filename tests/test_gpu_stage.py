@@ -105,6 +105,82 @@ def test_tiny_kv_lowp_greedy_vs_oracle(pkg, ref, tiny, fused, kv):
     pkg.freeStage(ctx)
 
 
+@pytest.mark.parametrize("fused", [True, False])
+def test_tiny_paged_kv_matches_contiguous(pkg, ref, tiny, fused):
+    """A paged KV cache (16-position pages from a shared pool) against the
+    contiguous arena: three sequences decoded interleaved so that their pages
+    interleave in the pool, one freed half way and its pages reused by a
+    fourth.  Every step's logits are bitwise those of the contiguous stage
+    (the same rows in the same order, only their addresses differ) and the
+    greedy tokens those of the oracle."""
+    m, w = tiny
+    paged, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, fused_decode=fused, kv_page_tokens=16, kv_pages=40)
+    flat, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, fused_decode=fused)
+    assert paged.info()["kv_bytes"] * 256 * 8 == flat.info()["kv_bytes"] * 40 * 16
+    oracles = {}
+    toks, pos = {}, {}
+    for i, sid in enumerate(["a", "b", "c"]):
+        prompt = pkg.pack.synth_prompt(m, 5 + 9 * i, seed=40 + i)
+        oracles[sid] = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
+        outs = []
+        for ctx in (paged, flat):
+            outs.append(pkg.forward(ctx, {"seq_id": sid, "token_pos": 0, "token_ids": prompt, "temperature": 0}))
+            outs[-1]["logits"] = ctx.peek("logits", 1)[0].copy()
+        assert np.array_equal(outs[0]["logits"], outs[1]["logits"])
+        want = oracles[sid].forward(1, 0, token_ids=prompt)
+        assert outs[0]["token_id"] == want["token_id"]
+        toks[sid], pos[sid] = outs[0]["token_id"], len(prompt)
+    for step in range(40):
+        if step == 20:
+            for ctx in (paged, flat):
+                pkg.free_seq(ctx, "b")
+            del toks["b"]
+            prompt = pkg.pack.synth_prompt(m, 30, seed=99)
+            oracles["d"] = ref.RefStage(m.dims(), 0, m.n_layers, True, True, w)
+            for ctx in (paged, flat):
+                r = pkg.forward(ctx, {"seq_id": "d", "token_pos": 0, "token_ids": prompt, "temperature": 0})
+            assert r["token_id"] == oracles["d"].forward(1, 0, token_ids=prompt)["token_id"]
+            toks["d"], pos["d"] = r["token_id"], len(prompt)
+        for sid in list(toks):
+            got = []
+            for ctx in (paged, flat):
+                got.append(pkg.forward(ctx, {"seq_id": sid, "token_pos": pos[sid], "token_ids": [toks[sid]],
+                                             "temperature": 0})["token_id"])
+                got.append(ctx.peek("logits", 1)[0].copy())
+            assert np.array_equal(got[1], got[3]), (step, sid)
+            want = oracles[sid].forward(1, pos[sid], token_ids=[toks[sid]])
+            assert got[0] == got[2] == want["token_id"], (step, sid)
+            assert maxrel(got[1], want["logits"]) <= LOGIT_TOL
+            toks[sid], pos[sid] = got[0], pos[sid] + 1
+    for sid in toks:
+        assert pkg.kv_len(paged, sid) == pkg.kv_len(flat, sid) == pos[sid]
+    pkg.freeStage(paged)
+    pkg.freeStage(flat)
+
+
+def test_tiny_paged_kv_pool_exhaustion(pkg, tiny):
+    """A forward that needs more pages than the pool has left fails with
+    TN_ECAPACITY and takes nothing: the pages of its new sequence and of a
+    grown one go back, and freeing a sequence makes room again."""
+    m, w = tiny
+    ctx, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, kv_page_tokens=16, kv_pages=4)
+    pkg.forward(ctx, {"seq_id": "x", "token_pos": 0, "token_ids": pkg.pack.synth_prompt(m, 40), "temperature": 0})
+    with pytest.raises(pkg._lib.TnError) as e:  # 3 pages held, 2 more needed
+        pkg.forward(ctx, {"seq_id": "y", "token_pos": 0, "token_ids": pkg.pack.synth_prompt(m, 20, seed=2),
+                          "temperature": 0})
+    assert e.value.code == pkg._lib.TN_ECAPACITY
+    assert pkg.kv_len(ctx, "y") == 0
+    with pytest.raises(pkg._lib.TnError):  # one sequence growing past the pool, alongside a new one
+        pkg.forward_batch(ctx, [{"seq_id": "x", "token_pos": 40, "token_ids": [1] * 9, "temperature": 0},
+                                {"seq_id": "z", "token_pos": 0, "token_ids": [2], "temperature": 0}])
+    assert pkg.kv_len(ctx, "x") == 40 and pkg.kv_len(ctx, "z") == 0
+    pkg.forward(ctx, {"seq_id": "y", "token_pos": 0, "token_ids": [3] * 16, "temperature": 0})  # the 4th page
+    pkg.free_seq(ctx, "x")
+    pkg.forward(ctx, {"seq_id": "z", "token_pos": 0, "token_ids": [2] * 48, "temperature": 0})  # x's 3 pages
+    assert pkg.kv_len(ctx, "z") == 48
+    pkg.freeStage(ctx)
+
+
 def test_tiny_two_stages_reference_hops(pkg, ref, tiny):
     """The reference runtime's hop semantics: prefill hops only the last
     position (web/tabnet-node.js:167-169), so stage 1's KV starts at one row."""
