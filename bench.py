@@ -590,6 +590,12 @@ def run_ours(args):
                 "avg_launch_us": round(dom_us, 2),
                 "all_matvecs": {"achieved": round(tot_bytes / (tot_ms / 1e3) / 1e9, 1), "launches": n_launch,
                                 "share_of_step_time": round(tot_ms / sum(v[0] for v in prof.values()), 4)},
+                # every matvec class of the step: average launch time and GB/s
+                "per_class": {k: {"avg_launch_us": round(prof[k][0] / prof[k][1] * 1e3, 2),
+                                  "achieved": round(matvec_bytes(pkg, m, k) / (prof[k][0] / prof[k][1] / 1e3) / 1e9,
+                                                    1),
+                                  "frac": round(matvec_bytes(pkg, m, k) / (prof[k][0] / prof[k][1] / 1e3) / 1e9
+                                                / peak, 4)} for k in mv},
                 "timing": "CUDA events around each launch on the stage stream (profiled pass after the timed one)"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
