@@ -672,8 +672,20 @@ def fused_decode(pkg, torch, ctx, pipe, args) -> dict:
             pipe.pos[mb][0] += 1
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
+    # a profiled pass of two steps: device time per launch class
+    P.check(lib.tn_stage_set_profile(ctx.handle, 1))
+    ctx.profile(reset=True)
+    for _ in range(2):
+        out = pkg.forward_batch(ctx, [{"seq_id": mb, "token_pos": pipe.pos[mb][0], "token_ids": [toks[mb]],
+                                       "temperature": 0} for mb in range(M)])
+        toks = [o["token_id"] for o in out]
+        for mb in range(M):
+            pipe.pos[mb][0] += 1
+    prof = {k: [round(v[0] / 2, 3), v[1] // 2] for k, v in ctx.profile().items() if v[1]}
+    P.check(lib.tn_stage_set_profile(ctx.handle, 0))
     n_tok = args.steps * M
     return {"value": round(n_tok / (ms / 1e3), 3), "unit": "tok/s", "rows_per_step": M,
+            "profile_ms_per_step": prof,
             "ms_per_step": round(ms / args.steps, 4), "steps": args.steps, "gpu_launches": launches * args.steps,
             "clocks": clk,
             "e2e": {"value": round(n_tok / e2e_s, 3), "unit": "tok/s", "h2d_bytes_per_step": 4 * M,

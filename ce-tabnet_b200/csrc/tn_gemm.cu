@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       last_raw[r] = -1;
     }
     for (int s = 0; s < a.sa; s++) {
-      mbar_init(&afull[s], GM_DQ_WARPS);
+      mbar_init(&afull[s], GM_DQ_WARPS / 2);  // one dequant warp per lane quarter writes a slice
       mbar_init(&aempty[s], 1);
     }
     for (int s = 0; s < a.sb; s++) {
@@ -351,73 +351,99 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       }
     }
   } else {
-    // ================= dequant (warps 2..9): row quarter * 32 + lane of the M tile, K half kh
-    const int quarter = warp & 3, kh = (warp - 2) >> 2;
+    // ================= dequant (warps 2..9): row quarter * 32 + lane of the M
+    // tile.  The two warps of a lane quarter take alternate slices (parity
+    // par), each both K halves of its slice, so that two slices per quarter
+    // are in flight: a slice's chain (record loads, dequant, TMEM stores and
+    // their wait, the hand-off) is latency-bound.
+    const int quarter = warp & 3, par = (warp - 2) >> 2;
     const uint32_t lanes = (uint32_t)(quarter * 32) << 16;
     const int m = quarter * 32 + lane;             // M-tile row
     const int tt = m >> 4, g = m & 7, u = (m >> 3) & 1;  // record tile, row g + 8 u of it
     const uint32_t off2 = KIND == MK_Q4 ? 0x64086408u : 0x64806480u;  // fp16 (1024 + bias) twice
-    for (int k = 0; k < K; k++) {
-      const int q0 = k / a.ksl, i0 = k - q0 * a.ksl, r = q0 % a.raw_stages;
+    const int NQ = (K + a.ksl - 1) / a.ksl;
+    bool live = true;
+    for (int q0 = 0; q0 < NQ && live; q0++) {
+      const int r = q0 % a.raw_stages, nk = min(a.ksl, K - q0 * a.ksl);
       // (a barrier wait costs hundreds of cycles even when the phase is complete:
       // one per raw stage, not one per slice)
-      if (i0 == 0 && !__all_sync(0xffffffffu, GM_WAIT(&rfull[r], (q0 / a.raw_stages) & 1, &abort_flag))) break;
-      // block 2p + kh of this row: lane slots 4 g + c of the record (c = 0..3), word
-      // 2h + kh (q4) / 4h + 2kh + u (q8) for element half h, and the row's scale;
-      // each slot is read as whole 16-byte vectors
-      const uint8_t* rec = raw + (size_t)r * raw_stage + (size_t)(tt * a.ksl + i0) * REC;
-      uint32_t w[2][4];
-#pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const uint4* slot = reinterpret_cast<const uint4*>(rec + (4 * g + c) * (AB / 32));
-        if (KIND == MK_Q4) {
-          const uint4 v = slot[0];  // words 0..3 = (h, q) = (0,0) (0,1) (1,0) (1,1)
-          w[0][c] = kh ? v.y : v.x;
-          w[1][c] = kh ? v.w : v.z;
-        } else {
-          const uint4 v0 = slot[0], v1 = slot[1];  // words 4h + 2q + u
-          w[0][c] = kh ? (u ? v0.w : v0.z) : (u ? v0.y : v0.x);
-          w[1][c] = kh ? (u ? v1.w : v1.z) : (u ? v1.y : v1.x);
-        }
+      if (!__all_sync(0xffffffffu, GM_WAIT(&rfull[r], (q0 / a.raw_stages) & 1, &abort_flag))) break;
+      if (par >= nk) {  // no slice of this stage for this warp
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&rempty[r]);
+        continue;
       }
-      const uint32_t sc = reinterpret_cast<const uint32_t*>(rec + AB)[2 * g + kh];
-      __syncwarp();
-      if (lane == 0 && (i0 == a.ksl - 1 || k == K - 1)) mbar_arrive(&rempty[r]);  // stage read to the end
-      const int sa = k % a.sa;
-      if (k >= a.sa) {
-        if (!__all_sync(0xffffffffu, GM_WAIT(&aempty[sa], ((k / a.sa) - 1) & 1, &abort_flag))) break;
-        tc_fence_after();
-      }
-      const uint32_t d2 = __byte_perm(sc, 0, u ? 0x3232 : 0x1010);  // this row's scale, both halves
-      // element e = 16 h + 4 c + i of the block = K column e of this half: fp16
-      // pair (e, e + 1) goes to column e / 2
-      uint32_t hi[16], lo[16];
-#pragma unroll
-      for (int h = 0; h < 2; h++)
+      for (int i0 = par; i0 < nk; i0 += 2) {
+        const int k = q0 * a.ksl + i0;
+        // blocks 2p and 2p + 1 of this row: lane slots 4 g + c of the record
+        // (c = 0..3), word 2h + kh (q4) / 4h + 2kh + u (q8) for element half h
+        // of block half kh, and the row's two scales; each slot is read as
+        // whole 16-byte vectors
+        const uint8_t* rec = raw + (size_t)r * raw_stage + (size_t)(tt * a.ksl + i0) * REC;
+        uint32_t w[2][2][4];
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-          uint32_t bytes;
+          const uint4* slot = reinterpret_cast<const uint4*>(rec + (4 * g + c) * (AB / 32));
           if (KIND == MK_Q4) {
-            // byte i = (s(row g) << 4) | s(row g + 8), s = n ^ 8
-            bytes = (((u == 0) ? (w[h][c] >> 4) : w[h][c]) & 0x0F0F0F0Fu) ^ 0x08080808u;
+            const uint4 v = slot[0];  // words 0..3 = (h, kh) = (0,0) (0,1) (1,0) (1,1)
+            w[0][0][c] = v.x;
+            w[1][0][c] = v.y;
+            w[0][1][c] = v.z;
+            w[1][1][c] = v.w;
           } else {
-            bytes = w[h][c] ^ 0x80808080u;  // q8 value of row g + 8 u, biased by 128
+            const uint4 v0 = slot[0], v1 = slot[1];  // words 4h + 2kh + u
+            w[0][0][c] = u ? v0.y : v0.x;
+            w[1][0][c] = u ? v0.w : v0.z;
+            w[0][1][c] = u ? v1.y : v1.x;
+            w[1][1][c] = u ? v1.w : v1.z;
           }
-          uint32_t ph[2], pl[2];
-          dq4(bytes, d2, off2, ph, pl);
-          const int col = 8 * h + 2 * c;
-          hi[col] = ph[0];
-          hi[col + 1] = ph[1];
-          lo[col] = pl[0];
-          lo[col + 1] = pl[1];
         }
-      const uint32_t abase = tmem + lanes + a.a_col0 + (uint32_t)sa * GM_A_COLS + (uint32_t)(16 * kh);
-      tmem_st16(abase, hi);
-      tmem_st16(abase + GM_A_COLS / 2, lo);
-      tmem_st_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&afull[sa]);
+        const uint2 sc2 = reinterpret_cast<const uint2*>(rec + AB)[g];  // scales of blocks 2p, 2p + 1
+        __syncwarp();
+        if (lane == 0 && i0 + 2 >= nk) mbar_arrive(&rempty[r]);  // this warp's reads of the stage are done
+        const int sa = k % a.sa;
+        if (k >= a.sa) {
+          if (!__all_sync(0xffffffffu, GM_WAIT(&aempty[sa], ((k / a.sa) - 1) & 1, &abort_flag))) {
+            live = false;
+            break;
+          }
+          tc_fence_after();
+        }
+#pragma unroll
+        for (int kh = 0; kh < 2; kh++) {
+          const uint32_t sc = kh ? sc2.y : sc2.x;
+          const uint32_t d2 = __byte_perm(sc, 0, u ? 0x3232 : 0x1010);  // this row's scale, both halves
+          // element e = 16 h + 4 c + i of the block = K column e of this half: fp16
+          // pair (e, e + 1) goes to column e / 2
+          uint32_t hi[16], lo[16];
+#pragma unroll
+          for (int h = 0; h < 2; h++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+              uint32_t bytes;
+              if (KIND == MK_Q4) {
+                // byte i = (s(row g) << 4) | s(row g + 8), s = n ^ 8
+                bytes = (((u == 0) ? (w[kh][h][c] >> 4) : w[kh][h][c]) & 0x0F0F0F0Fu) ^ 0x08080808u;
+              } else {
+                bytes = w[kh][h][c] ^ 0x80808080u;  // q8 value of row g + 8 u, biased by 128
+              }
+              uint32_t ph[2], pl[2];
+              dq4(bytes, d2, off2, ph, pl);
+              const int col = 8 * h + 2 * c;
+              hi[col] = ph[0];
+              hi[col + 1] = ph[1];
+              lo[col] = pl[0];
+              lo[col + 1] = pl[1];
+            }
+          const uint32_t abase = tmem + lanes + a.a_col0 + (uint32_t)sa * GM_A_COLS + (uint32_t)(16 * kh);
+          tmem_st16(abase, hi);
+          tmem_st16(abase + GM_A_COLS / 2, lo);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[sa]);
+      }
     }
   }
 
