@@ -279,14 +279,18 @@ def test_temperature_sampling_matches_oracle_draw(pkg, ref, tiny):
     pkg.freeStage(ctx)
 
 
-def test_device_step_matches_forward(pkg, ref, tiny, torch_cuda):
+@pytest.mark.parametrize("page", [0, 16])
+def test_device_step_matches_forward(pkg, ref, tiny, torch_cuda, page):
+    """tn_stage_step_async (device token ids in and out) against forward; with
+    16-position KV pages the steps cross into each sequence's second page,
+    taken and copied to the device table on the step's stream."""
     torch = torch_cuda
     m, w = tiny
     lib = pkg._lib.load()
     import ctypes as C
 
     a, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
-    b, _ = _stage(pkg, m, w, 0, m.n_layers, True, True)
+    b, _ = _stage(pkg, m, w, 0, m.n_layers, True, True, kv_page_tokens=page)
     prompts = [pkg.pack.synth_prompt(m, 6, seed=20 + i) for i in range(3)]
     toks = [pkg.forward(a, {"seq_id": i, "token_pos": 0, "token_ids": p, "temperature": 0})["token_id"]
             for i, p in enumerate(prompts)]
@@ -294,7 +298,7 @@ def test_device_step_matches_forward(pkg, ref, tiny, torch_cuda):
         pkg.forward(b, {"seq_id": i, "token_pos": 0, "token_ids": p, "temperature": 0})
     ids = (C.c_uint64 * 3)(*[b.seq_key(i) for i in range(3)])
     cur = list(toks)
-    for step in range(8):
+    for step in range(12):
         pos = (C.c_int32 * 3)(*[6 + step] * 3)
         din = torch.tensor(cur, dtype=torch.int32, device="cuda")
         dout = torch.zeros(3, dtype=torch.int32, device="cuda")
