@@ -237,16 +237,27 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
     }
   } else if (warp == 1) {
     // ================= MMA issuer
+    // A barrier test costs hundreds of cycles even when the phase is already
+    // complete, and the issuer's loop sets the pace at a few tokens: the next
+    // slice's stages are tested before this slice's MMAs are issued (the
+    // test's latency hides behind the issue) and waited for only if not ready.
+    bool ready = false;
     for (int k = 0; k < K; k++) {
       // chunk c accumulates into partial buffer c & 1 (TMEM columns (1 + b) acc_cols ..)
       const int c = k / GM_CHUNK, b = c & 1;
       const bool first = k % GM_CHUNK == 0, last = k % GM_CHUNK == GM_CHUNK - 1 || k == K - 1;
       if (first && c >= 2 && !__all_sync(0xffffffffu, GM_WAIT(&pempty[b], ((c >> 1) - 1) & 1, &abort_flag))) break;
       const int sa = k % a.sa, sb = k % a.sb;
-      if (!__all_sync(0xffffffffu, GM_WAIT(&afull[sa], (k / a.sa) & 1, &abort_flag) &&
-                                       GM_WAIT(&bfull[sb], (k / a.sb) & 1, &abort_flag)))
+      if (!ready && !__all_sync(0xffffffffu, GM_WAIT(&afull[sa], (k / a.sa) & 1, &abort_flag) &&
+                                                 GM_WAIT(&bfull[sb], (k / a.sb) & 1, &abort_flag)))
         break;
       tc_fence_after();
+      bool next = false;
+      if (k + 1 < K) {
+        const bool na = mbar_test_wait(&afull[(k + 1) % a.sa], ((k + 1) / a.sa) & 1);
+        const bool nb = mbar_test_wait(&bfull[(k + 1) % a.sb], ((k + 1) / a.sb) & 1);
+        next = na && nb;
+      }
       if (lane == 0) {
         const uint32_t d = tmem + (uint32_t)(1 + b) * a.acc_cols;
         const uint32_t ahi = tmem + a.a_col0 + (uint32_t)sa * GM_A_COLS, alo = ahi + GM_A_COLS / 2;
@@ -266,6 +277,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
         if (last) umma_commit(&pfull[b]);  // the chunk's partial is complete
       }
       __syncwarp();
+      ready = __all_sync(0xffffffffu, next);
     }
     // completion of every MMA issued above (also after giving up, so the
     // TMEM is only freed when nothing writes it any more)
