@@ -82,6 +82,8 @@ struct GemmArgs {
   int ldy, mode;
   int sa, sb, raw_stages, ksl;  // A stages (TMEM), B stages (smem), raw stages of ksl slices
   uint32_t acc_cols, a_col0, idesc;
+  uint32_t idesc2;  // (fold) N = 2 NT: w_hi times the x_hi | x_lo rows of a B stage in one MMA
+  int fold;         // partial columns [0, NT) hold hi.hi + lo.hi, [NT, 2 NT) hi.lo
   float* ws;            // split-K partials [tile][split][NT][128]
   int* cnt;             // split-K arrivals per (M tile, N tile), zero between launches
   int* err;
@@ -227,7 +229,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
     pdl_wait();  // xs is written by the previous kernel
     for (int k = 0; k < K; k++) {
       const int s = k % a.sb;
-      if (k >= a.sb && !__all_sync(0xffffffffu, GM_WAIT(&bempty[s], ((k / a.sb) - 1) & 1, &abort_flag))) break;
+      // (with as many A as B stages, one commit frees both: the A stage's barrier)
+      uint64_t* const empty = a.sa == a.sb ? &aempty[s] : &bempty[s];
+      if (k >= a.sb && !__all_sync(0xffffffffu, GM_WAIT(empty, ((k / a.sb) - 1) & 1, &abort_flag))) break;
       if (lane == 0) {
         mbar_expect_tx(&bfull[s], bbytes);
         bulk_g2s(smem + (size_t)s * bbytes, a.xs + ((size_t)nt * a.pairs + kb + k) * bbytes, bbytes, &bfull[s]);
@@ -268,12 +272,18 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
           // a K16 step: 8 TMEM columns of A, 32 bytes further along B's swizzled rows
           const uint64_t dj = (uint64_t)(2 * j);
           const uint32_t aj = (uint32_t)(8 * j);
-          umma_f16_ts(d, ahi + aj, bhi + dj, a.idesc, !(first && j == 0));
-          umma_f16_ts(d, ahi + aj, blo + dj, a.idesc, 1u);
-          umma_f16_ts(d, alo + aj, bhi + dj, a.idesc, 1u);
+          if (a.fold) {
+            // the lo rows of B follow its hi rows: one MMA over both
+            umma_f16_ts(d, ahi + aj, bhi + dj, a.idesc2, !(first && j == 0));
+            umma_f16_ts(d, alo + aj, bhi + dj, a.idesc, 1u);
+          } else {
+            umma_f16_ts(d, ahi + aj, bhi + dj, a.idesc, !(first && j == 0));
+            umma_f16_ts(d, ahi + aj, blo + dj, a.idesc, 1u);
+            umma_f16_ts(d, alo + aj, bhi + dj, a.idesc, 1u);
+          }
         }
         umma_commit(&aempty[sa]);  // the stages are free once these MMAs have read them
-        umma_commit(&bempty[sb]);
+        if (a.sa != a.sb) umma_commit(&bempty[sb]);
         if (last) umma_commit(&pfull[b]);  // the chunk's partial is complete
       }
       __syncwarp();
@@ -313,6 +323,13 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       for (int c0 = 0; c0 < a.NT; c0 += 16) {
         uint32_t v[16], u[16];
         tmem_ld16(pb + (uint32_t)c0, v);
+        if (a.fold) {
+          uint32_t w2[16];  // the hi.lo products
+          tmem_ld16(pb + (uint32_t)(a.NT + c0), w2);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 16; j++) v[j] = __float_as_uint(__uint_as_float(v[j]) + __uint_as_float(w2[j]));
+        }
         if (c > 0) tmem_ld16(sbuf + (uint32_t)c0, u);
         tmem_ld_wait();
         if (c > 0) {
@@ -670,8 +687,11 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   a.ldy = ldy;
   a.mode = mode;
   // TMEM: running sum at column 0, partial buffers at acc_cols and 2 acc_cols,
-  // then the A stages (64 columns each) in the rest of the 512 columns
-  a.acc_cols = (uint32_t)((NT + 31) / 32 * 32);
+  // then the A stages (64 columns each) in the rest of the 512 columns.  Up
+  // to 32 tokens the w_hi MMA covers x_hi and x_lo at once (two MMAs per K16
+  // step instead of three; the partials take 2 NT columns)
+  a.fold = NT <= 32;
+  a.acc_cols = (uint32_t)(((a.fold ? 2 * NT : NT) + 31) / 32 * 32);
   a.a_col0 = 3 * a.acc_cols;
   a.sa = std::min(GM_MAX_SA, (int)((512 - a.a_col0) / GM_A_COLS));
   TN_REQUIRE(a.sa >= 2, TN_EUNSUPPORTED, "gemm: no room for two A stages in tensor memory");
@@ -689,6 +709,7 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   // kind::f16 instruction descriptor: f32 accumulator (bit 4), A and B fp16
   // (formats 0), both K-major, N >> 3 at bit 17, M >> 4 at bit 24
   a.idesc = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+  a.idesc2 = (1u << 4) | ((uint32_t)((2 * NT) >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
   a.err = err;
   // split K when the (M tile, N tile) grid fills at most half the SMs: at most
   // one wave, at least two accumulation chunks per split, and at most
