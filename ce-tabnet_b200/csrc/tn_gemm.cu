@@ -81,6 +81,7 @@ struct GemmArgs {
   float* y;
   int ldy, mode;
   int sa, sb, raw_stages, ksl;  // A stages (TMEM), B stages (smem), raw stages of ksl slices
+  int sps;                      // K slices per A / B stage (a step): 2 where TMEM has room, else 1
   uint32_t acc_cols, a_col0, idesc;
   uint32_t idesc2;  // (fold) N = 2 NT: w_hi times the x_hi | x_lo rows of a B stage in one MMA
   int fold;         // partial columns [0, NT) hold hi.hi + lo.hi, [NT, 2 NT) hi.lo
@@ -143,7 +144,8 @@ __device__ __forceinline__ void dq4(uint32_t u, uint32_t d2, uint32_t off2, uint
 
 __device__ __forceinline__ void drain_bar() { asm volatile("bar.sync 1, %0;" ::"n"(GM_DR_WARPS * 32) : "memory"); }
 
-template <int KIND>
+// SPS: K slices per A / B stage (GemmArgs::sps)
+template <int KIND, int SPS>
 __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const __grid_constant__ CUtensorMap wmap) {
   constexpr int REC = tile_rec_bytes(KIND), AB = tile_a_bytes(KIND);
   extern __shared__ uint8_t gsm_dyn[];
@@ -167,8 +169,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
   const int K = ke - kb;  // slices of this split
   const uint32_t sbase = (smem_u32(gsm_dyn) + 1023u) & ~1023u;
   uint8_t* const smem = gsm_dyn + (sbase - smem_u32(gsm_dyn));
-  const uint32_t bbytes = 2u * (uint32_t)a.NT * 128u;
-  uint8_t* const raw = smem + (size_t)a.sb * bbytes;
+  const uint32_t bbytes = 2u * (uint32_t)a.NT * 128u;  // one slice's x_hi | x_lo tile
+  const uint32_t bstage = bbytes * (uint32_t)SPS;
+  uint8_t* const raw = smem + (size_t)a.sb * bstage;
+  const int NG = (K + SPS - 1) / SPS;  // steps of SPS slices
+  const uint32_t acols = (uint32_t)(GM_A_COLS * SPS);  // TMEM columns of an A stage
   const uint32_t raw_stage = (uint32_t)(GM_RT * a.ksl * REC);  // [8 tiles][ksl slices][record]
 
   if (tid == 0) {
@@ -179,7 +184,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       last_raw[r] = -1;
     }
     for (int s = 0; s < a.sa; s++) {
-      mbar_init(&afull[s], GM_DQ_WARPS / 2);  // one dequant warp per lane quarter writes a slice
+      mbar_init(&afull[s], GM_DQ_WARPS / 2 * SPS);  // one dequant warp per lane quarter and slice
       mbar_init(&aempty[s], 1);
     }
     for (int s = 0; s < a.sb; s++) {
@@ -225,17 +230,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       __syncwarp();
     }
   } else if (warp == GM_WB) {
-    // ================= activations: the slice's x_hi | x_lo tile, one bulk copy
+    // ================= activations: a step's x_hi | x_lo tiles (contiguous in
+    // xs, slice after slice), one bulk copy
     pdl_wait();  // xs is written by the previous kernel
-    for (int k = 0; k < K; k++) {
-      const int s = k % a.sb;
+    for (int g = 0; g < NG; g++) {
+      const int s = g % a.sb, nk = min(SPS, K - g * SPS);
       // (with as many A as B stages, one commit frees both: the A stage's barrier)
       uint64_t* const empty = a.sa == a.sb ? &aempty[s] : &bempty[s];
-      if (k >= a.sb && !__all_sync(0xffffffffu, GM_WAIT(empty, ((k / a.sb) - 1) & 1, &abort_flag))) break;
+      if (g >= a.sb && !__all_sync(0xffffffffu, GM_WAIT(empty, ((g / a.sb) - 1) & 1, &abort_flag))) break;
       if (lane == 0) {
-        mbar_expect_tx(&bfull[s], bbytes);
-        bulk_g2s(smem + (size_t)s * bbytes, a.xs + ((size_t)nt * a.pairs + kb + k) * bbytes, bbytes, &bfull[s]);
-        last_b[s] = k;
+        mbar_expect_tx(&bfull[s], bbytes * nk);
+        bulk_g2s(smem + (size_t)s * bstage, a.xs + ((size_t)nt * a.pairs + kb + g * SPS) * bbytes, bbytes * nk,
+                 &bfull[s]);
+        last_b[s] = g;
       }
       __syncwarp();
     }
@@ -246,40 +253,48 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
     // slice's stages are tested before this slice's MMAs are issued (the
     // test's latency hides behind the issue) and waited for only if not ready.
     bool ready = false;
-    for (int k = 0; k < K; k++) {
-      // chunk c accumulates into partial buffer c & 1 (TMEM columns (1 + b) acc_cols ..)
-      const int c = k / GM_CHUNK, b = c & 1;
-      const bool first = k % GM_CHUNK == 0, last = k % GM_CHUNK == GM_CHUNK - 1 || k == K - 1;
+    for (int g = 0; g < NG; g++) {
+      // chunk c (GM_CHUNK slices, whole steps) accumulates into partial buffer
+      // c & 1 (TMEM columns (1 + b) acc_cols ..)
+      const int k0 = g * SPS, nk = min(SPS, K - k0);
+      const int c = k0 / GM_CHUNK, b = c & 1;
+      const bool first = k0 % GM_CHUNK == 0, last = (k0 + nk) % GM_CHUNK == 0 || k0 + nk == K;
       if (first && c >= 2 && !__all_sync(0xffffffffu, GM_WAIT(&pempty[b], ((c >> 1) - 1) & 1, &abort_flag))) break;
-      const int sa = k % a.sa, sb = k % a.sb;
-      if (!ready && !__all_sync(0xffffffffu, GM_WAIT(&afull[sa], (k / a.sa) & 1, &abort_flag) &&
-                                                 GM_WAIT(&bfull[sb], (k / a.sb) & 1, &abort_flag)))
+      const int sa = g % a.sa, sb = g % a.sb;
+      if (!ready && !__all_sync(0xffffffffu, GM_WAIT(&afull[sa], (g / a.sa) & 1, &abort_flag) &&
+                                                 GM_WAIT(&bfull[sb], (g / a.sb) & 1, &abort_flag)))
         break;
       tc_fence_after();
       bool next = false;
-      if (k + 1 < K) {
-        const bool na = mbar_test_wait(&afull[(k + 1) % a.sa], ((k + 1) / a.sa) & 1);
-        const bool nb = mbar_test_wait(&bfull[(k + 1) % a.sb], ((k + 1) / a.sb) & 1);
+      if (g + 1 < NG) {
+        const bool na = mbar_test_wait(&afull[(g + 1) % a.sa], ((g + 1) / a.sa) & 1);
+        const bool nb = mbar_test_wait(&bfull[(g + 1) % a.sb], ((g + 1) / a.sb) & 1);
         next = na && nb;
       }
       if (lane == 0) {
         const uint32_t d = tmem + (uint32_t)(1 + b) * a.acc_cols;
-        const uint32_t ahi = tmem + a.a_col0 + (uint32_t)sa * GM_A_COLS, alo = ahi + GM_A_COLS / 2;
-        const uint32_t st = sbase + (uint32_t)sb * bbytes;
-        const uint64_t bhi = sw128_desc(st), blo = sw128_desc(st + bbytes / 2);
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          // a K16 step: 8 TMEM columns of A, 32 bytes further along B's swizzled rows
-          const uint64_t dj = (uint64_t)(2 * j);
-          const uint32_t aj = (uint32_t)(8 * j);
-          if (a.fold) {
-            // the lo rows of B follow its hi rows: one MMA over both
-            umma_f16_ts(d, ahi + aj, bhi + dj, a.idesc2, !(first && j == 0));
-            umma_f16_ts(d, alo + aj, bhi + dj, a.idesc, 1u);
-          } else {
-            umma_f16_ts(d, ahi + aj, bhi + dj, a.idesc, !(first && j == 0));
-            umma_f16_ts(d, ahi + aj, blo + dj, a.idesc, 1u);
-            umma_f16_ts(d, alo + aj, bhi + dj, a.idesc, 1u);
+        for (int kk = 0; kk < SPS; kk++) {
+          if (kk >= nk) break;
+          const uint32_t ahi = tmem + a.a_col0 + (uint32_t)sa * acols + (uint32_t)kk * GM_A_COLS;
+          const uint32_t alo = ahi + GM_A_COLS / 2;
+          const uint32_t st = sbase + (uint32_t)sb * bstage + (uint32_t)kk * bbytes;
+          const uint64_t bhi = sw128_desc(st), blo = sw128_desc(st + bbytes / 2);
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            // a K16 step: 8 TMEM columns of A, 32 bytes further along B's swizzled rows
+            const uint64_t dj = (uint64_t)(2 * j);
+            const uint32_t aj = (uint32_t)(8 * j);
+            const uint32_t acc = !(first && kk == 0 && j == 0);
+            if (a.fold) {
+              // the lo rows of B follow its hi rows: one MMA over both
+              umma_f16_ts(d, ahi + aj, bhi + dj, a.idesc2, acc);
+              umma_f16_ts(d, alo + aj, bhi + dj, a.idesc, 1u);
+            } else {
+              umma_f16_ts(d, ahi + aj, bhi + dj, a.idesc, acc);
+              umma_f16_ts(d, ahi + aj, blo + dj, a.idesc, 1u);
+              umma_f16_ts(d, alo + aj, bhi + dj, a.idesc, 1u);
+            }
           }
         }
         umma_commit(&aempty[sa]);  // the stages are free once these MMAs have read them
@@ -430,9 +445,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
         const uint2 sc2 = reinterpret_cast<const uint2*>(rec + AB)[g];  // scales of blocks 2p, 2p + 1
         __syncwarp();
         if (lane == 0 && i0 + 2 >= nk) mbar_arrive(&rempty[r]);  // this warp's reads of the stage are done
-        const int sa = k % a.sa;
-        if (k >= a.sa) {
-          if (!__all_sync(0xffffffffu, GM_WAIT(&aempty[sa], ((k / a.sa) - 1) & 1, &abort_flag))) {
+        const int gs = k / SPS, sa = gs % a.sa;  // this slice's step and A stage
+        if (gs >= a.sa) {
+          if (!__all_sync(0xffffffffu, GM_WAIT(&aempty[sa], ((gs / a.sa) - 1) & 1, &abort_flag))) {
             live = false;
             break;
           }
@@ -464,12 +479,22 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
               lo[col] = pl[0];
               lo[col + 1] = pl[1];
             }
-          const uint32_t abase = tmem + lanes + a.a_col0 + (uint32_t)sa * GM_A_COLS + (uint32_t)(16 * kh);
+          const uint32_t abase =
+              tmem + lanes + a.a_col0 + (uint32_t)sa * acols + (uint32_t)(k % SPS) * GM_A_COLS + (uint32_t)(16 * kh);
           tmem_st16(abase, hi);
           tmem_st16(abase + GM_A_COLS / 2, lo);
         }
         tmem_st_wait();
         tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&afull[sa]);
+      }
+    }
+    // two slices a step and an odd K: the last step has no slice of parity 1,
+    // but its A stage waits for every dequant warp
+    if (live && SPS == 2 && (K & 1) && par == 1) {
+      const int gs = K / 2, sa = gs % a.sa;
+      if (gs < a.sa || __all_sync(0xffffffffu, GM_WAIT(&aempty[sa], ((gs / a.sa) - 1) & 1, &abort_flag))) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&afull[sa]);
       }
@@ -567,13 +592,15 @@ static int gemm_max_dyn() {
     cudaGetDevice(&dev);
     cudaFuncAttributes fa{};
     if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        cudaFuncGetAttributes(&fa, k_gemm<MK_Q8>) != cudaSuccess) {
+        cudaFuncGetAttributes(&fa, k_gemm<MK_Q8, 1>) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
     v = optin - (int)fa.sharedSizeBytes;
-    if (cudaFuncSetAttribute(k_gemm<MK_Q4>, cudaFuncAttributeMaxDynamicSharedMemorySize, v) != cudaSuccess ||
-        cudaFuncSetAttribute(k_gemm<MK_Q8>, cudaFuncAttributeMaxDynamicSharedMemorySize, v) != cudaSuccess) {
+    if (cudaFuncSetAttribute(k_gemm<MK_Q4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, v) != cudaSuccess ||
+        cudaFuncSetAttribute(k_gemm<MK_Q8, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, v) != cudaSuccess ||
+        cudaFuncSetAttribute(k_gemm<MK_Q4, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, v) != cudaSuccess ||
+        cudaFuncSetAttribute(k_gemm<MK_Q8, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, v) != cudaSuccess) {
       cudaGetLastError();
       v = 0;
     }
@@ -693,11 +720,14 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   a.fold = NT <= 32;
   a.acc_cols = (uint32_t)(((a.fold ? 2 * NT : NT) + 31) / 32 * 32);
   a.a_col0 = 3 * a.acc_cols;
-  a.sa = std::min(GM_MAX_SA, (int)((512 - a.a_col0) / GM_A_COLS));
+  // two K slices a stage where two such stages fit (each step's barrier
+  // operations then serve twice the MMAs), else one
+  a.sps = (int)((512 - a.a_col0) / (2 * GM_A_COLS)) >= 2 ? 2 : 1;
+  a.sa = std::min(GM_MAX_SA, (int)((512 - a.a_col0) / (GM_A_COLS * a.sps)));
   TN_REQUIRE(a.sa >= 2, TN_EUNSUPPORTED, "gemm: no room for two A stages in tensor memory");
   // shared memory: a few B stages, then as many raw stages (~18 KB boxes) as fit
   // (a copy's loaded latency is several microseconds: the ring must be deep)
-  const int bb = 2 * NT * 128;
+  const int bb = 2 * NT * 128 * a.sps;  // a B stage
   const int mi = 2;  // boxes of 4 slices (one stage wait per 4 slices)
   a.ksl = 1 << mi;
   a.sb = NT <= 64 ? 4 : 3;
@@ -729,9 +759,11 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   const size_t smem = (size_t)a.sb * bb + raw_bytes + 1024;
   const int grid = mtiles * ks * nt;
   if (m.kind == MK_Q4)
-    TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q4>, dim3(grid), dim3(GM_THREADS), smem, s, a, m.wmap[mi]));
+    TN_CHECK_CUDA(launch_pdl(a.sps == 2 ? k_gemm<MK_Q4, 2> : k_gemm<MK_Q4, 1>, dim3(grid), dim3(GM_THREADS), smem, s,
+                             a, m.wmap[mi]));
   else
-    TN_CHECK_CUDA(launch_pdl(k_gemm<MK_Q8>, dim3(grid), dim3(GM_THREADS), smem, s, a, m.wmap[mi]));
+    TN_CHECK_CUDA(launch_pdl(a.sps == 2 ? k_gemm<MK_Q8, 2> : k_gemm<MK_Q8, 1>, dim3(grid), dim3(GM_THREADS), smem, s,
+                             a, m.wmap[mi]));
   return TN_OK;
 }
 
