@@ -184,7 +184,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       last_raw[r] = -1;
     }
     for (int s = 0; s < a.sa; s++) {
-      mbar_init(&afull[s], GM_DQ_WARPS / 2 * SPS);  // one dequant warp per lane quarter and slice
+      // one dequant warp per lane quarter and slice, and with as many B as A
+      // stages the B tile's copy too (one barrier for the MMA issuer to test)
+      mbar_init(&afull[s], GM_DQ_WARPS / 2 * SPS + (a.sa == a.sb ? 1 : 0));
       mbar_init(&aempty[s], 1);
     }
     for (int s = 0; s < a.sb; s++) {
@@ -239,9 +241,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       uint64_t* const empty = a.sa == a.sb ? &aempty[s] : &bempty[s];
       if (g >= a.sb && !__all_sync(0xffffffffu, GM_WAIT(empty, ((g / a.sb) - 1) & 1, &abort_flag))) break;
       if (lane == 0) {
-        mbar_expect_tx(&bfull[s], bbytes * nk);
-        bulk_g2s(smem + (size_t)s * bstage, a.xs + ((size_t)nt * a.pairs + kb + g * SPS) * bbytes, bbytes * nk,
-                 &bfull[s]);
+        uint64_t* const full = a.sa == a.sb ? &afull[s] : &bfull[s];
+        mbar_expect_tx(full, bbytes * nk);
+        bulk_g2s(smem + (size_t)s * bstage, a.xs + ((size_t)nt * a.pairs + kb + g * SPS) * bbytes, bbytes * nk, full);
         last_b[s] = g;
       }
       __syncwarp();
@@ -261,14 +263,15 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       const bool first = k0 % GM_CHUNK == 0, last = (k0 + nk) % GM_CHUNK == 0 || k0 + nk == K;
       if (first && c >= 2 && !__all_sync(0xffffffffu, GM_WAIT(&pempty[b], ((c >> 1) - 1) & 1, &abort_flag))) break;
       const int sa = g % a.sa, sb = g % a.sb;
+      const bool merged = a.sa == a.sb;  // afull also counts the B copy
       if (!ready && !__all_sync(0xffffffffu, GM_WAIT(&afull[sa], (g / a.sa) & 1, &abort_flag) &&
-                                                 GM_WAIT(&bfull[sb], (g / a.sb) & 1, &abort_flag)))
+                                                 (merged || GM_WAIT(&bfull[sb], (g / a.sb) & 1, &abort_flag))))
         break;
       tc_fence_after();
       bool next = false;
       if (g + 1 < NG) {
         const bool na = mbar_test_wait(&afull[(g + 1) % a.sa], ((g + 1) / a.sa) & 1);
-        const bool nb = mbar_test_wait(&bfull[(g + 1) % a.sb], ((g + 1) / a.sb) & 1);
+        const bool nb = merged || mbar_test_wait(&bfull[(g + 1) % a.sb], ((g + 1) / a.sb) & 1);
         next = na && nb;
       }
       if (lane == 0) {
@@ -514,7 +517,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1) k_gemm(const GemmArgs a, const 
       const int k = last_b[s];
       if (k < 0) continue;
       abort_flag = 0;
-      if (!GM_WAIT(&bfull[s], (k / a.sb) & 1, &abort_flag)) break;
+      if (!GM_WAIT(a.sa == a.sb ? &afull[s] : &bfull[s], (k / a.sb) & 1, &abort_flag)) break;
     }
     atomicExch(a.err, 1);
   }
@@ -730,7 +733,7 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   const int bb = 2 * NT * 128 * a.sps;  // a B stage
   const int mi = 2;  // boxes of 4 slices (one stage wait per 4 slices)
   a.ksl = 1 << mi;
-  a.sb = NT <= 64 ? 4 : 3;
+  a.sb = a.sps == 2 ? a.sa : 3;  // (two-slice steps: one barrier per step for A and B)
   const int raw_stage_b = GM_RT * a.ksl * REC;
   a.raw_stages = std::min(GM_MAX_RAW, (max_dyn - 1024 - a.sb * bb) / raw_stage_b);
   const int raw_bytes = a.raw_stages * raw_stage_b;
