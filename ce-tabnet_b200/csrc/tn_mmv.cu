@@ -220,7 +220,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
       auto take = [&]() -> int {
         const int st = k % a.stages;
         if (k >= a.stages) {
-          if (!mbar_wait(&empty[st], ((k / a.stages) - 1) & 1, &abort_flag)) return -1;
+          if (!mbar_wait_fast(&empty[st], ((k / a.stages) - 1) & 1, &abort_flag)) return -1;
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         }
         return abort_flag ? -1 : st;
@@ -489,7 +489,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     for (int cg = 0; cg < NG; cg++) acc[cg][0] = acc[cg][1] = acc[cg][2] = acc[cg][3] = 0.f;
     // ring stage st of the current unit and the parity of its fill
     for (int st = 0, ph = 0;; (++st == a.stages) ? (st = 0, ph ^= 1) : 0) {
-      if (!__all_sync(FULL, mbar_wait(&full[st], ph, &abort_flag))) break;
+      if (!__all_sync(FULL, mbar_wait_fast(&full[st], ph, &abort_flag))) break;
       const int4 d = udesc[st];
       if (d.x < 0) break;
       const int t = d.x, sc = d.y & (kPieceEnd - 1), first = d.z, n = d.w;
@@ -740,7 +740,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     };
     for (int pi = 0;; pi++) {
       const int b = pi % MMV_NB;
-      const bool ok = __all_sync(FULL, mbar_wait(&red_full[b], (pi / MMV_NB) & 1, &abort_flag));
+      const bool ok = __all_sync(FULL, mbar_wait_fast(&red_full[b], (pi / MMV_NB) & 1, &abort_flag));
       const int t = rmeta[b][0], sc0 = rmeta[b][1], cnt_u = rmeta[b][2];
       if (!ok || abort_flag) {
         bad = true;
