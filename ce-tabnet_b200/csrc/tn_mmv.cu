@@ -608,7 +608,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
         vh[cg] = (vh[cg] * sa) * sb;
       }
       const int b = pi % MMV_NB;
-      if (pi >= MMV_NB) mbar_wait(&red_empty[b], ((pi / MMV_NB) - 1) & 1, &abort_flag);
+      if (pi >= MMV_NB) mbar_wait_fast(&red_empty[b], ((pi / MMV_NB) - 1) & 1, &abort_flag);
       if ((c & (TT == 1 ? 3 : 1)) == 0) {
 #pragma unroll
         for (int cg = 0; cg < NG; cg++) {
@@ -632,7 +632,7 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
     // no more pieces
     {
       const int b = pi % MMV_NB;
-      if (pi >= MMV_NB) mbar_wait(&red_empty[b], ((pi / MMV_NB) - 1) & 1, &abort_flag);
+      if (pi >= MMV_NB) mbar_wait_fast(&red_empty[b], ((pi / MMV_NB) - 1) & 1, &abort_flag);
       if (warp == 0 && lane == 0) rmeta[b][0] = -1;
       __syncwarp();
       if (lane == 0) mbar_arrive(&red_full[b]);
