@@ -538,6 +538,13 @@ static int recover_kernel_error(tn_stage* st, cudaStream_t s) {
 }
 
 // the layer stack for T rows already described by the control block
+// kernels one matvec / matvec_dec call over T tokens launches (the GEMM: its
+// activation prep and the GEMM; the decode matvec: one per 4 tokens)
+static int mv_launches(const tn_stage* st, const Matrix& m, int T) {
+  if (m.kind != MK_Q4 && m.kind != MK_Q8) return 1;
+  return gemm_ok(m, T) && st->gemm_ws ? 2 : (T + 3) / 4;
+}
+
 static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t s) {
   const RowInfo* rows = (const RowInfo*)st->d_ctl;
   const int* outrows = (const int*)(st->d_ctl + st->ctl_outrows_off);
@@ -546,6 +553,7 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
   int rc;
   st->ev_used = 0;
   st->step_launches = 0;
+  auto mvl = [&](const Matrix& m, int rows) { return mv_launches(st, m, rows); };
   if (input_kind == IN_IDS)
     TN_STEP_LAUNCH(TN_PROF_OTHER, 1, embed_rows(st->embed, st->ids, T, st->h, H, st->err, s));
   else
@@ -574,10 +582,10 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
       f.q_dim = st->qDim;
       f.kv_dim = st->kvDim;
       f.hd = st->hd;
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec_dec(L.qkv, T, st->h, H, st->qkv, ldqkv, EPI_QKV_ROPE, f, st->kerr, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, mvl(L.qkv, T), matvec_dec(L.qkv, T, st->h, H, st->qkv, ldqkv, EPI_QKV_ROPE, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.attn_norm, st->xn, H, H, T, s));
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, 1, matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_QKV, mvl(L.qkv, T), matvec(L.qkv, T, st->xn, H, st->qkv, ldqkv, EPI_STORE, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
       TN_STEP_LAUNCH(TN_PROF_ROPE_KV, 1,
                      rope_kv(st->qkv, ldqkv, rows, st->cs, st->q, kc, vc, st->kv_type, st->kvmap, st->nH,
                              st->nKV, st->hd, T, s));
@@ -586,32 +594,32 @@ static int run_step(tn_stage* st, int T, int n_out, int input_kind, cudaStream_t
                    attention(st->q, st->qDim, kc, vc, st->kv_type, st->kvmap, rows, T, st->nH, st->nKV, st->hd, ap,
                              st->att, st->qDim, st->attn_ws, st->attn_cnt, s));
     if (fuse && matvec_dec_ok(L.o, T))
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, mvl(L.o, T), matvec_dec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, 1, matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_O, mvl(L.o, T), matvec(L.o, T, st->att, st->qDim, st->h, H, EPI_RESID, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
     if (fuse && matvec_dec_ok(L.gu, T)) {
       MvFuse f;
       f.norm_w = L.ffn_norm;
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec_dec(L.gu, T, st->h, H, st->act, st->F, EPI_SWIGLU, f, st->kerr, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, mvl(L.gu, T), matvec_dec(L.gu, T, st->h, H, st->act, st->F, EPI_SWIGLU, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, nullptr, L.ffn_norm, st->xn, H, H, T, s));
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, 1, matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_GATE_UP, mvl(L.gu, T), matvec(L.gu, T, st->xn, H, st->act, st->F, EPI_SWIGLU, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
     }
     if (fuse && matvec_dec_ok(L.down, T))
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec_dec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, mvl(L.down, T), matvec_dec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, MvFuse(), st->kerr, s));
     else
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, 1, matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_DOWN, mvl(L.down, T), matvec(L.down, T, st->act, st->F, st->h, H, EPI_RESID, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
   }
   if (st->last) {
     if (!(st->flags & TN_FLAG_NO_FUSED_DECODE) && matvec_dec_ok(st->lm_head, n_out)) {
       MvFuse f;
       f.norm_w = st->final_norm;
       f.rowsel = outrows;
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1,
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, mvl(st->lm_head, n_out),
                      matvec_dec(st->lm_head, n_out, st->h, H, st->logits, st->V, EPI_STORE, f, st->kerr, s));
     } else {
       TN_STEP_LAUNCH(TN_PROF_NORM, 1, rmsnorm(st->h, H, outrows, st->final_norm, st->xn, H, H, n_out, s));
-      TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, 1,
+      TN_STEP_LAUNCH(TN_PROF_MATVEC_LM_HEAD, mvl(st->lm_head, n_out),
                      matvec(st->lm_head, n_out, st->xn, H, st->logits, st->V, EPI_STORE, st->kerr, st->gemm_ws, st->gemm_ws_bytes, s));
     }
     TN_STEP_LAUNCH(TN_PROF_OTHER, 1, sample_rows(st->logits, n_out, st->V, params, st->tok_out, s));
