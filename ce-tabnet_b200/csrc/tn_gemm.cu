@@ -733,7 +733,9 @@ int gemm(const Matrix& m, int T, const float* x, int ldx, const int* rowsel, flo
   const int bb = 2 * NT * 128 * a.sps;  // a B stage
   const int mi = 2;  // boxes of 4 slices (one stage wait per 4 slices)
   a.ksl = 1 << mi;
-  a.sb = a.sa;  // as many B as A stages: one barrier per step for both (3 B stages at 128 tokens measured 1-6 % slower)
+  // as many B as A stages: one barrier per step for both (three B stages
+  // next to two A stages at 128 tokens measured 1-6 % slower)
+  a.sb = a.sa;
   const int raw_stage_b = GM_RT * a.ksl * REC;
   a.raw_stages = std::min(GM_MAX_RAW, (max_dyn - 1024 - a.sb * bb) / raw_stage_b);
   const int raw_bytes = a.raw_stages * raw_stage_b;
