@@ -70,6 +70,8 @@ def parse_args(argv=None):
                    help="attention sweep: paged cache with pages of this many positions (0: contiguous)")
     p.add_argument("--kv-cache", choices=["f32", "f16", "f8"], default="f32",
                    help="decode: KV cache element type (f32 = the reference's rows; f16 / f8 opt in)")
+    p.add_argument("--kv-page-tokens", type=int, default=0,
+                   help="decode: paged KV cache with pages of this many positions (0: contiguous per sequence)")
     p.add_argument("--reps", type=int, default=20, help="kernel sweeps: timed launches per point")
     return p.parse_args(argv)
 
@@ -84,6 +86,7 @@ def workload_config(args, world: int) -> dict:
                         f"{args.prompt}-token prompts, one micro-batch per stage step",
             "model": args.model, "microbatches": args.microbatches, "seqs_per_microbatch": 1,
             "prompt_len": args.prompt, "stages": world, "parallelism": f"pp{world}", "kv_cache": args.kv_cache,
+            "kv_page_tokens": args.kv_page_tokens,
             "l2": "weights (39 GB at N=1) exceed the 126 MB L2 every step; no flush needed",
             "sampling": "greedy (temperature 0)",
             "weights": "seeded synthetic: Irwin-Hall(4) approximation of N(0, 0.02) per element, quantised "
@@ -487,7 +490,8 @@ def run_ours(args):
     ctx = pkg.initStage({"arch": "llama", "dims": m.dims(), "layers": [lo, hi], "is_first": st["is_first"],
                          "is_last": st["is_last"], "weights": w,
                          "opts": {"device": local, "max_ctx": args.prompt + n_decode + 4, "max_seqs": M,
-                                  "max_tokens_per_step": 512, "kv_dtype": args.kv_cache}})
+                                  "max_tokens_per_step": 512, "kv_dtype": args.kv_cache,
+                                  "kv_page_tokens": args.kv_page_tokens}})
     del w
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
