@@ -821,8 +821,12 @@ static int mmv_occ(int smem) {
   return o;
 }
 
-// q4_0 matrices at least four times as tall as wide (gate/up, lm_head)
-static bool mmv_wide(const Matrix& m) { return m.kind == MK_Q4 && (int64_t)m.rows >= 4 * (int64_t)m.cols; }
+// q4_0 matrices at least four times as tall as wide, over at least 8192
+// columns (the 70B gate/up and lm_head: faster; the 8B ones, 4096 columns,
+// measured slower, 457 vs 506 tok/s in the 8B decode)
+static bool mmv_wide(const Matrix& m) {
+  return m.kind == MK_Q4 && m.cols >= 8192 && (int64_t)m.rows >= 4 * (int64_t)m.cols;
+}
 
 // Two CTAs per SM when they fit (more warps to overlap the MMA work), with
 // the deepest ring that keeps that occupancy; a stage is free again as soon
