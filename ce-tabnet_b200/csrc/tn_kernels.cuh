@@ -83,7 +83,6 @@ inline cudaError_t launch_pdl_cluster(void (*kern)(KArgs...), dim3 grid, dim3 bl
 // shared-memory stage each).
 struct MmShape {
   int ks = 0, ckp = 0, nsc = 0, scp = 0;
-  int sc = 0;  // most block pairs per sub-chunk the shape was planned with
   int stages = 0, smem = 0, ctas = 1;  // ring depth, dynamic shared memory, resident CTAs per SM
   uint32_t stage_bytes = 0;
 };

@@ -153,12 +153,10 @@ __host__ __device__ __forceinline__ int mmv_pool0(int nsu, int gk, int nsc) {
 __host__ __device__ constexpr int mmv_red_bytes(int tt) { return (MMV_NB * MMV_NW * 16 * tt * 4 + 127) / 128 * 128; }
 constexpr int kPieceEnd = 1 << 16;  // unit descriptor flag (with the sub-chunk): the last unit of a piece
 
-// SC: most block pairs per sub-chunk (one ring stage); mmv_sc, or twice that
-// for tall q4_0 matrices at one token (mmv_wide)
-template <int KIND, int TT, int SC = mmv_sc(KIND, TT)>
+template <int KIND, int TT>
 __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
   constexpr int AB = tile_a_bytes(KIND), REC = tile_rec_bytes(KIND);
-  constexpr int PPW = SC / MMV_NW, NV = 16 * TT, NC = MMV_NW * 32;
+  constexpr int SC = mmv_sc(KIND, TT), PPW = SC / MMV_NW, NV = 16 * TT, NC = MMV_NW * 32;
   // B column groups of 8 columns (tokens 2 cg, 2 cg + 1 x 4 digits; one token:
   // 2 block parities x 4 digits), and 32-value groups of a tile's row sums
   // (the epilogue lanes; also the workspace stride of a part)
@@ -798,49 +796,42 @@ __global__ void __launch_bounds__(MMV_THREADS, 2) k_mmv(const MmvArgs a) {
 
 // ---------------------------------------------------------------- host side
 // dynamic shared memory a CTA may take next to the kernel's static arrays
-template <int KIND, int TT, int SC>
+template <int KIND, int TT>
 static int mmv_max_dyn() {
   int dev = 0, optin = 0;
   cudaGetDevice(&dev);
   cudaFuncAttributes fa{};
   if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-      cudaFuncGetAttributes(&fa, k_mmv<KIND, TT, SC>) != cudaSuccess) {
+      cudaFuncGetAttributes(&fa, k_mmv<KIND, TT>) != cudaSuccess) {
     cudaGetLastError();
     return 0;
   }
   return std::min(MMV_MAX_SMEM, optin - (int)fa.sharedSizeBytes);
 }
 
-template <int KIND, int TT, int SC>
+template <int KIND, int TT>
 static int mmv_occ(int smem) {
   int o = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_mmv<KIND, TT, SC>, MMV_THREADS, smem) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k_mmv<KIND, TT>, MMV_THREADS, smem) != cudaSuccess) {
     cudaGetLastError();
     o = 0;
   }
   return o;
 }
 
-// q4_0 matrices at least four times as tall as wide, over at least 8192
-// columns (the 70B gate/up and lm_head: faster; the 8B ones, 4096 columns,
-// measured slower, 457 vs 506 tok/s in the 8B decode)
-static bool mmv_wide(const Matrix& m) {
-  return m.kind == MK_Q4 && m.cols >= 8192 && (int64_t)m.rows >= 4 * (int64_t)m.cols;
-}
-
 // Two CTAs per SM when they fit (more warps to overlap the MMA work), with
 // the deepest ring that keeps that occupancy; a stage is free again as soon
 // as its operands are in registers, so every stage is in flight.
-template <int KIND, int TT, int SC = mmv_sc(KIND, TT)>
+template <int KIND, int TT>
 static void mmv_pick(MmShape* sh) {
-  const int stage = (int)sh->stage_bytes, max_dyn = mmv_max_dyn<KIND, TT, SC>();
-  if (cudaFuncSetAttribute(k_mmv<KIND, TT, SC>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn) != cudaSuccess)
+  const int stage = (int)sh->stage_bytes, max_dyn = mmv_max_dyn<KIND, TT>();
+  if (cudaFuncSetAttribute(k_mmv<KIND, TT>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_dyn) != cudaSuccess)
     cudaGetLastError();
   const int rb = mmv_red_bytes(TT);
   int best_s = 2, best_o = 0;
   for (int s = std::min(MMV_MAX_STAGES, (max_dyn - rb) / stage); s >= 2; s--) {
     // (s goes down: the first depth that reaches an occupancy is the deepest one)
-    const int o = std::min(mmv_occ<KIND, TT, SC>(rb + s * stage), 2);
+    const int o = std::min(mmv_occ<KIND, TT>(rb + s * stage), 2);
     if (o > best_o) {
       best_o = o;
       best_s = s;
@@ -860,12 +851,7 @@ int mm_prepare(Matrix* m) {
   for (int i = 0; i < 3; i++) {
     const int tt = 1 << i;
     MmShape& sh = m->mm[i];
-    // tall q4_0 matrices at one token take two-sub-chunk units: half the
-    // ring hand-offs per weight byte (57344x8192: 49.4 -> 46.2 us; the
-    // lm_head too), where long or square ones measured slower
-    const bool wide = tt == 1 && mmv_wide(*m);
-    const int cp = MMV_CE / tt / 64, scmax = wide ? 2 * mmv_sc(m->kind, tt) : mmv_sc(m->kind, tt);
-    sh.sc = scmax;
+    const int cp = MMV_CE / tt / 64, scmax = mmv_sc(m->kind, tt);
     sh.ks = (m->pairs + cp - 1) / cp;
     sh.ckp = (m->pairs + sh.ks - 1) / sh.ks;
     sh.nsc = (sh.ckp + scmax - 1) / scmax;
@@ -875,8 +861,7 @@ int mm_prepare(Matrix* m) {
     ks_max = std::max(ks_max, sh.ks);
     // (set once per matrix, outside any stream capture)
     if (m->kind == MK_Q4) {
-      if (tt == 1 && wide) mmv_pick<MK_Q4, 1, 2 * mmv_sc(MK_Q4, 1)>(&sh);
-      else if (tt == 1) mmv_pick<MK_Q4, 1>(&sh);
+      if (tt == 1) mmv_pick<MK_Q4, 1>(&sh);
       else if (tt == 2) mmv_pick<MK_Q4, 2>(&sh);
       else mmv_pick<MK_Q4, 4>(&sh);
     } else {
@@ -898,13 +883,6 @@ static int launch_mmv(const Matrix& m, int T, const float* x, int ldx, float* y,
   const int grid = std::max(sh.ks, std::min(m.tiles * sh.ks, sh.ctas * num_sms()));
   const MmvArgs a{m.data, m.rows, m.tiles, m.pairs, m.cols, T, x, ldx, y, ldy, mode, sh.ks, sh.ckp, sh.nsc,
                   sh.scp, sh.stages, sh.stage_bytes, err, m.cnt, m.ws, f};
-  if constexpr (KIND == MK_Q4 && TT == 1) {
-    if (sh.sc == 2 * mmv_sc(KIND, TT)) {
-      TN_CHECK_CUDA(launch_pdl(k_mmv<KIND, TT, 2 * mmv_sc(KIND, TT)>, dim3(grid), dim3(MMV_THREADS), (size_t)sh.smem,
-                               s, a));
-      return TN_OK;
-    }
-  }
   TN_CHECK_CUDA(launch_pdl(k_mmv<KIND, TT>, dim3(grid), dim3(MMV_THREADS), (size_t)sh.smem, s, a));
   return TN_OK;
 }
