@@ -713,7 +713,10 @@ struct SlotTxn {
     }
   }
   // pages for rows [0, rows) of the slot's sequence, their page-table
-  // entries copied to the device on s ahead of the step's kernels
+  // entries copied to the device on s ahead of the step's kernels.  (The
+  // copy reads the pinned host entries when it runs; an entry changes only
+  // when its slot is reused, after tn_stage_free_seq, which callers may not
+  // issue while that sequence's steps are in flight.)
   int grow(int slot, int rows, cudaStream_t s) {
     if (!st->page_tokens) return TN_OK;
     const int need = (rows + st->page_tokens - 1) >> st->page_shift, j0 = st->seq_pages[slot];

@@ -130,8 +130,11 @@ int tn_stage_forward(tn_stage* st, const tn_fwd_req* req, tn_fwd_out* out);
  * them as independent forward calls).  reqs[i] and outs[i] as above. */
 int tn_stage_forward_batch(tn_stage* st, const tn_fwd_req* reqs, int32_t n_reqs, tn_fwd_out* outs);
 
-/* Release one sequence's KV slot (no reference counterpart: the reference
- * keeps every sequence's KV until freeStage, web/inference-worker.js:677-684). */
+/* Release one sequence's KV slot and, with a paged cache, its pages (no
+ * reference counterpart: the reference keeps every sequence's KV until
+ * freeStage, web/inference-worker.js:677-684).  Steps of that sequence
+ * enqueued with tn_stage_step_async must have finished: the slot and its
+ * pages may be handed to the next sequence at once. */
 int tn_stage_free_seq(tn_stage* st, uint64_t seq_id);
 
 /* KV rows currently cached for seq_id (0 if unknown). */
